@@ -1,0 +1,438 @@
+"""Benchmark of the DS hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemm|fused_add_mul|reduce|recurrence]
+
+Default workload (the headline metric): DS dot_general C = A @ B with
+M = N = K = 4096, A and B float64 ~ U[-1, 1] drawn from default_rng(2) (A
+first), split to (hi, lo), multiplied in DS arithmetic and recombined to f64.
+One step = one ds_dot_general_f64 call on device-resident inputs.  Inputs
+(2 x 128 MiB) and output (128 MiB) exceed the 126 MB L2.  value = whole-job
+DS-GEMM GFLOP/s (2*M*N*K per GEMM); with N GPUs every rank multiplies its
+own 4096-row block of A by the replicated B (weak scaling, no collective in
+the step).  e2e repeats the step through the public API with pinned host
+buffers: A and B copied in and C copied out every step.
+
+--impl reference times the reference's CPU path for the same workload on the
+host cores (rank 0 only): the DS pass restated in NumPy (split, four float32
+matmuls with f32 accumulation, two_sum, recombine; oracle/ds_pass_ref.py).
+The reference itself needs JAX/XLA, which this image does not have.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ds-experiment_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "DS-GEMM GFLOP/s at 4096³ (1–8 B200); DS elementwise HBM GB/s; err vs f64"
+GEMM_DIM = 4096
+
+
+# ---------------------------------------------------------------------------
+# helpers
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(kernel_family, workload):
+    """Per-launch DRAM bytes of a kernel family from profiles/ncu_traffic.txt
+    (lines: family workload bytes_per_launch), or None."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel_family \
+                and parts[1] == workload:
+            return float(parts[2])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        if not sm:
+            return None
+        mx = max(float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+
+def gemm_inputs(rank):
+    """Rank 0: exactly the 4096^3 config (default_rng(2), A then B).  Rank r > 0
+    multiplies its own A block (default_rng((2, r))) by the same B."""
+    rng = np.random.default_rng(2)
+    A = rng.uniform(-1, 1, (GEMM_DIM, GEMM_DIM))
+    B = rng.uniform(-1, 1, (GEMM_DIM, GEMM_DIM))
+    if rank > 0:
+        A = np.random.default_rng((2, rank)).uniform(-1, 1, (GEMM_DIM, GEMM_DIM))
+    return A, B
+
+
+def gemm_error(C, A, B, samples=256):
+    from oracle import exact
+    rows, cols = exact.sample_indices(A.shape[0], B.shape[1], samples, seed=77)
+    truth = exact.exact_gemm_entries(A, B, rows, cols)
+    err = np.abs(C[rows, cols] - truth)
+    return float(err.max()), float(np.median(err)), rows, cols, truth
+
+
+def reference_gemm_error(A, B, rows, cols, truth):
+    """Error of the reference DS path (4 x f32 dots, DsTransformPass.cpp:359-365)
+    on the sampled entries."""
+    from oracle import ds_pass_ref
+    ah, al = ds_pass_ref.from_float(A[rows])
+    # only the sampled rows and columns are needed
+    uniq_c, inv_c = np.unique(cols, return_inverse=True)
+    bh, bl = ds_pass_ref.from_float(B[:, uniq_c])
+    p = np.einsum("ik,ki->i", ah, bh[:, inv_c])
+    e1 = np.einsum("ik,ki->i", ah, bl[:, inv_c])
+    e2 = np.einsum("ik,ki->i", al, bh[:, inv_c])
+    e3 = np.einsum("ik,ki->i", al, bl[:, inv_c])
+    h, l = ds_pass_ref.two_sum(p, (e1 + e2) + e3)
+    ref = ds_pass_ref.to_float(h, l)
+    return float(np.abs(ref - truth).max())
+
+
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+    from ds_b200 import _lib, ops
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream()
+    result = {}
+    if args.workload != "gemm":
+        raise SystemExit("only --workload gemm is the driver's contract; see --help")
+
+    A, B = gemm_inputs(rank)
+    dA = torch.from_numpy(A).to(dev)
+    dB = torch.from_numpy(B).to(dev)
+    algo = args.algorithm
+
+    def step():
+        return ops.ds_matmul_f64(dA, dB, algorithm=algo)
+
+    for _ in range(args.warmup):
+        C = step()
+    torch.cuda.synchronize()
+    C_host = C.cpu().numpy() if rank == 0 else None
+
+    clocks = ClockSampler(local)
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        C = step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    _lib.profile_enable(False)
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms)
+    flops_step = 2.0 * GEMM_DIM ** 3
+    value = world * flops_step / (ms * 1e-3) / 1e9
+
+    # dominant kernel and its roofline
+    fam = "ozaki_gemm"
+    k_ms, k_n = _lib.profile_read(fam)
+    launches = {}
+    for f in ("ozaki_split", "ozaki_gemm", "ozaki_crt", "dot_simt", "dot_vec", "elementwise",
+              "reduce", "recurrence"):
+        t, n = _lib.profile_read(f)
+        if n:
+            launches[f] = {"launches": n, "ms_total": round(t, 4)}
+    peaks, peak_src = measured_peaks()
+    if k_n:
+        from ds_b200 import gemm_info
+        info = gemm_info(GEMM_DIM, GEMM_DIM, GEMM_DIM)
+        per_launch_ms = k_ms / k_n
+        ops_per_launch = info["tensor_ops_per_launch"]
+        achieved = ops_per_launch / (per_launch_ms * 1e-3) / 1e12
+        peak = 2.0 * peaks["bf16_tflops"]
+        roofline = {"bound": "tensor", "kernel": fam, "achieved": round(achieved, 1),
+                    "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                    "traffic": ncu_traffic(fam, "gemm4096"),
+                    "peak_source": f"2 x {peak_src} bf16_tflops (B200 dense int8 rate = "
+                                   "2x bf16); int8 ops counted as 2 per MAC",
+                    "kernel_ms_per_launch": round(per_launch_ms, 4)}
+    else:
+        fam = "dot_simt"
+        k_ms, k_n = _lib.profile_read(fam)
+        per_launch_ms = k_ms / max(k_n, 1)
+        roofline = {"bound": "tensor", "kernel": fam, "achieved": None, "peak": None,
+                    "unit": "TFLOP/s", "frac": None, "traffic": None,
+                    "note": "CUDA-core path (tensor-core kernel unavailable)",
+                    "kernel_ms_per_launch": round(per_launch_ms, 4)}
+    gpu_launches = sum(v["launches"] for v in launches.values())
+
+    # e2e through the public API with pinned host buffers
+    hA = torch.from_numpy(A).pin_memory()
+    hB = torch.from_numpy(B).pin_memory()
+    hC = torch.empty((GEMM_DIM, GEMM_DIM), dtype=torch.float64).pin_memory()
+
+    def e2e_step():
+        a = hA.to(dev, non_blocking=True)
+        b = hB.to(dev, non_blocking=True)
+        c = ops.ds_matmul_f64(a, b, algorithm=algo)
+        hC.copy_(c, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e = {"value": round(world * flops_step / (e_ms * 1e-3) / 1e9, 1), "unit": "GFLOP/s",
+           "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": int(A.nbytes + B.nbytes),
+           "d2h_bytes_per_step": int(A.nbytes)}
+
+    if rank == 0:
+        err_max, err_med, rows, cols, truth = gemm_error(C_host, A, B)
+        ref_err = reference_gemm_error(A, B, rows, cols, truth)
+        result["accuracy"] = {"max_abs_err_vs_exact": err_max, "median_abs_err": err_med,
+                              "reference_ds_path_max_abs_err": ref_err,
+                              "sampled_entries": int(len(rows)),
+                              "truth": "exact products summed with math.fsum"}
+        if world == 1:
+            result["cpu_baseline"] = cpu_baseline_gemm(A, B)
+            if not args.no_secondary:
+                result["secondary"] = secondary_metrics(dev)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (numpy default_rng(2) U[-1,1] f64, as the config)",
+        "config": {"workload": "ds_dot_general_f64 4096x4096x4096 (A, B f64 U[-1,1] seed 2; "
+                               "per-rank 4096-row A block, B replicated)",
+                   "M": GEMM_DIM * world, "N": GEMM_DIM, "K": GEMM_DIM,
+                   "algorithm": algo, "parallelism": f"rows{world}",
+                   "l2": "inputs 256 MiB + output 128 MiB per step exceed the 126 MB L2"},
+        "e2e": e2e, "roofline": roofline, "gpu_launches": gpu_launches,
+        "kernel_launches": launches, "clocks": clk,
+    }
+    line.update(result)
+    return line
+
+
+def cpu_baseline_gemm(A, B, reps=1):
+    """The reference DS path on the host (NumPy restatement, BLAS on all cores)."""
+    from oracle import ds_pass_ref
+    t = time.perf_counter()
+    for _ in range(reps):
+        ds_pass_ref.dot_general_f64(A, B)
+    dt = (time.perf_counter() - t) / reps
+    return {"value": round(2.0 * A.shape[0] * A.shape[1] * B.shape[1] / dt / 1e9, 2),
+            "unit": "GFLOP/s", "cores": host_cores(), "kind": "port",
+            "sample": f"one full {A.shape[0]}x{A.shape[1]}x{B.shape[1]} DS GEMM: split, four "
+                      "float32 numpy matmuls (f32 accumulation), two_sum, recombine"}
+
+
+def secondary_metrics(dev):
+    """Short HBM-bound checks: fused (a+b)*c and the DS sum at 2^26 elements."""
+    import torch
+    from ds_b200 import ops
+    from oracle import exact
+    out = {}
+    n = 1 << 26
+    rng = np.random.default_rng(0)
+    a = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
+    b = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
+    c = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
+    for _ in range(3):
+        ops.ds_fused_add_mul3_to_f64(a, b, c)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        y = ops.ds_fused_add_mul3_to_f64(a, b, c)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    out["fused_add_mul3_2p26"] = {"GB/s": round(32.0 * n / (ms * 1e-3) / 1e9, 1),
+                                  "ms": round(ms, 4), "bytes_per_elem": 32}
+    del a, b, c, y
+    s = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)
+    x = s * 1e8 + np.random.default_rng(1).uniform(0, 1, n) * 1e-3
+    dx = torch.from_numpy(x).to(dev)
+    for _ in range(3):
+        r = ops.ds_sum_f64(dx)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        r = ops.ds_sum_f64(dx)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    truth = exact.exact_sum(x)
+    out["ds_sum_2p26"] = {"GB/s": round(8.0 * n / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
+                          "abs_err_vs_fsum": abs(float(r.item()) - truth)}
+    return out
+
+
+REF_ROWS = 1024  # rows of A per reference step (a quarter of the GEMM)
+
+
+def run_reference(args):
+    """Each step multiplies one 1024-row block of A (cycling over the four
+    blocks) by B through the NumPy restatement of the reference DS pass, so a
+    step is about 0.3 s of host work; GFLOP/s counts that block's 2*m*N*K."""
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return None
+    A, B = gemm_inputs(0)
+    from oracle import ds_pass_ref
+    blocks = [A[i:i + REF_ROWS] for i in range(0, GEMM_DIM, REF_ROWS)]
+    for i in range(args.warmup):
+        ds_pass_ref.dot_general_f64(blocks[i % len(blocks)], B)
+    t = time.perf_counter()
+    for i in range(args.steps):
+        ds_pass_ref.dot_general_f64(blocks[i % len(blocks)], B)
+    dt = (time.perf_counter() - t) / args.steps
+    value = 2.0 * REF_ROWS * GEMM_DIM * GEMM_DIM / dt / 1e9
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "GFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32x2 (DS)", "data": "synthetic (default_rng(2))",
+        "config": {"workload": "ds_dot_general_f64 4096x4096x4096 (A, B f64 U[-1,1] seed 2)",
+                   "M": GEMM_DIM, "N": GEMM_DIM, "K": GEMM_DIM},
+        "cpu_baseline": {"value": round(value, 2), "unit": "GFLOP/s", "cores": host_cores(),
+                         "kind": "port",
+                         "sample": f"per step a {REF_ROWS}x4096 block of A times B (4096^2): "
+                                   "the DS pass restated in NumPy (split, 4 float32 matmuls, "
+                                   "two_sum, recombine) with BLAS on all host cores; the "
+                                   "reference needs JAX/XLA, absent in this image"},
+        "e2e": {"value": round(value, 2), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gemm")
+    ap.add_argument("--algorithm", default="tensor", choices=["tensor", "cuda_core"])
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if line is not None:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,478 @@
+// The C ABI of libds_b200 (declared in include/ds_b200.h): shape checks with
+// the reference handlers' messages, then the launchers in kernels.h.
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsb {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int ok() { return DS_OK; }
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(cache.size())) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+namespace {
+
+int invalid(const std::string& msg) { return set_error(DS_INVALID_ARGUMENT, msg); }
+
+bool valid_buffer(const ds_buffer* b) {
+  return b != nullptr && b->rank >= 0 && b->rank <= 16 && (b->rank == 0 || b->dims != nullptr);
+}
+
+// Product of all dims but the last (cpp/ds_add.cpp:8-13); 1 for rank <= 1.
+int64_t batch_size(const ds_buffer* b) {
+  int64_t n = 1;
+  for (int64_t i = 0; i + 1 < b->rank; ++i) n *= b->dims[i];
+  return n;
+}
+
+int64_t last_dim(const ds_buffer* b) { return b->rank > 0 ? b->dims[b->rank - 1] : 1; }
+
+int64_t total(const ds_buffer* b) {
+  int64_t n = 1;
+  for (int64_t i = 0; i < b->rank; ++i) n *= b->dims[i];
+  return n;
+}
+
+bool bad_dims(const ds_buffer* b) {
+  for (int64_t i = 0; i < b->rank; ++i)
+    if (b->dims[i] < 0) return true;
+  return false;
+}
+
+int check_buffers(std::initializer_list<const ds_buffer*> bufs, const char* op) {
+  for (const ds_buffer* b : bufs) {
+    if (!valid_buffer(b) || bad_dims(b)) return invalid(std::string(op) + ": invalid buffer descriptor");
+  }
+  for (const ds_buffer* b : bufs) {
+    if (total(b) > 0 && b->data == nullptr) return invalid(std::string(op) + ": null data pointer");
+  }
+  return DS_OK;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Shape checks of DsAdd / DsSub / DsMul (cpp/ds_add.cpp:30-38).
+int packed_binary(const char* op, int which, const ds_buffer* a, const ds_buffer* b,
+                  const ds_buffer* y, void* stream) {
+  if (int st = check_buffers({a, b, y}, op)) return st;
+  const std::string name(op);
+  if (a->rank == 0 || b->rank == 0 || last_dim(a) != 2 || last_dim(b) != 2)
+    return invalid(name + " expects last dim == 2");
+  if (a->rank != b->rank || batch_size(a) != batch_size(b))
+    return invalid(name + " input shapes must match");
+  if (y->rank == 0 || last_dim(y) != 2 || batch_size(y) != batch_size(a))
+    return invalid(name + " output shape mismatch");
+  return ew_packed(which, static_cast<const float*>(a->data), static_cast<const float*>(b->data),
+                   static_cast<float*>(y->data), batch_size(a), as_stream(stream));
+}
+
+// Shape checks of the rank-1 fused handlers (cpp/ds_fused_add_mul_to_f64.cpp:
+// 265-274): rank-1 inputs of equal length, output [N] (or [N,2] when packed).
+int fused_checks(const char* op, std::initializer_list<const ds_buffer*> ins,
+                 const ds_buffer* out, bool packed_out) {
+  std::vector<const ds_buffer*> all(ins);
+  all.push_back(out);
+  for (const ds_buffer* b : all)
+    if (!valid_buffer(b) || bad_dims(b)) return invalid(std::string(op) + ": invalid buffer descriptor");
+  for (const ds_buffer* b : ins)
+    if (b->rank != 1) return invalid(std::string(op) + " expects rank-1 inputs");
+  const int64_t n = (*ins.begin())->dims[0];
+  for (const ds_buffer* b : ins)
+    if (b->dims[0] != n) return invalid("input lengths must match");
+  if (packed_out) {
+    if (out->rank != 2 || out->dims[0] != n || out->dims[1] != 2)
+      return invalid("output shape must be [N,2]");
+  } else if (out->rank != 1 || out->dims[0] != n) {
+    return invalid("output shape must be [N]");
+  }
+  for (const ds_buffer* b : all)
+    if (n > 0 && b->data == nullptr) return invalid(std::string(op) + ": null data pointer");
+  return DS_OK;
+}
+
+const double* f64p(const ds_buffer* b) { return static_cast<const double*>(b->data); }
+
+// [outer, red, inner] view of a reduce over contiguous ascending dims.
+int reduce_geometry(const char* op, const ds_buffer* in, const int64_t* dims, int64_t nd,
+                    const ds_buffer* out, int64_t& outer, int64_t& red, int64_t& inner) {
+  if (nd < 0 || (nd > 0 && dims == nullptr)) return invalid(std::string(op) + ": invalid dimensions");
+  for (int64_t i = 0; i < nd; ++i) {
+    if (dims[i] < 0 || dims[i] >= in->rank)
+      return invalid(std::string(op) + ": reduce dimension out of range");
+    if (i > 0 && dims[i] != dims[i - 1] + 1)
+      return invalid(std::string(op) +
+                     ": reduce dimensions must be contiguous and ascending");
+  }
+  outer = 1;
+  red = 1;
+  inner = 1;
+  const int64_t d0 = nd > 0 ? dims[0] : in->rank;
+  for (int64_t i = 0; i < in->rank; ++i) {
+    if (i < d0)
+      outer *= in->dims[i];
+    else if (i < d0 + nd)
+      red *= in->dims[i];
+    else
+      inner *= in->dims[i];
+  }
+  // Output shape: the input shape without the reduced dims.
+  if (out->rank != in->rank - nd) return invalid(std::string(op) + ": output shape mismatch");
+  for (int64_t i = 0, o = 0; i < in->rank; ++i) {
+    if (i >= d0 && i < d0 + nd) continue;
+    if (out->dims[o++] != in->dims[i]) return invalid(std::string(op) + ": output shape mismatch");
+  }
+  return DS_OK;
+}
+
+struct DotGeom {
+  int64_t batch = 1, M = 1, N = 1, K = 0;
+  int64_t a_sb = 0, a_sr = 0, a_sk = 1;
+  int64_t b_sb = 0, b_sr = 0, b_sk = 1;
+};
+
+// Operand view of one dot_general side: [batch..., free?, K] in any order of
+// the last two dims.
+int dot_side(const ds_buffer* x, int64_t nb, int64_t contracting, int64_t& rows, int64_t& K,
+             int64_t& s_b, int64_t& s_r, int64_t& s_k) {
+  const int64_t r = x->rank;
+  if (r != nb + 1 && r != nb + 2) return invalid("dot_general: each operand must have one free dimension at most");
+  if (contracting < nb || contracting >= r) return invalid("dot_general: contracting dimension must follow the batch dimensions");
+  int64_t inner = 1;
+  for (int64_t i = nb; i < r; ++i) inner *= x->dims[i];
+  s_b = inner;
+  K = x->dims[contracting];
+  if (r == nb + 1) {
+    rows = 1;
+    s_r = 0;
+    s_k = 1;
+  } else if (contracting == r - 1) {
+    rows = x->dims[r - 2];
+    s_r = K;
+    s_k = 1;
+  } else {
+    rows = x->dims[r - 1];
+    s_r = 1;
+    s_k = rows;
+  }
+  return DS_OK;
+}
+
+int dot_geometry(const ds_buffer* lhs, const ds_buffer* rhs, const ds_dot_dims* dd,
+                 const ds_buffer* out, DotGeom& g) {
+  if (dd == nullptr) return invalid("dot_general: missing dimension numbers");
+  const int64_t nb = dd->n_batch;
+  if (nb < 0 || nb > 4) return invalid("dot_general: at most 4 batch dimensions");
+  g.batch = 1;
+  for (int64_t i = 0; i < nb; ++i) {
+    if (dd->lhs_batch[i] != i || dd->rhs_batch[i] != i)
+      return invalid("dot_general: batch dimensions must be the leading dimensions");
+    if (i >= lhs->rank || i >= rhs->rank || lhs->dims[i] != rhs->dims[i])
+      return invalid("dot_general: batch dimensions must match");
+    g.batch *= lhs->dims[i];
+  }
+  int64_t Ka = 0, Kb = 0;
+  if (int st = dot_side(lhs, nb, dd->lhs_contracting, g.M, Ka, g.a_sb, g.a_sr, g.a_sk)) return st;
+  if (int st = dot_side(rhs, nb, dd->rhs_contracting, g.N, Kb, g.b_sb, g.b_sr, g.b_sk)) return st;
+  if (Ka != Kb) return invalid("dot_general: contracting dimensions must match");
+  g.K = Ka;
+  // Result: [batch..., lhs free?, rhs free?].
+  std::vector<int64_t> want(lhs->dims, lhs->dims + nb);
+  if (lhs->rank == nb + 2) want.push_back(g.M);
+  if (rhs->rank == nb + 2) want.push_back(g.N);
+  if (out->rank != static_cast<int64_t>(want.size())) return invalid("dot_general: output shape mismatch");
+  for (size_t i = 0; i < want.size(); ++i)
+    if (out->dims[i] != want[i]) return invalid("dot_general: output shape mismatch");
+  return DS_OK;
+}
+
+size_t dot_workspace(const DotGeom& g, int32_t algorithm) {
+  if (g.M == 1 && g.N == 1) return dot_vec_workspace_bytes(g.batch, g.K);
+  if (algorithm == DS_DOT_TENSOR_INT8 && dot_ozaki_supported(g.M, g.N, g.K))
+    return dot_ozaki_workspace_bytes(g.batch, g.M, g.N, g.K);
+  return 0;
+}
+
+int dot_run(const DotGeom& g, DotProblem& p, int32_t algorithm, void* ws, size_t ws_bytes,
+            cudaStream_t s) {
+  p.batch = g.batch;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.a.s_b = g.a_sb;
+  p.a.s_r = g.a_sr;
+  p.a.s_k = g.a_sk;
+  p.b.s_b = g.b_sb;
+  p.b.s_r = g.b_sr;
+  p.b.s_k = g.b_sk;
+  if (algorithm != DS_DOT_TENSOR_INT8 && algorithm != DS_DOT_CUDA_CORE)
+    return invalid("dot_general: unknown algorithm");
+  if (g.M == 1 && g.N == 1) return dot_batched_vec(p, ws, ws_bytes, s);
+  if (algorithm == DS_DOT_TENSOR_INT8 && dot_ozaki_supported(g.M, g.N, g.K))
+    return dot_ozaki(p, ws, ws_bytes, s);
+  return dot_simt(p, s);
+}
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+extern "C" {
+
+const char* ds_last_error(void) { return g_last_error.c_str(); }
+
+const char* ds_version(void) { return "ds_b200 0.1 (sm_100a)"; }
+
+int ds_from_f64(const ds_buffer* x, const ds_buffer* y, void* stream) {
+  if (int st = check_buffers({x, y}, "ds_from_f64")) return st;
+  if (y->rank == 0 || last_dim(y) != 2) return invalid("ds_from_f64 output last dim must be 2");
+  const int64_t n = batch_size(x) * last_dim(x);
+  if (batch_size(y) != n) return invalid("ds_from_f64 shape mismatch");
+  return ew_from_f64(f64p(x), static_cast<float*>(y->data), n, as_stream(stream));
+}
+
+int ds_to_f64(const ds_buffer* x, const ds_buffer* y, void* stream) {
+  if (int st = check_buffers({x, y}, "ds_to_f64")) return st;
+  if (x->rank == 0 || last_dim(x) != 2) return invalid("ds_to_f64 input last dim must be 2");
+  if (batch_size(x) != batch_size(y) * last_dim(y)) return invalid("ds_to_f64 shape mismatch");
+  return ew_to_f64(static_cast<const float*>(x->data), static_cast<double*>(y->data),
+                   batch_size(x), as_stream(stream));
+}
+
+int ds_from_f32(const ds_buffer* x, const ds_buffer* y, void* stream) {
+  if (int st = check_buffers({x, y}, "ds_from_f32")) return st;
+  if (y->rank == 0 || last_dim(y) != 2) return invalid("ds_from_f32 output last dim must be 2");
+  if (total(x) * 2 != total(y)) return invalid("ds_from_f32 shape mismatch");
+  return ew_from_f32(static_cast<const float*>(x->data), static_cast<float*>(y->data), total(x),
+                     as_stream(stream));
+}
+
+int ds_to_f32(const ds_buffer* x, const ds_buffer* y, void* stream) {
+  if (int st = check_buffers({x, y}, "ds_to_f32")) return st;
+  if (x->rank == 0 || last_dim(x) != 2) return invalid("ds_to_f32 input last dim must be 2");
+  if (total(x) != total(y) * 2) return invalid("ds_to_f32 shape mismatch");
+  return ew_to_f32(static_cast<const float*>(x->data), static_cast<float*>(y->data), total(y),
+                   as_stream(stream));
+}
+
+int ds_add(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y, void* stream) {
+  return packed_binary("ds.add", 0, a, b, y, stream);
+}
+
+int ds_sub(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y, void* stream) {
+  return packed_binary("ds.sub", 1, a, b, y, stream);
+}
+
+int ds_mul(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y, void* stream) {
+  return packed_binary("ds.mul", 2, a, b, y, stream);
+}
+
+int ds_fused_add_mul(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out,
+                     void* stream) {
+  if (int st = fused_checks("ds.fused_add_mul", {x, y}, out, true)) return st;
+  return ew_fused_add_mul_packed(f64p(x), f64p(y), static_cast<float*>(out->data), x->dims[0],
+                                 as_stream(stream));
+}
+
+static int fused_add_mul_f64(const char* op, const ds_buffer* x, const ds_buffer* y,
+                             const ds_buffer* out, void* stream) {
+  if (int st = fused_checks(op, {x, y}, out, false)) return st;
+  return ew_fused_add_mul_f64(f64p(x), f64p(y), static_cast<double*>(out->data), x->dims[0],
+                              as_stream(stream));
+}
+
+int ds_fused_add_mul_to_f64(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out,
+                            void* stream) {
+  return fused_add_mul_f64("ds.fused_add_mul_to_f64", x, y, out, stream);
+}
+
+int ds_fused_axpy(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out, void* stream) {
+  return fused_add_mul_f64("ds_fused_axpy", x, y, out, stream);
+}
+
+int ds_fused_add_mul_to_f64_cuda(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out,
+                                 void* stream) {
+  return fused_add_mul_f64("ds_fused_add_mul_to_f64_cuda", x, y, out, stream);
+}
+
+int ds_fused_add_sub_to_f64_cuda(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out,
+                                 void* stream) {
+  if (int st = fused_checks("ds_fused_add_sub_to_f64_cuda", {x, y}, out, false)) return st;
+  return ew_fused_add_sub_f64(f64p(x), f64p(y), static_cast<double*>(out->data), x->dims[0],
+                              as_stream(stream));
+}
+
+int ds_recurrence_add_mul_to_f64_cuda(const ds_buffer* x, const ds_buffer* y, int32_t k,
+                                      const ds_buffer* out, void* stream) {
+  if (int st = fused_checks("ds_recurrence_add_mul_to_f64_cuda", {x, y}, out, false)) return st;
+  if (k < 0) return invalid("k must be nonnegative");
+  return ew_recurrence_add_mul(f64p(x), f64p(y), static_cast<double*>(out->data), x->dims[0], k,
+                               as_stream(stream));
+}
+
+int ds_fused_add_mul3_to_f64(const ds_buffer* a, const ds_buffer* b, const ds_buffer* c,
+                             const ds_buffer* out, void* stream) {
+  if (int st = fused_checks("ds_fused_add_mul3_to_f64", {a, b, c}, out, false)) return st;
+  return ew_fused_add_mul3_f64(f64p(a), f64p(b), f64p(c), static_cast<double*>(out->data),
+                               a->dims[0], as_stream(stream));
+}
+
+int ds_recurrence_mul_add_to_f64(const ds_buffer* x, const ds_buffer* a, const ds_buffer* b,
+                                 int32_t k, const ds_buffer* out, void* stream) {
+  if (int st = fused_checks("ds_recurrence_mul_add_to_f64", {x, a, b}, out, false)) return st;
+  if (k < 0) return invalid("k must be nonnegative");
+  return ew_recurrence_mul_add(f64p(x), f64p(a), f64p(b), static_cast<double*>(out->data),
+                               x->dims[0], k, as_stream(stream));
+}
+
+size_t ds_reduce_workspace_size(const ds_buffer* in, const int64_t* dimensions,
+                                int64_t n_dimensions) {
+  if (!valid_buffer(in) || bad_dims(in)) return 0;
+  if (n_dimensions < 0 || (n_dimensions > 0 && dimensions == nullptr)) return 0;
+  for (int64_t i = 0; i < n_dimensions; ++i)
+    if (dimensions[i] < 0 || dimensions[i] >= in->rank) return 0;
+  const int64_t d0 = n_dimensions > 0 ? dimensions[0] : in->rank;
+  int64_t outer = 1, red = 1, inner = 1;
+  for (int64_t i = 0; i < in->rank; ++i) {
+    if (i < d0)
+      outer *= in->dims[i];
+    else if (i < d0 + n_dimensions)
+      red *= in->dims[i];
+    else
+      inner *= in->dims[i];
+  }
+  return reduce_workspace_bytes(outer, red, inner);
+}
+
+static int reduce_common(const char* op, const ds_buffer* in, const int64_t* dimensions,
+                         int64_t n_dimensions, int32_t body, const ds_buffer* out,
+                         ReduceArgs& args) {
+  if (body < DS_BODY_ADD || body > DS_BODY_MUL) return invalid(std::string(op) + ": unknown body");
+  return reduce_geometry(op, in, dimensions, n_dimensions, out, args.outer, args.red, args.inner);
+}
+
+int ds_reduce(const ds_buffer* in_hi, const ds_buffer* in_lo, const ds_buffer* init_hi,
+              const ds_buffer* init_lo, const int64_t* dimensions, int64_t n_dimensions,
+              int32_t body, const ds_buffer* out_hi, const ds_buffer* out_lo, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({in_hi, in_lo, init_hi, init_lo, out_hi, out_lo}, "ds_reduce"))
+    return st;
+  if (in_hi->rank != in_lo->rank || total(in_hi) != total(in_lo))
+    return invalid("ds_reduce: hi and lo inputs must have the same shape");
+  if (out_hi->rank != out_lo->rank || total(out_hi) != total(out_lo))
+    return invalid("ds_reduce: hi and lo outputs must have the same shape");
+  if (total(init_hi) != 1 || total(init_lo) != 1)
+    return invalid("ds_reduce: init values must be scalars");
+  ReduceArgs a;
+  if (int st = reduce_common("ds_reduce", in_hi, dimensions, n_dimensions, body, out_hi, a))
+    return st;
+  a.in_hi = static_cast<const float*>(in_hi->data);
+  a.in_lo = static_cast<const float*>(in_lo->data);
+  a.init_hi = static_cast<const float*>(init_hi->data);
+  a.init_lo = static_cast<const float*>(init_lo->data);
+  a.out_hi = static_cast<float*>(out_hi->data);
+  a.out_lo = static_cast<float*>(out_lo->data);
+  a.body = body;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return reduce_launch(a, as_stream(stream));
+}
+
+int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dimensions,
+                  int64_t n_dimensions, int32_t body, const ds_buffer* out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({in, init, out}, "ds_reduce_f64")) return st;
+  if (total(init) != 1) return invalid("ds_reduce_f64: init value must be a scalar");
+  ReduceArgs a;
+  if (int st = reduce_common("ds_reduce_f64", in, dimensions, n_dimensions, body, out, a))
+    return st;
+  a.in_f64 = f64p(in);
+  a.init_f64 = f64p(init);
+  a.out_f64 = static_cast<double*>(out->data);
+  a.body = body;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return reduce_launch(a, as_stream(stream));
+}
+
+size_t ds_dot_general_workspace_size(const ds_buffer* lhs, const ds_buffer* rhs,
+                                     const ds_dot_dims* dims, int32_t algorithm) {
+  if (!valid_buffer(lhs) || !valid_buffer(rhs) || bad_dims(lhs) || bad_dims(rhs)) return 0;
+  DotGeom g;
+  // Build the expected output descriptor from the operands to reuse the checks.
+  std::vector<int64_t> od;
+  if (dims == nullptr || dims->n_batch < 0 || dims->n_batch > 4) return 0;
+  for (int64_t i = 0; i < dims->n_batch && i < lhs->rank; ++i) od.push_back(lhs->dims[i]);
+  const int64_t nb = dims->n_batch;
+  if (lhs->rank == nb + 2) od.push_back(lhs->dims[dims->lhs_contracting == nb + 1 ? nb : nb + 1]);
+  if (rhs->rank == nb + 2) od.push_back(rhs->dims[dims->rhs_contracting == nb ? nb + 1 : nb]);
+  ds_buffer out{nullptr, od.data(), static_cast<int64_t>(od.size())};
+  const std::string saved = g_last_error;
+  const int st = dot_geometry(lhs, rhs, dims, &out, g);
+  g_last_error = saved;
+  if (st != DS_OK) return 0;
+  return dot_workspace(g, algorithm);
+}
+
+int ds_dot_general(const ds_buffer* lhs_hi, const ds_buffer* lhs_lo, const ds_buffer* rhs_hi,
+                   const ds_buffer* rhs_lo, const ds_dot_dims* dims, int32_t algorithm,
+                   const ds_buffer* out_hi, const ds_buffer* out_lo, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({lhs_hi, lhs_lo, rhs_hi, rhs_lo, out_hi, out_lo}, "ds_dot_general"))
+    return st;
+  if (total(lhs_hi) != total(lhs_lo) || total(rhs_hi) != total(rhs_lo) ||
+      total(out_hi) != total(out_lo))
+    return invalid("ds_dot_general: hi and lo tensors must have the same shape");
+  DotGeom g;
+  if (int st = dot_geometry(lhs_hi, rhs_hi, dims, out_hi, g)) return st;
+  DotProblem p;
+  p.a.hi = static_cast<const float*>(lhs_hi->data);
+  p.a.lo = static_cast<const float*>(lhs_lo->data);
+  p.b.hi = static_cast<const float*>(rhs_hi->data);
+  p.b.lo = static_cast<const float*>(rhs_lo->data);
+  p.c.hi = static_cast<float*>(out_hi->data);
+  p.c.lo = static_cast<float*>(out_lo->data);
+  return dot_run(g, p, algorithm, workspace, workspace_bytes, as_stream(stream));
+}
+
+int ds_dot_general_f64(const ds_buffer* lhs, const ds_buffer* rhs, const ds_dot_dims* dims,
+                       int32_t algorithm, const ds_buffer* out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({lhs, rhs, out}, "ds_dot_general_f64")) return st;
+  DotGeom g;
+  if (int st = dot_geometry(lhs, rhs, dims, out, g)) return st;
+  DotProblem p;
+  p.a.f64 = f64p(lhs);
+  p.b.f64 = f64p(rhs);
+  p.c.f64 = static_cast<double*>(out->data);
+  return dot_run(g, p, algorithm, workspace, workspace_bytes, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,239 @@
+// DS reduce: the reduce body of the DS pass (DsTransformPass.cpp:376-448,
+// acc = ds_op(acc, elem) over (hi, lo) pairs) as CUDA kernels.
+//
+// Shapes are viewed as [outer, red, inner] (the reduced dimensions are
+// contiguous).  Three kernels cover that:
+//   - outer == 1, inner == 1 (a full reduction, e.g. jnp.sum of a vector):
+//     every thread folds a grid-strided set of elements in index order (two
+//     16-byte loads per step: f64 pairs, or hi/lo pairs), a warp shuffle tree
+//     and a block tree combine threads, and block partials go to the caller's
+//     workspace; a one-block kernel folds the partials with the same fixed
+//     tree and applies init.  With one block the first kernel finishes alone.
+//   - inner == 1, outer > 1: one block per row.
+//   - inner > 1: one thread per (outer, inner) column, folding `red`
+//     elements in order (coalesced across the inner index).
+// Add and subtract bodies accumulate with ds_add (subtract: init - sum);
+// multiply accumulates with ds_mul.  Every combine order is fixed by the
+// shape, so results are deterministic.  HBM-bound for long inputs.
+#include "common.cuh"
+#include "ds_arith.cuh"
+#include "kernels.h"
+#include "profile.h"
+
+namespace dsb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ ds2 combine(bool is_mul, ds2 a, ds2 b) {
+  return is_mul ? mul(a, b) : add(a, b);
+}
+
+__device__ __forceinline__ ds2 identity(bool is_mul) {
+  return ds2{is_mul ? 1.0f : 0.0f, 0.0f};
+}
+
+__device__ __forceinline__ ds2 shfl_down(ds2 v, int d) {
+  return ds2{__shfl_down_sync(0xffffffffu, v.hi, d), __shfl_down_sync(0xffffffffu, v.lo, d)};
+}
+
+// Block-wide fixed-order tree; the result is valid in thread 0.
+__device__ ds2 block_combine(bool is_mul, ds2 v) {
+  __shared__ ds2 warp_part[kWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = combine(is_mul, v, shfl_down(v, d));
+  if (lane == 0) warp_part[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < kWarps ? warp_part[lane] : identity(is_mul);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = combine(is_mul, v, shfl_down(v, d));
+  }
+  return v;
+}
+
+// Final step shared by every kernel: fold init in once, then write.
+__device__ __forceinline__ ds2 finish(int body, ds2 init, ds2 total) {
+  return body == 2 ? mul(init, total) : (body == 1 ? sub(init, total) : add(init, total));
+}
+
+struct Src {
+  const double* f64;  // f64 input (split on load), or
+  const float* hi;    // SoA DS input
+  const float* lo;
+  bool vec;           // 16-byte aligned pair loads allowed
+  __device__ __forceinline__ ds2 at(int64_t i) const {
+    return f64 ? from_f64(f64[i]) : ds2{hi[i], lo[i]};
+  }
+  __device__ __forceinline__ void pair(int64_t p, ds2& x0, ds2& x1) const {
+    if (f64) {
+      const double2 v = __ldcs(reinterpret_cast<const double2*>(f64) + p);
+      x0 = from_f64(v.x);
+      x1 = from_f64(v.y);
+    } else {
+      const float2 h = __ldcs(reinterpret_cast<const float2*>(hi) + p);
+      const float2 l = __ldcs(reinterpret_cast<const float2*>(lo) + p);
+      x0 = ds2{h.x, l.x};
+      x1 = ds2{h.y, l.y};
+    }
+  }
+};
+
+struct Dst {
+  double* f64;  // f64 output, or
+  float* hi;    // SoA DS output
+  float* lo;
+  __device__ __forceinline__ void put(int64_t i, ds2 v) const {
+    if (f64) {
+      f64[i] = to_f64(v);
+    } else {
+      hi[i] = v.hi;
+      lo[i] = v.lo;
+    }
+  }
+};
+
+__device__ __forceinline__ ds2 load_init(const double* init_f64, const float* init_hi,
+                                         const float* init_lo) {
+  return init_f64 ? from_f64(*init_f64) : ds2{*init_hi, *init_lo};
+}
+
+// Full reduction, stage 1.
+__global__ void __launch_bounds__(kThreads)
+reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
+                   const double* init_f64, const float* init_hi, const float* init_lo) {
+  const bool is_mul = body == 2;
+  ds2 acc = identity(is_mul);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (src.vec) {
+    const int64_t npairs = n >> 1;
+    for (int64_t base = tid; base < npairs; base += stride * kUnroll) {
+      ds2 x0[kUnroll], x1[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t p = base + u * stride;
+        if (p < npairs) src.pair(p, x0[u], x1[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t p = base + u * stride;
+        if (p < npairs) {
+          acc = combine(is_mul, acc, x0[u]);
+          acc = combine(is_mul, acc, x1[u]);
+        }
+      }
+    }
+    if ((n & 1) && tid == 0) acc = combine(is_mul, acc, src.at(n - 1));
+  } else {
+    for (int64_t i = tid; i < n; i += stride) acc = combine(is_mul, acc, src.at(i));
+  }
+  acc = block_combine(is_mul, acc);
+  if (threadIdx.x == 0) {
+    if (gridDim.x == 1) {
+      // An empty reduction returns init unchanged (bits included).
+      const ds2 init = load_init(init_f64, init_hi, init_lo);
+      dst.put(0, n == 0 ? init : finish(body, init, acc));
+    } else {
+      partials[blockIdx.x] = acc;
+    }
+  }
+}
+
+// Full reduction, stage 2: one block folds the G partials.
+__global__ void __launch_bounds__(kThreads)
+reduce_partials_kernel(const ds2* __restrict__ partials, int g, int body, Dst dst,
+                       const double* init_f64, const float* init_hi, const float* init_lo) {
+  const bool is_mul = body == 2;
+  ds2 acc = identity(is_mul);
+  for (int i = threadIdx.x; i < g; i += blockDim.x) acc = combine(is_mul, acc, partials[i]);
+  acc = block_combine(is_mul, acc);
+  if (threadIdx.x == 0) dst.put(0, finish(body, load_init(init_f64, init_hi, init_lo), acc));
+}
+
+// inner == 1, outer > 1: one block per row.
+__global__ void __launch_bounds__(kThreads)
+reduce_rows_kernel(Src src, int64_t outer, int64_t red, int body, Dst dst,
+                   const double* init_f64, const float* init_hi, const float* init_lo) {
+  const bool is_mul = body == 2;
+  const ds2 init = load_init(init_f64, init_hi, init_lo);
+  for (int64_t row = blockIdx.x; row < outer; row += gridDim.x) {
+    ds2 acc = identity(is_mul);
+    const int64_t off = row * red;
+    for (int64_t r = threadIdx.x; r < red; r += blockDim.x)
+      acc = combine(is_mul, acc, src.at(off + r));
+    acc = block_combine(is_mul, acc);
+    if (threadIdx.x == 0) dst.put(row, red == 0 ? init : finish(body, init, acc));
+    __syncthreads();
+  }
+}
+
+// inner > 1: one thread per (outer, inner) column.
+__global__ void __launch_bounds__(kThreads)
+reduce_cols_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body, Dst dst,
+                   const double* init_f64, const float* init_hi, const float* init_lo) {
+  const bool is_mul = body == 2;
+  const ds2 init = load_init(init_f64, init_hi, init_lo);
+  const int64_t cols = outer * inner;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < cols;
+       c += stride) {
+    const int64_t o = c / inner, j = c - o * inner;
+    const int64_t off = o * red * inner + j;
+    ds2 acc = identity(is_mul);
+    for (int64_t r = 0; r < red; ++r) acc = combine(is_mul, acc, src.at(off + r * inner));
+    dst.put(c, red == 0 ? init : finish(body, init, acc));
+  }
+}
+
+}  // namespace
+
+int reduce_full_blocks(int64_t n) {
+  return static_cast<int>(grid_for((n + 2 * kUnroll - 1) / (2 * kUnroll), kThreads, 4));
+}
+
+size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {
+  if (outer != 1 || inner != 1) return 0;
+  const int g = reduce_full_blocks(red);
+  return g > 1 ? static_cast<size_t>(g) * sizeof(ds2) : 0;
+}
+
+int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
+  Src src{a.in_f64, a.in_hi, a.in_lo, false};
+  src.vec = a.in_f64 ? aligned(a.in_f64, 16) : (aligned(a.in_hi, 8) && aligned(a.in_lo, 8));
+  Dst dst{a.out_f64, a.out_hi, a.out_lo};
+  const int64_t outer = a.outer, red = a.red, inner = a.inner;
+  if (outer * inner == 0) return ok();
+  if (outer == 1 && inner == 1) {
+    const int g = red == 0 ? 1 : reduce_full_blocks(red);
+    const size_t need = g > 1 ? static_cast<size_t>(g) * sizeof(ds2) : 0;
+    if (need > a.workspace_bytes || (need && !aligned(a.workspace, alignof(ds2)))) {
+      return set_error(DS_INVALID_ARGUMENT,
+                       "ds_reduce: workspace too small (need " + std::to_string(need) +
+                           " bytes, 8-byte aligned)");
+    }
+    ds2* partials = static_cast<ds2*>(a.workspace);
+    ProfileScope prof("reduce", s);
+    reduce_full_kernel<<<g, kThreads, 0, s>>>(src, red, a.body, partials, dst, a.init_f64,
+                                              a.init_hi, a.init_lo);
+    if (g > 1) {
+      reduce_partials_kernel<<<1, kThreads, 0, s>>>(partials, g, a.body, dst, a.init_f64,
+                                                    a.init_hi, a.init_lo);
+    }
+    return launch_status();
+  }
+  if (inner == 1) {
+    const unsigned g = static_cast<unsigned>(outer < sm_count() * 8 ? outer : sm_count() * 8);
+    reduce_rows_kernel<<<g, kThreads, 0, s>>>(src, outer, red, a.body, dst, a.init_f64,
+                                              a.init_hi, a.init_lo);
+    return launch_status();
+  }
+  reduce_cols_kernel<<<grid_for(outer * inner, kThreads, 8), kThreads, 0, s>>>(
+      src, outer, red, inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
+  return launch_status();
+}
+
+}  // namespace dsb

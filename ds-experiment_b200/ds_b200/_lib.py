@@ -1,0 +1,157 @@
+"""ctypes binding of libds_b200.so (the C ABI in include/ds_b200.h).
+
+Loading fails loudly when the library is missing: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libds_b200.so")
+
+DS_OK = 0
+DS_INVALID_ARGUMENT = 3
+DS_INTERNAL = 13
+
+DS_BODY_ADD, DS_BODY_SUB, DS_BODY_MUL = 0, 1, 2
+DS_DOT_TENSOR_INT8, DS_DOT_CUDA_CORE = 0, 1
+
+
+class DsError(RuntimeError):
+    """A non-OK ds_status; .code is the xla::ffi::ErrorCode value."""
+
+    def __init__(self, code, msg):
+        super().__init__(msg)
+        self.code = code
+
+
+class DsInvalidArgument(DsError, ValueError):
+    pass
+
+
+class DsInternal(DsError):
+    pass
+
+
+class DsBuffer(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p),
+                ("dims", ctypes.POINTER(ctypes.c_int64)),
+                ("rank", ctypes.c_int64)]
+
+
+class DsDotDims(ctypes.Structure):
+    _fields_ = [("n_batch", ctypes.c_int64),
+                ("lhs_batch", ctypes.c_int64 * 4),
+                ("rhs_batch", ctypes.c_int64 * 4),
+                ("lhs_contracting", ctypes.c_int64),
+                ("rhs_contracting", ctypes.c_int64)]
+
+
+_BUF = ctypes.POINTER(DsBuffer)
+_VP = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_DIMS = ctypes.POINTER(DsDotDims)
+
+# name -> (argtypes, restype)
+SIGNATURES = {
+    "ds_last_error": ([], ctypes.c_char_p),
+    "ds_version": ([], ctypes.c_char_p),
+    "ds_from_f64": ([_BUF, _BUF, _VP], ctypes.c_int),
+    "ds_to_f64": ([_BUF, _BUF, _VP], ctypes.c_int),
+    "ds_from_f32": ([_BUF, _BUF, _VP], ctypes.c_int),
+    "ds_to_f32": ([_BUF, _BUF, _VP], ctypes.c_int),
+    "ds_add": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_sub": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_mul": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_add_mul": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_add_mul_to_f64": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_axpy": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_add_mul_to_f64_cuda": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_add_sub_to_f64_cuda": ([_BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_recurrence_add_mul_to_f64_cuda": ([_BUF, _BUF, _I32, _BUF, _VP], ctypes.c_int),
+    "ds_fused_add_mul3_to_f64": ([_BUF, _BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_recurrence_mul_add_to_f64": ([_BUF, _BUF, _BUF, _I32, _BUF, _VP], ctypes.c_int),
+    "ds_reduce_workspace_size": ([_BUF, _I64P, _I64], _SZ),
+    "ds_reduce": ([_BUF, _BUF, _BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
+                  ctypes.c_int),
+    "ds_reduce_f64": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
+    "ds_dot_general_workspace_size": ([_BUF, _BUF, _DIMS, _I32], _SZ),
+    "ds_dot_general": ([_BUF, _BUF, _BUF, _BUF, _DIMS, _I32, _BUF, _BUF, _VP, _SZ, _VP],
+                       ctypes.c_int),
+    "ds_dot_general_f64": ([_BUF, _BUF, _DIMS, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
+    "ds_profile_enable": ([ctypes.c_int], None),
+    "ds_profile_reset": ([], None),
+    "ds_profile_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), _I64P], ctypes.c_int),
+}
+
+
+def profile_enable(on: bool = True) -> None:
+    lib().ds_profile_enable(1 if on else 0)
+
+
+def profile_reset() -> None:
+    lib().ds_profile_reset()
+
+
+def profile_read(name: str):
+    """(total milliseconds, launch count) of kernel family `name` since the
+    last reset; waits for the recorded events."""
+    ms = ctypes.c_double()
+    n = ctypes.c_int64()
+    check(lib().ds_profile_read(name.encode(), ctypes.byref(ms), ctypes.byref(n)), "profile")
+    return ms.value, n.value
+
+_lib = None
+
+
+def lib():
+    """Load libds_b200.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python ds-experiment_b200/build.py` "
+                "(there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (argtypes, restype) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().ds_last_error().decode()
+
+
+def check(status: int, what: str = "") -> None:
+    if status == DS_OK:
+        return
+    msg = last_error()
+    if status == DS_INVALID_ARGUMENT:
+        raise DsInvalidArgument(status, msg)
+    raise DsInternal(status, f"{what}: {msg}" if what else msg)
+
+
+def make_buffer(ptr: int, shape) -> tuple:
+    """A DsBuffer for `shape` at device address `ptr`; returns (buffer, dims)
+    (keep `dims` alive while the buffer is used)."""
+    shape = tuple(int(d) for d in shape)
+    dims = (ctypes.c_int64 * max(len(shape), 1))(*shape)
+    return DsBuffer(ptr, dims, len(shape)), dims
+
+
+def make_dot_dims(n_batch=0, lhs_contracting=1, rhs_contracting=0) -> DsDotDims:
+    d = DsDotDims()
+    d.n_batch = n_batch
+    for i in range(n_batch):
+        d.lhs_batch[i] = i
+        d.rhs_batch[i] = i
+    d.lhs_contracting = lhs_contracting
+    d.rhs_contracting = rhs_contracting
+    return d

@@ -1,0 +1,246 @@
+"""Custom-call surface of libds_b200, shaped like the reference's jax.ffi use.
+
+The reference registers its XLA-FFI handlers by target name and calls them
+with ``ffi.ffi_call(name, ShapeDtypeStruct(...), vmap_method=...)(*args,
+**attrs)`` (python/test_ds_add.py:16-48,
+python/test_ds_recurrence_add_mul_to_f64_cuda.py:18-31).  This module keeps
+that surface over torch CUDA tensors: ``register_ffi_target(name, lib.<sym>,
+platform="CUDA")`` binds a target name to a libds_b200 entry point, and
+``ffi_call`` allocates the results, passes torch's current CUDA stream and
+raises on a non-OK status.  Every reference target name is registered at
+import.  Scratch for ds_reduce / ds_dot_general comes from torch's caching
+allocator (the role XLA's scratch allocator plays for an FFI handler).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, Tuple
+
+import torch
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class ShapeDtypeStruct:
+    shape: Tuple[int, ...]
+    dtype: torch.dtype
+
+    def __init__(self, shape, dtype):
+        object.__setattr__(self, "shape", tuple(int(d) for d in shape))
+        object.__setattr__(self, "dtype", dtype)
+
+
+F64, F32 = torch.float64, torch.float32
+
+
+@dataclass(frozen=True)
+class _Convention:
+    """Operand dtypes, attribute names and result dtypes of one entry point,
+    in the order of the reference handler's Bind() (Args, Attrs, Rets)."""
+    args: Tuple[torch.dtype, ...]
+    attrs: Tuple[str, ...]
+    results: Tuple[torch.dtype, ...]
+    kind: str = "plain"  # plain | reduce | reduce_f64 | dot | dot_f64
+
+
+CONVENTIONS: Dict[str, _Convention] = {
+    "ds_from_f64": _Convention((F64,), (), (F32,)),
+    "ds_to_f64": _Convention((F32,), (), (F64,)),
+    "ds_from_f32": _Convention((F32,), (), (F32,)),
+    "ds_to_f32": _Convention((F32,), (), (F32,)),
+    "ds_add": _Convention((F32, F32), (), (F32,)),
+    "ds_sub": _Convention((F32, F32), (), (F32,)),
+    "ds_mul": _Convention((F32, F32), (), (F32,)),
+    "ds_fused_add_mul": _Convention((F64, F64), (), (F32,)),
+    "ds_fused_add_mul_to_f64": _Convention((F64, F64), (), (F64,)),
+    "ds_fused_axpy": _Convention((F64, F64), (), (F64,)),
+    "ds_fused_add_mul_to_f64_cuda": _Convention((F64, F64), (), (F64,)),
+    "ds_fused_add_sub_to_f64_cuda": _Convention((F64, F64), (), (F64,)),
+    "ds_recurrence_add_mul_to_f64_cuda": _Convention((F64, F64), ("k",), (F64,)),
+    "ds_fused_add_mul3_to_f64": _Convention((F64, F64, F64), (), (F64,)),
+    "ds_recurrence_mul_add_to_f64": _Convention((F64, F64, F64), ("k",), (F64,)),
+    "ds_reduce": _Convention((F32, F32, F32, F32), ("dimensions", "body"), (F32, F32),
+                             "reduce"),
+    "ds_reduce_f64": _Convention((F64, F64), ("dimensions", "body"), (F64,), "reduce_f64"),
+    "ds_dot_general": _Convention((F32, F32, F32, F32),
+                                  ("lhs_batching_dimensions", "rhs_batching_dimensions",
+                                   "lhs_contracting_dimensions",
+                                   "rhs_contracting_dimensions", "algorithm"),
+                                  (F32, F32), "dot"),
+    "ds_dot_general_f64": _Convention((F64, F64),
+                                      ("lhs_batching_dimensions", "rhs_batching_dimensions",
+                                       "lhs_contracting_dimensions",
+                                       "rhs_contracting_dimensions", "algorithm"),
+                                      (F64,), "dot_f64"),
+}
+
+# The reference's target names, each bound to its replacement entry point.
+REFERENCE_TARGETS = {
+    "ds_from_f64": "ds_from_f64",
+    "ds_to_f64": "ds_to_f64",
+    "ds_from_f32": "ds_from_f32",
+    "ds_to_f32": "ds_to_f32",
+    "ds_add": "ds_add",
+    "ds_sub": "ds_sub",
+    "ds_mul": "ds_mul",
+    "ds_fused_add_mul": "ds_fused_add_mul",
+    "ds_fused_add_mul_to_f64": "ds_fused_add_mul_to_f64",
+    "ds_fused_axpy": "ds_fused_axpy",
+    "ds_fused_add_mul_to_f64_cuda": "ds_fused_add_mul_to_f64_cuda",
+    "ds_fused_add_sub_to_f64_cuda": "ds_fused_add_sub_to_f64_cuda",
+    "ds_recurrence_add_mul_to_f64_cuda": "ds_recurrence_add_mul_to_f64_cuda",
+    "ds_fused_add_mul3_to_f64": "ds_fused_add_mul3_to_f64",
+    "ds_recurrence_mul_add_to_f64": "ds_recurrence_mul_add_to_f64",
+    "ds_reduce": "ds_reduce",
+    "ds_reduce_f64": "ds_reduce_f64",
+    "ds_dot_general": "ds_dot_general",
+    "ds_dot_general_f64": "ds_dot_general_f64",
+}
+
+# target name -> libds_b200 symbol; every reference target is bound at import.
+_registry: Dict[str, str] = dict(REFERENCE_TARGETS)
+
+
+def register_ffi_target(name: str, target, platform: str = "CUDA") -> None:
+    """Bind custom-call target `name` to a libds_b200 entry point.
+
+    `target` is a ctypes function of libds_b200 (``lib.ds_add``) or its
+    symbol name.  Only platform "CUDA" exists: there is no host fallback.
+    """
+    if platform.upper() not in ("CUDA", "GPU"):
+        raise ValueError(f"platform {platform!r} is not provided; libds_b200 runs on CUDA only")
+    sym = target if isinstance(target, str) else getattr(target, "__name__", None)
+    if sym not in CONVENTIONS:
+        raise ValueError(f"{sym!r} is not a libds_b200 entry point")
+    _registry[name] = sym
+
+
+def registered_targets():
+    return sorted(_registry)
+
+
+def _stream_handle() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check_tensor(t, dtype, what):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{what}: expected a torch.Tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError(f"{what}: libds_b200 operates on CUDA tensors only")
+    if t.dtype != dtype:
+        raise TypeError(f"{what}: expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{what}: tensor must be contiguous (row-major)")
+
+
+def _buf(t):
+    return _lib.make_buffer(t.data_ptr(), t.shape)
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
+    """Return a callable running target `target_name` on torch CUDA tensors.
+
+    result_shape_dtypes: a ShapeDtypeStruct or a sequence of them, one per
+    result.  Attributes are keyword arguments, as in jax.ffi.ffi_call.
+    vmap_method is accepted for signature compatibility; the entry points
+    already take arbitrary leading (batch) dimensions.
+    """
+    if target_name not in _registry:
+        raise KeyError(f"custom-call target {target_name!r} is not registered")
+    sym = _registry[target_name]
+    conv = CONVENTIONS[sym]
+    fn = getattr(_lib.lib(), sym)
+    single = isinstance(result_shape_dtypes, ShapeDtypeStruct)
+    results_spec = [result_shape_dtypes] if single else list(result_shape_dtypes)
+    if len(results_spec) != len(conv.results):
+        raise ValueError(f"{target_name}: expected {len(conv.results)} result(s)")
+    for spec, dt in zip(results_spec, conv.results):
+        if spec.dtype != dt:
+            raise TypeError(f"{target_name}: result dtype must be {dt}, got {spec.dtype}")
+
+    def call(*args: torch.Tensor, **attrs):
+        if len(args) != len(conv.args):
+            raise TypeError(f"{target_name}: expected {len(conv.args)} operand(s), got {len(args)}")
+        for i, (t, dt) in enumerate(zip(args, conv.args)):
+            _check_tensor(t, dt, f"{target_name} operand {i}")
+        unknown = set(attrs) - set(conv.attrs)
+        if unknown:
+            raise TypeError(f"{target_name}: unknown attribute(s) {sorted(unknown)}")
+        device = args[0].device
+        with torch.cuda.device(device):
+            outs = [torch.empty(s.shape, dtype=s.dtype, device=device) for s in results_spec]
+            keep = []
+            bufs = []
+            for t in list(args) + outs:
+                b, d = _buf(t)
+                keep.append(d)
+                bufs.append(b)
+            refs = [ctypes.byref(b) for b in bufs]
+            stream = _stream_handle()
+            if conv.kind == "plain":
+                call_args = refs[:len(args)]
+                for name in conv.attrs:
+                    if name not in attrs:
+                        raise TypeError(f"{target_name}: missing attribute {name!r}")
+                    call_args.append(int(attrs[name]))
+                call_args += refs[len(args):]
+                status = fn(*call_args, stream)
+            elif conv.kind in ("reduce", "reduce_f64"):
+                dims = tuple(int(d) for d in attrs.get("dimensions", ()))
+                body = int(attrs.get("body", _lib.DS_BODY_ADD))
+                cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
+                ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
+                ws = _workspace(ws_bytes, device)
+                if conv.kind == "reduce":
+                    status = fn(refs[0], refs[1], refs[2], refs[3], cdims, len(dims), body,
+                                refs[4], refs[5], ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+                                stream)
+                else:
+                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2],
+                                ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream)
+            else:
+                dd = _dot_dims(attrs, args[0].dim())
+                algorithm = int(attrs.get("algorithm", _lib.DS_DOT_TENSOR_INT8))
+                rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
+                ws_bytes = _lib.lib().ds_dot_general_workspace_size(
+                    refs[0], rhs_ref, ctypes.byref(dd), algorithm)
+                ws = _workspace(ws_bytes, device)
+                wsp = ctypes.c_void_p(ws.data_ptr())
+                if conv.kind == "dot":
+                    status = fn(refs[0], refs[1], refs[2], refs[3], ctypes.byref(dd), algorithm,
+                                refs[4], refs[5], wsp, ws_bytes, stream)
+                else:
+                    status = fn(refs[0], refs[1], ctypes.byref(dd), algorithm, refs[2], wsp,
+                                ws_bytes, stream)
+            _lib.check(status, target_name)
+        return outs[0] if single else tuple(outs)
+
+    return call
+
+
+def _dot_dims(attrs, lhs_rank) -> _lib.DsDotDims:
+    lb = tuple(attrs.get("lhs_batching_dimensions", ()))
+    rb = tuple(attrs.get("rhs_batching_dimensions", ()))
+    lc = tuple(attrs.get("lhs_contracting_dimensions", (lhs_rank - 1,)))
+    rc = tuple(attrs.get("rhs_contracting_dimensions", (len(rb),)))
+    if len(lb) != len(rb):
+        raise ValueError("dot_general: lhs and rhs batching dimensions differ in count")
+    if len(lc) != 1 or len(rc) != 1:
+        raise ValueError("dot_general: exactly one contracting dimension per operand is supported")
+    if len(lb) > 4:
+        raise ValueError("dot_general: at most 4 batch dimensions")
+    d = _lib.DsDotDims()
+    d.n_batch = len(lb)
+    for i, (x, y) in enumerate(zip(lb, rb)):
+        d.lhs_batch[i] = int(x)
+        d.rhs_batch[i] = int(y)
+    d.lhs_contracting = int(lc[0])
+    d.rhs_contracting = int(rc[0])
+    return d

@@ -1,0 +1,179 @@
+"""Python functions over the custom-call targets, one per reference op.
+
+They mirror the helper functions of the reference's FFI tests
+(python/test_ds_add.py:35-48: ``ds_from_f64(x)``, ``ds_add(a, b)``,
+``ds_to_f64(x)``; python/test_ds_recurrence_add_mul_to_f64_cuda.py:24-31),
+and add the DS pass's reduce and dot_general (DsTransformPass.cpp:337-448)
+as ``ds_reduce*`` and ``ds_dot_general*``.  All take and return torch CUDA
+tensors and run on torch's current stream.
+"""
+from __future__ import annotations
+
+from typing import Iterable, Optional, Sequence
+
+import torch
+
+from . import _lib
+from .ffi import ShapeDtypeStruct, ffi_call
+
+F64, F32 = torch.float64, torch.float32
+
+_BODIES = {"add": _lib.DS_BODY_ADD, "sub": _lib.DS_BODY_SUB, "subtract": _lib.DS_BODY_SUB,
+           "mul": _lib.DS_BODY_MUL, "multiply": _lib.DS_BODY_MUL}
+_ALGOS = {"tensor": _lib.DS_DOT_TENSOR_INT8, "int8": _lib.DS_DOT_TENSOR_INT8,
+          "cuda_core": _lib.DS_DOT_CUDA_CORE, "simt": _lib.DS_DOT_CUDA_CORE}
+
+
+def _sds(shape, dtype):
+    return ShapeDtypeStruct(tuple(shape), dtype)
+
+
+# ---- split / recombine ------------------------------------------------------
+
+def ds_from_f64(x: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_from_f64", _sds(tuple(x.shape) + (2,), F32))(x)
+
+
+def ds_to_f64(x: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_to_f64", _sds(tuple(x.shape[:-1]), F64))(x)
+
+
+def ds_from_f32(x: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_from_f32", _sds(tuple(x.shape) + (2,), F32))(x)
+
+
+def ds_to_f32(x: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_to_f32", _sds(tuple(x.shape[:-1]), F32))(x)
+
+
+# ---- packed elementwise -------------------------------------------------------
+
+def ds_add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_add", _sds(a.shape, F32))(a, b)
+
+
+def ds_sub(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_sub", _sds(a.shape, F32))(a, b)
+
+
+def ds_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return ffi_call("ds_mul", _sds(a.shape, F32))(a, b)
+
+
+# ---- fused f64 chains -----------------------------------------------------------
+
+def ds_fused_add_mul(x, y):
+    """(x + y) * y -> packed DS [N, 2]."""
+    return ffi_call("ds_fused_add_mul", _sds(tuple(x.shape) + (2,), F32))(x, y)
+
+
+def ds_fused_add_mul_to_f64(x, y):
+    """(x + y) * y -> f64 [N]."""
+    return ffi_call("ds_fused_add_mul_to_f64", _sds(x.shape, F64))(x, y)
+
+
+def ds_fused_axpy(x, y):
+    """(x + y) * y -> f64 (the reference op of this name computes this chain)."""
+    return ffi_call("ds_fused_axpy", _sds(x.shape, F64))(x, y)
+
+
+def ds_fused_add_mul_to_f64_cuda(x, y):
+    return ffi_call("ds_fused_add_mul_to_f64_cuda", _sds(x.shape, F64))(x, y)
+
+
+def ds_fused_add_sub_to_f64_cuda(x, y):
+    """(x + y) - x -> f64."""
+    return ffi_call("ds_fused_add_sub_to_f64_cuda", _sds(x.shape, F64))(x, y)
+
+
+def ds_recurrence_add_mul_to_f64_cuda(x, y, k: int):
+    """z = x; k times z = (z + y) * y."""
+    return ffi_call("ds_recurrence_add_mul_to_f64_cuda", _sds(x.shape, F64))(x, y, k=int(k))
+
+
+def ds_fused_add_mul3_to_f64(a, b, c):
+    """(a + b) * c -> f64."""
+    return ffi_call("ds_fused_add_mul3_to_f64", _sds(a.shape, F64))(a, b, c)
+
+
+def ds_recurrence_mul_add_to_f64(x, a, b, k: int):
+    """x <- x * a + b, k times."""
+    return ffi_call("ds_recurrence_mul_add_to_f64", _sds(x.shape, F64))(x, a, b, k=int(k))
+
+
+# ---- reduce ---------------------------------------------------------------------
+
+def _reduce_dims(rank: int, dimensions: Optional[Iterable[int]]):
+    if dimensions is None:
+        return tuple(range(rank))
+    dims = sorted(int(d) % rank if rank else int(d) for d in dimensions)
+    return tuple(dims)
+
+
+def _out_shape(shape, dims):
+    return tuple(s for i, s in enumerate(shape) if i not in dims)
+
+
+def ds_reduce(hi: torch.Tensor, lo: torch.Tensor, init=(0.0, 0.0),
+              dimensions: Optional[Sequence[int]] = None, body: str = "add"):
+    """DS reduce of SoA (hi, lo) over `dimensions` (default: all) -> (hi, lo)."""
+    dims = _reduce_dims(hi.dim(), dimensions)
+    ih = torch.tensor(float(init[0]), dtype=F32, device=hi.device)
+    il = torch.tensor(float(init[1]), dtype=F32, device=hi.device)
+    out = _sds(_out_shape(hi.shape, dims), F32)
+    return ffi_call("ds_reduce", (out, out))(hi, lo, ih, il, dimensions=dims,
+                                             body=_BODIES[body])
+
+
+def ds_reduce_f64(x: torch.Tensor, init: float = 0.0,
+                  dimensions: Optional[Sequence[int]] = None, body: str = "add"):
+    """DS reduce of an f64 tensor (split on load, recombined on store)."""
+    dims = _reduce_dims(x.dim(), dimensions)
+    it = torch.tensor(float(init), dtype=F64, device=x.device)
+    return ffi_call("ds_reduce_f64", _sds(_out_shape(x.shape, dims), F64))(
+        x, it, dimensions=dims, body=_BODIES[body])
+
+
+def ds_sum_f64(x: torch.Tensor, dimensions=None) -> torch.Tensor:
+    return ds_reduce_f64(x, 0.0, dimensions, "add")
+
+
+# ---- dot_general -------------------------------------------------------------------
+
+def _dot_out_shape(ls, rs, lb, lc, rc):
+    nb = len(lb)
+    out = list(ls[:nb])
+    out += [d for i, d in enumerate(ls) if i >= nb and i != lc]
+    out += [d for i, d in enumerate(rs) if i >= nb and i != rc]
+    return tuple(out)
+
+
+def ds_dot_general(lhs_hi, lhs_lo, rhs_hi, rhs_lo, lhs_contracting=None, rhs_contracting=None,
+                   lhs_batch=(), rhs_batch=(), algorithm: str = "tensor"):
+    """DS dot_general on SoA operands -> (hi, lo).  Defaults: A[..., M, K] @ B[..., K, N]."""
+    nb = len(lhs_batch)
+    lc = lhs_hi.dim() - 1 if lhs_contracting is None else int(lhs_contracting)
+    rc = nb if rhs_contracting is None else int(rhs_contracting)
+    out = _sds(_dot_out_shape(lhs_hi.shape, rhs_hi.shape, lhs_batch, lc, rc), F32)
+    return ffi_call("ds_dot_general", (out, out))(
+        lhs_hi, lhs_lo, rhs_hi, rhs_lo, lhs_batching_dimensions=tuple(lhs_batch),
+        rhs_batching_dimensions=tuple(rhs_batch), lhs_contracting_dimensions=(lc,),
+        rhs_contracting_dimensions=(rc,), algorithm=_ALGOS[algorithm])
+
+
+def ds_dot_general_f64(lhs, rhs, lhs_contracting=None, rhs_contracting=None, lhs_batch=(),
+                       rhs_batch=(), algorithm: str = "tensor"):
+    """DS dot_general of f64 operands (split and recombine fused) -> f64."""
+    nb = len(lhs_batch)
+    lc = lhs.dim() - 1 if lhs_contracting is None else int(lhs_contracting)
+    rc = nb if rhs_contracting is None else int(rhs_contracting)
+    out = _sds(_dot_out_shape(lhs.shape, rhs.shape, lhs_batch, lc, rc), F64)
+    return ffi_call("ds_dot_general_f64", out)(
+        lhs, rhs, lhs_batching_dimensions=tuple(lhs_batch),
+        rhs_batching_dimensions=tuple(rhs_batch), lhs_contracting_dimensions=(lc,),
+        rhs_contracting_dimensions=(rc,), algorithm=_ALGOS[algorithm])
+
+
+def ds_matmul_f64(A, B, algorithm: str = "tensor"):
+    """A[M, K] @ B[K, N] in DS arithmetic, f64 in and out."""
+    return ds_dot_general_f64(A, B, algorithm=algorithm)

@@ -1,0 +1,228 @@
+/*
+ * ds_b200.h -- C ABI of the B200 (sm_100a) double-single (DS) operator library
+ * (libds_b200.so).
+ *
+ * A DS value is a pair of float32 (hi, lo) whose exact sum carries about 48
+ * significant bits.  Packed DS tensors have a trailing dimension of 2 with hi
+ * at even and lo at odd offsets; SoA DS tensors are two f32 tensors of the
+ * same shape.
+ *
+ * Each entry point replaces one XLA-FFI custom-call target of the reference
+ * (rcast915/ds-experiment) and keeps its operands, attribute, result and
+ * shape checks; the citation above each declaration names the handler it
+ * replaces.  Differences from the reference, all deliberate:
+ *   - every op runs as sm_100a CUDA on the caller's stream (the reference's
+ *     CPU handlers loop on the host; its three CUDA handlers launch on the
+ *     legacy default stream and call cudaDeviceSynchronize).  No entry point
+ *     synchronises; results are ready when the stream reaches them.
+ *   - buffers are described by ds_buffer (device pointer + dims), which is
+ *     what an XLA-FFI adapter gets from ffi::Buffer::untyped_data() and
+ *     dimensions(); no XLA or torch type appears here.
+ *   - ds_reduce and ds_dot_general are new targets for the DS pass's reduce
+ *     and dot_general rewrites; they take caller-provided workspace (XLA's
+ *     scratch allocator in an FFI adapter), sized by the *_workspace_size
+ *     queries.
+ *
+ * Return value: a ds_status.  Codes follow xla::ffi::ErrorCode (absl
+ * numbering): DS_INVALID_ARGUMENT for the reference's shape errors (same
+ * messages), DS_INTERNAL for CUDA errors (message = cudaGetErrorString).
+ * ds_last_error() returns the calling thread's last message.
+ */
+#ifndef DS_B200_H_
+#define DS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DS_API __attribute__((visibility("default")))
+#else
+#define DS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  DS_OK = 0,
+  DS_INVALID_ARGUMENT = 3, /* xla::ffi::ErrorCode::kInvalidArgument */
+  DS_INTERNAL = 13         /* xla::ffi::ErrorCode::kInternal */
+};
+
+/* A device tensor: data + dims[rank] (row-major, contiguous). */
+typedef struct ds_buffer {
+  void* data;
+  const int64_t* dims;
+  int64_t rank;
+} ds_buffer;
+
+/* Reduction bodies the DS pass rewrites (DsTransformPass.cpp:392-395). */
+enum { DS_BODY_ADD = 0, DS_BODY_SUB = 1, DS_BODY_MUL = 2 };
+
+/* dot_general algorithms. */
+enum {
+  /* exact integer-residue (Ozaki scheme II) GEMM on the int8 tcgen05 tensor
+     cores; the default */
+  DS_DOT_TENSOR_INT8 = 0,
+  /* CUDA-core GEMM: exact f32 products (two_prod) summed in DS arithmetic */
+  DS_DOT_CUDA_CORE = 1
+};
+
+/* dot_general dimension numbers (stablehlo.dot_general).  One contracting
+   dimension per operand; batch dimensions must be the leading ones, in order. */
+typedef struct ds_dot_dims {
+  int64_t n_batch;
+  int64_t lhs_batch[4];
+  int64_t rhs_batch[4];
+  int64_t lhs_contracting;
+  int64_t rhs_contracting;
+} ds_dot_dims;
+
+/* Message of the calling thread's last failing call ("" if none). */
+DS_API const char* ds_last_error(void);
+
+/* Library version string. */
+DS_API const char* ds_version(void);
+
+/* ---- split / recombine -------------------------------------------------- */
+
+/* DsFromF64, cpp/ds_from_f64.cpp:91-122: x f64[...] -> y f32[..., 2],
+   hi = f32(x), lo = f32(x - f64(hi)). */
+DS_API int ds_from_f64(const ds_buffer* x, const ds_buffer* y, void* stream);
+
+/* DsToF64, cpp/ds_to_f64.cpp:139-169: x f32[..., 2] -> y f64[...],
+   y = f64(hi) + f64(lo). */
+DS_API int ds_to_f64(const ds_buffer* x, const ds_buffer* y, void* stream);
+
+/* ds_from_f32 ("Host" target, cpp/ds_from_f32.cpp:185-210): x f32[...] ->
+   y f32[..., 2] = (x, 0). */
+DS_API int ds_from_f32(const ds_buffer* x, const ds_buffer* y, void* stream);
+
+/* ds_to_f32 ("Host" target, cpp/ds_to_f32.cpp:226-249): x f32[..., 2] ->
+   y f32[...] = hi + lo (an f32 add). */
+DS_API int ds_to_f32(const ds_buffer* x, const ds_buffer* y, void* stream);
+
+/* ---- packed elementwise ------------------------------------------------- */
+
+/* DsAdd, cpp/ds_add.cpp:23-73: a, b, y f32[..., 2]. */
+DS_API int ds_add(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y,
+           void* stream);
+
+/* DsSub, cpp/ds_sub.cpp:23-73. */
+DS_API int ds_sub(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y,
+           void* stream);
+
+/* DsMul, cpp/ds_mul.cpp:38-86 (Dekker two_prod with the 4097 split). */
+DS_API int ds_mul(const ds_buffer* a, const ds_buffer* b, const ds_buffer* y,
+           void* stream);
+
+/* ---- fused f64 chains (rank-1 inputs of equal length) ------------------- */
+
+/* DsFusedAddMul, cpp/ds_fused_add_mul.cpp:66-112: (x + y) * y,
+   x, y f64[N] -> out f32[N, 2]. */
+DS_API int ds_fused_add_mul(const ds_buffer* x, const ds_buffer* y,
+                     const ds_buffer* out, void* stream);
+
+/* DsFusedAddMulToF64, cpp/ds_fused_add_mul_to_f64.cpp:70-116: (x + y) * y,
+   out f64[N]. */
+DS_API int ds_fused_add_mul_to_f64(const ds_buffer* x, const ds_buffer* y,
+                            const ds_buffer* out, void* stream);
+
+/* DsFusedAxpy, cpp/ds_fused_axpy.cpp:75-120 (computes (x + y) * y, as the
+   reference does; not built by the reference's CMakeLists). */
+DS_API int ds_fused_axpy(const ds_buffer* x, const ds_buffer* y, const ds_buffer* out,
+                  void* stream);
+
+/* DsFusedAddMulToF64Cuda, cpp/ds_fused_add_mul_to_f64_cuda.cu:88-132. */
+DS_API int ds_fused_add_mul_to_f64_cuda(const ds_buffer* x, const ds_buffer* y,
+                                 const ds_buffer* out, void* stream);
+
+/* DsFusedAddSubToF64Cuda, cpp/ds_fused_add_sub_to_f64_cuda.cu:52-121:
+   (x + y) - x. */
+DS_API int ds_fused_add_sub_to_f64_cuda(const ds_buffer* x, const ds_buffer* y,
+                                 const ds_buffer* out, void* stream);
+
+/* DsRecurrenceAddMulToF64Cuda, cpp/ds_recurrence_add_mul_to_f64_cuda.cu:
+   98-149: z = split(x); k times z = (z + y) * y; out = f64(z).
+   k < 0 -> DS_INVALID_ARGUMENT ("k must be nonnegative"). */
+DS_API int ds_recurrence_add_mul_to_f64_cuda(const ds_buffer* x, const ds_buffer* y,
+                                      int32_t k, const ds_buffer* out,
+                                      void* stream);
+
+/* Three-input (a + b) * c: DsFusedAddMulToF64 (cpp/ds_fused_add_mul_to_f64.
+   cpp:81-93) with the multiplier split from its own input. */
+DS_API int ds_fused_add_mul3_to_f64(const ds_buffer* a, const ds_buffer* b,
+                             const ds_buffer* c, const ds_buffer* out,
+                             void* stream);
+
+/* x <- x * a + b, k times (ds_add(ds_mul(X, A), B)), the recurrence kernel
+   (cpp/ds_recurrence_add_mul_to_f64_cuda.cu:69-93) with a multiply-add
+   body. */
+DS_API int ds_recurrence_mul_add_to_f64(const ds_buffer* x, const ds_buffer* a,
+                                 const ds_buffer* b, int32_t k,
+                                 const ds_buffer* out, void* stream);
+
+/* ---- reduce (DsTransformPass.cpp:376-448) -------------------------------- */
+
+/* DS reduce of SoA input (in_hi, in_lo f32[...]) over `dimensions` (which
+   must be contiguous and ascending) with init (init_hi, init_lo: f32 rank-0
+   device scalars) and body DS_BODY_*.  Outputs out_hi, out_lo have the input
+   shape without the reduced dimensions.  The body is the pass's: acc =
+   ds_op(acc, elem).  Elements are folded per thread in index order, then in
+   a fixed shuffle/block tree, then block partials in block order, so results
+   are deterministic for a given shape; init is applied once, last
+   (subtract: init - sum; add: init + sum; multiply: init * product). */
+DS_API size_t ds_reduce_workspace_size(const ds_buffer* in, const int64_t* dimensions,
+                                int64_t n_dimensions);
+DS_API int ds_reduce(const ds_buffer* in_hi, const ds_buffer* in_lo,
+              const ds_buffer* init_hi, const ds_buffer* init_lo,
+              const int64_t* dimensions, int64_t n_dimensions, int32_t body,
+              const ds_buffer* out_hi, const ds_buffer* out_lo,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same with the pass's entry split and exit recombine fused: f64 input,
+   f64 rank-0 init, f64 output (jnp.sum of an f64 array under the pass). */
+DS_API int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init,
+                  const int64_t* dimensions, int64_t n_dimensions, int32_t body,
+                  const ds_buffer* out, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* ---- dot_general (DsTransformPass.cpp:337-370) --------------------------- */
+
+/* DS dot_general of SoA operands (lhs_hi, lhs_lo), (rhs_hi, rhs_lo) f32 with
+   stablehlo dimension numbers; result (out_hi, out_lo) f32 of shape
+   [batch..., lhs free, rhs free].  The reference lowers this to four f32
+   dots (f32 accumulation) and a two_sum; here the product is computed from
+   the exact DS values (see algorithm). */
+DS_API size_t ds_dot_general_workspace_size(const ds_buffer* lhs, const ds_buffer* rhs,
+                                     const ds_dot_dims* dims, int32_t algorithm);
+DS_API int ds_dot_general(const ds_buffer* lhs_hi, const ds_buffer* lhs_lo,
+                   const ds_buffer* rhs_hi, const ds_buffer* rhs_lo,
+                   const ds_dot_dims* dims, int32_t algorithm,
+                   const ds_buffer* out_hi, const ds_buffer* out_lo,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same with split and recombine fused: f64 operands, f64 result (the
+   pass on f64 arguments: emitFromFloat -> dot_general -> emitToFloat). */
+DS_API int ds_dot_general_f64(const ds_buffer* lhs, const ds_buffer* rhs,
+                       const ds_dot_dims* dims, int32_t algorithm,
+                       const ds_buffer* out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---- diagnostics (no reference counterpart) ------------------------------ */
+
+/* Per-kernel GPU time.  While enabled, each op brackets its main kernel with
+   CUDA events on the launch stream under a family name ("elementwise",
+   "recurrence", "reduce", "dot_simt", "dot_vec", "ozaki_split",
+   "ozaki_gemm", "ozaki_crt").  ds_profile_read waits for the recorded
+   events and returns the summed milliseconds and the launch count. */
+DS_API void ds_profile_enable(int on);
+DS_API void ds_profile_reset(void);
+DS_API int ds_profile_read(const char* name, double* total_ms, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DS_B200_H_ */

@@ -1,0 +1,171 @@
+"""The C ABI without a GPU: symbols, signatures and the reference's shape errors.
+
+Every shape check runs before any CUDA call, so invalid calls return
+DS_INVALID_ARGUMENT with the reference handler's message on a CPU-only host.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "ds_b200.h")
+
+
+@pytest.fixture(scope="module")
+def L():
+    import importlib
+    build = importlib.import_module("build")  # ds-experiment_b200/build.py
+    build.build()
+    from ds_b200 import _lib
+    return _lib
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"DS_API\s+[\w\s\*]+?\b(ds_\w+)\s*\(", text)))
+
+
+def test_header_symbols_exported(L):
+    syms = header_symbols()
+    assert len(syms) >= 20
+    cdll = ctypes.CDLL(L.LIB_PATH)
+    for s in syms:
+        assert hasattr(cdll, s), f"{s} declared in ds_b200.h but not exported"
+    # the Python binding declares a signature for every header entry point
+    assert set(syms) == set(L.SIGNATURES), set(syms) ^ set(L.SIGNATURES)
+
+
+def test_library_loads_and_reports_version(L):
+    assert b"sm_100a" in L.lib().ds_version()
+
+
+def _b(L, shape, ptr=0x1000):
+    return L.make_buffer(ptr, shape)
+
+
+def _call_err(L, name, *args):
+    fn = getattr(L.lib(), name)
+    st = fn(*args)
+    return st, L.last_error()
+
+
+def test_packed_shape_errors(L):
+    a, _ka = _b(L, (4, 2))
+    b3, _kb = _b(L, (4, 3))
+    y, _ky = _b(L, (4, 2))
+    y5, _ky5 = _b(L, (5, 2))
+    a3d, _k3 = _b(L, (2, 2, 2))
+    r = ctypes.byref
+    for name, op in (("ds_add", "ds.add"), ("ds_sub", "ds.sub"), ("ds_mul", "ds.mul")):
+        st, msg = _call_err(L, name, r(a), r(b3), r(y), None)
+        assert st == L.DS_INVALID_ARGUMENT and msg == f"{op} expects last dim == 2"
+        st, msg = _call_err(L, name, r(a), r(a3d), r(y), None)
+        assert st == L.DS_INVALID_ARGUMENT and msg == f"{op} input shapes must match"
+        st, msg = _call_err(L, name, r(a), r(a), r(y5), None)
+        assert st == L.DS_INVALID_ARGUMENT and msg == f"{op} output shape mismatch"
+
+
+def test_split_recombine_shape_errors(L):
+    r = ctypes.byref
+    x, _k1 = _b(L, (8,))
+    y_bad, _k2 = _b(L, (8, 3))
+    y_mis, _k3 = _b(L, (7, 2))
+    st, msg = _call_err(L, "ds_from_f64", r(x), r(y_bad), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_from_f64 output last dim must be 2")
+    st, msg = _call_err(L, "ds_from_f64", r(x), r(y_mis), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_from_f64 shape mismatch")
+    p, _k4 = _b(L, (8, 3))
+    st, msg = _call_err(L, "ds_to_f64", r(p), r(x), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_to_f64 input last dim must be 2")
+    p2, _k5 = _b(L, (8, 2))
+    o7, _k6 = _b(L, (7,))
+    st, msg = _call_err(L, "ds_to_f64", r(p2), r(o7), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_to_f64 shape mismatch")
+    st, msg = _call_err(L, "ds_from_f32", r(x), r(y_mis), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_from_f32 shape mismatch")
+    st, msg = _call_err(L, "ds_to_f32", r(p2), r(o7), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_to_f32 shape mismatch")
+
+
+def test_fused_shape_errors(L):
+    r = ctypes.byref
+    x, _1 = _b(L, (8,))
+    y7, _2 = _b(L, (7,))
+    m, _3 = _b(L, (2, 4))
+    o8, _4 = _b(L, (8,))
+    o82, _5 = _b(L, (8, 2))
+    st, msg = _call_err(L, "ds_fused_add_mul_to_f64_cuda", r(m), r(x), r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_fused_add_mul_to_f64_cuda expects rank-1 inputs")
+    st, msg = _call_err(L, "ds_fused_add_sub_to_f64_cuda", r(x), r(y7), r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "input lengths must match")
+    st, msg = _call_err(L, "ds_fused_add_mul_to_f64", r(x), r(x), r(o82), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "output shape must be [N]")
+    st, msg = _call_err(L, "ds_fused_add_mul", r(x), r(x), r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "output shape must be [N,2]")
+    st, msg = _call_err(L, "ds_fused_axpy", r(m), r(x), r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "ds_fused_axpy expects rank-1 inputs")
+    # k < 0 (cpp/ds_recurrence_add_mul_to_f64_cuda.cu:115-117)
+    st, msg = _call_err(L, "ds_recurrence_add_mul_to_f64_cuda", r(x), r(x), -1, r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "k must be nonnegative")
+    st, msg = _call_err(L, "ds_recurrence_mul_add_to_f64", r(x), r(x), r(x), -3, r(o8), None)
+    assert (st, msg) == (L.DS_INVALID_ARGUMENT, "k must be nonnegative")
+
+
+def test_null_pointer_rejected(L):
+    r = ctypes.byref
+    x, _1 = _b(L, (8,), ptr=0)
+    y, _2 = _b(L, (8, 2))
+    st, msg = _call_err(L, "ds_from_f64", r(x), r(y), None)
+    assert st == L.DS_INVALID_ARGUMENT and "null" in msg
+
+
+def test_reduce_and_dot_shape_errors(L):
+    r = ctypes.byref
+    x, _1 = _b(L, (4, 5, 6))
+    init, _2 = _b(L, ())
+    out, _3 = _b(L, (4, 6))
+    dims = (ctypes.c_int64 * 2)(0, 2)  # not contiguous
+    st, msg = _call_err(L, "ds_reduce_f64", r(x), r(init), dims, 2, 0, r(out), None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "contiguous" in msg
+    d1 = (ctypes.c_int64 * 1)(1)
+    bad, _4 = _b(L, (4, 5))
+    st, msg = _call_err(L, "ds_reduce_f64", r(x), r(init), d1, 1, 0, r(bad), None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "output shape" in msg
+    st, msg = _call_err(L, "ds_reduce_f64", r(x), r(init), d1, 1, 7, r(out), None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "body" in msg
+    # dot_general: contracting sizes differ
+    A, _5 = _b(L, (8, 16))
+    B, _6 = _b(L, (15, 4))
+    C, _7 = _b(L, (8, 4))
+    dd = L.make_dot_dims(0, 1, 0)
+    st, msg = _call_err(L, "ds_dot_general_f64", r(A), r(B), r(dd), 0, r(C), None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "contracting" in msg
+    B2, _8 = _b(L, (16, 4))
+    C2, _9 = _b(L, (8, 5))
+    st, msg = _call_err(L, "ds_dot_general_f64", r(A), r(B2), r(dd), 0, r(C2), None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "output shape" in msg
+    st, msg = _call_err(L, "ds_dot_general_f64", r(A), r(B2), r(dd), 9, r(_b(L, (8, 4))[0]),
+                        None, 0, None)
+    assert st == L.DS_INVALID_ARGUMENT and "algorithm" in msg
+
+
+def test_ffi_surface_registry():
+    from ds_b200 import ffi
+    names = ffi.registered_targets()
+    for t in ("ds_add", "ds_sub", "ds_mul", "ds_from_f64", "ds_to_f64", "ds_from_f32",
+              "ds_to_f32", "ds_fused_add_mul", "ds_fused_add_mul_to_f64", "ds_fused_axpy",
+              "ds_fused_add_mul_to_f64_cuda", "ds_fused_add_sub_to_f64_cuda",
+              "ds_recurrence_add_mul_to_f64_cuda", "ds_reduce", "ds_dot_general"):
+        assert t in names
+    with pytest.raises(ValueError):
+        ffi.register_ffi_target("ds_add", "ds_add", platform="cpu")
+
+
+def test_cpu_tensor_rejected():
+    import torch
+    from ds_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.ds_from_f64(torch.zeros(4, dtype=torch.float64))

@@ -1,0 +1,165 @@
+"""DS dot_general on the GPU against exact sampled truth and the reference path.
+
+The reference lowers dot_general to four f32 dots with f32 accumulation and a
+two_sum (DsTransformPass.cpp:337-370); oracle/ds_pass_ref.py restates it.  No
+reference test pins GEMM bits, so parity is error: on every case the GPU
+result's error against the exact product (oracle/exact.py) must be no worse
+than the reference path's, and within a DS-level bound of sum_k |a_ik b_kj|.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from gpu_util import cu, host
+from oracle import ds_pass_ref, exact
+
+pytestmark = pytest.mark.gpu
+
+ALGOS = ["tensor", "cuda_core"]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from ds_b200 import ops as _ops
+    return _ops
+
+
+def ds_of(x):
+    """The exact value of the DS split of x (hi + lo)."""
+    hi = x.astype(np.float32)
+    lo = (x - hi.astype(np.float64)).astype(np.float32)
+    return hi.astype(np.float64) + lo.astype(np.float64)
+
+
+def check_gemm(got, A, B, samples=512, tol_bits=44, ref=None):
+    """Sampled-exact error check of C = A @ B (float64 A, B)."""
+    M, N = got.shape
+    rows, cols = exact.sample_indices(M, N, samples)
+    truth = exact.exact_gemm_entries(A, B, rows, cols)
+    mag = np.array([np.dot(np.abs(A[r]), np.abs(B[:, c])) for r, c in zip(rows, cols)])
+    err = np.abs(got[rows, cols] - truth)
+    assert np.all(err <= 2.0 ** -tol_bits * mag + 1e-300), (err / mag).max()
+    if ref is not None:
+        ref_err = np.abs(ref[rows, cols] - truth)
+        assert err.max() <= ref_err.max(), (err.max(), ref_err.max())
+    return err.max(), (err / np.maximum(mag, 1e-300)).max()
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("M,N,K", [(1, 7, 5), (5, 1, 9), (33, 17, 65), (128, 256, 128),
+                                   (200, 300, 500), (256, 512, 1024)])
+def test_gemm_shapes(ops, algo, M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rng.uniform(-1, 1, (M, K))
+    B = rng.uniform(-1, 1, (K, N))
+    got = host(ops.ds_matmul_f64(cu(A), cu(B), algorithm=algo))
+    ref = ds_pass_ref.dot_general_f64(A, B)
+    check_gemm(got, A, B, ref=ref)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_config3_slice(ops, algo):
+    """512 x 512 x 4096 slice of the 4096^3 config (A, B ~ U[-1,1], seed 2)."""
+    rng = np.random.default_rng(2)
+    A = rng.uniform(-1, 1, (512, 4096))
+    B = rng.uniform(-1, 1, (4096, 512))
+    got = host(ops.ds_matmul_f64(cu(A), cu(B), algorithm=algo))
+    ref = ds_pass_ref.dot_general_f64(A, B)
+    check_gemm(got, A, B, samples=256, ref=ref)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_f32_inputs_soa(ops, algo):
+    """f32 inputs enter as (v, 0) (emitFromFloat, DsTransformPass.cpp:174-179)."""
+    import torch
+    rng = np.random.default_rng(3)
+    A = rng.standard_normal((96, 160)).astype(np.float32)
+    B = rng.standard_normal((160, 80)).astype(np.float32)
+    z = lambda a: torch.zeros(a.shape, dtype=torch.float32, device="cuda")
+    hi, lo = ops.ds_dot_general(cu(A), z(A), cu(B), z(B), algorithm=algo)
+    got = host(hi).astype(np.float64) + host(lo).astype(np.float64)
+    A64, B64 = A.astype(np.float64), B.astype(np.float64)
+    ref = ds_pass_ref.dot_general_f64(A, B)
+    check_gemm(got, A64, B64, samples=300, ref=ref)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_transposed_and_batched_layouts(ops, algo):
+    rng = np.random.default_rng(4)
+    At = rng.uniform(-1, 1, (70, 40))   # [K, M]
+    Bt = rng.uniform(-1, 1, (50, 70))   # [N, K]
+    got = host(ops.ds_dot_general_f64(cu(At), cu(Bt), lhs_contracting=0, rhs_contracting=1,
+                                      algorithm=algo))
+    check_gemm(got, At.T.copy(), Bt.T.copy(), samples=200)
+    Ab = rng.uniform(-1, 1, (3, 20, 30))
+    Bb = rng.uniform(-1, 1, (3, 30, 10))
+    got = host(ops.ds_dot_general_f64(cu(Ab), cu(Bb), lhs_contracting=2, rhs_contracting=1,
+                                      lhs_batch=(0,), rhs_batch=(0,), algorithm=algo))
+    for b in range(3):
+        check_gemm(got[b], Ab[b], Bb[b], samples=100)
+
+
+def test_batched_vector_dot(ops):
+    """dot_general with batch 0 and contracting 1 on both: config 5's batched dot
+    shape (scaled down), entries 1 + 1e-7 u (near-cancellation free sums)."""
+    rng = np.random.default_rng(4)
+    X = 1.0 + 1e-7 * rng.uniform(-1, 1, (64, 65536))
+    Y = 1.0 + 1e-7 * rng.uniform(-1, 1, (64, 65536))
+    got = host(ops.ds_dot_general_f64(cu(X), cu(Y), lhs_contracting=1, rhs_contracting=1,
+                                      lhs_batch=(0,), rhs_batch=(0,)))
+    truth = np.array([exact.exact_dot(X[i], Y[i]) for i in range(64)])
+    assert np.max(np.abs(got - truth) / truth) < 2.0 ** -44
+    # vector . vector, one long dot product
+    v = rng.uniform(-1, 1, 1 << 20)
+    w = rng.uniform(-1, 1, 1 << 20)
+    d = float(host(ops.ds_dot_general_f64(cu(v), cu(w), lhs_contracting=0, rhs_contracting=0)))
+    assert abs(d - exact.exact_dot(v, w)) < 2.0 ** -44 * np.dot(np.abs(v), np.abs(w))
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_reference_edge_cases(ops, algo):
+    """tests/test_matmul.py:67-152 and tests/test_dot_product.py:66-176 cases."""
+    import torch
+    f32 = np.float32
+
+    def mm(A, B):
+        A = np.asarray(A, np.float64)
+        B = np.asarray(B, np.float64)
+        return host(ops.ds_matmul_f64(cu(A), cu(B), algorithm=algo))
+
+    # identity: A @ I == A exactly for DS-representable A
+    rng = np.random.default_rng(42)
+    A4 = rng.standard_normal((4, 4)).astype(f32).astype(np.float64)
+    assert np.array_equal(mm(A4, np.eye(4)), A4)
+    # NaN in A row 0 -> that output row has NaN; Inf -> Inf or NaN
+    A_nan = np.array([[1.0, np.nan], [3.0, 4.0]])
+    r = mm(A_nan, np.ones((2, 2)))
+    assert np.all(np.isnan(r[0])) and np.all(np.isfinite(r[1]))
+    A_inf = np.array([[1.0, np.inf], [3.0, 4.0]])
+    r = mm(A_inf, np.ones((2, 2)))
+    assert np.all(np.isinf(r[0]) | np.isnan(r[0])) and np.array_equal(r[1], [7.0, 7.0])
+    # subnormal inputs: finite
+    r = mm(np.full((3, 4), f32(1.5e-40)), np.ones((4, 3)))
+    assert np.all(np.isfinite(r))
+    # cancellation rows (test_matmul.py:99-113, :131-148)
+    row = np.array([[1e6, -1e6 + 1, 1e6, -1e6 + 1]], f32)
+    assert mm(row, np.ones((4, 1)))[0, 0] == 2.0
+    trip = np.zeros((1, 99), f32)
+    trip[0, 0::3], trip[0, 1::3], trip[0, 2::3] = 1e6, 1.0, -1e6
+    assert mm(trip, np.ones((99, 1)))[0, 0] == 33.0
+    # zero operand
+    assert np.array_equal(mm(np.zeros((5, 6)), rng.random((6, 7))), np.zeros((5, 7)))
+
+
+def test_precision_highest_256(ops):
+    """tests/test_matmul.py:322-341: (A*A) @ B at 256^2 with f32 inputs; DS error
+    must not exceed strict-f32 error (the reference's own assertion)."""
+    rng = np.random.default_rng(7)
+    A = rng.standard_normal((256, 256)).astype(np.float32)
+    B = rng.standard_normal((256, 256)).astype(np.float32)
+    AA = (A.astype(np.float64) ** 2)
+    got = host(ops.ds_matmul_f64(cu(AA), cu(B.astype(np.float64))))
+    f64 = AA @ B.astype(np.float64)
+    f32 = (A * A) @ B
+    assert np.mean(np.abs(got - f64)) <= np.mean(np.abs(f32 - f64))

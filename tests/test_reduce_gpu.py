@@ -1,0 +1,137 @@
+"""DS reduce on the GPU against exact sums and the reference DS path.
+
+The reference's reduce is XLA's tree over the pass's DS body
+(DsTransformPass.cpp:376-448) and no reference test pins its bits, so parity
+is measured as error: the GPU result's error against math.fsum must be no
+worse than a small multiple of the reference-order (sequential) DS fold's
+error, and within a DS-precision bound of the input magnitudes.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal
+from gpu_util import cu, host
+from oracle import exact
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from ds_b200 import ops as _ops
+    return _ops
+
+
+def config2_inputs(n, seed=1):
+    """x_i = s_i*1e8 + u_i*1e-3, s alternating +-1, u ~ U[0,1) (seed 1)."""
+    s = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)
+    u = np.random.default_rng(seed).uniform(0, 1, n)
+    return s * 1e8 + u * 1e-3
+
+
+def ds_bound(x):
+    """Error budget of a DS sum: ~2^-46 of the largest partial magnitude per
+    level of a log-depth tree plus the per-thread folds."""
+    ax = np.abs(np.asarray(x, np.float64))
+    return 2.0 ** -46 * (ax.max() * math.log2(max(ax.size, 2)) * 64 + 1e-300)
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 1000, 10_000, 65_537, 1 << 20])
+def test_config2_sum_error(ops, dso, n):
+    x = config2_inputs(n)
+    truth = exact.exact_sum(x)
+    got = float(host(ops.ds_sum_f64(cu(x))))
+    h, l = dso.ds_reduce_f64_seq(x)
+    ref = float(h) + float(l)
+    f32 = float(np.sum(x.astype(np.float32), dtype=np.float32))
+    err, ref_err, f32_err = abs(got - truth), abs(ref - truth), abs(f32 - truth)
+    assert err <= max(4 * ref_err, ds_bound(x)), (err, ref_err)
+    if n >= 1000:
+        assert err < f32_err / 1000, (err, f32_err)
+
+
+def test_sum_of_tenths(ops):
+    """README.md:199-201: 10,000 x 0.1 (f64 in); the reference DS error is 1.49e-05."""
+    x = np.full(10_000, 0.1)
+    got = float(host(ops.ds_sum_f64(cu(x))))
+    assert abs(got - exact.exact_sum(x)) < 1e-10
+
+
+def test_triplet_cancellation(ops):
+    """handoff.md:191-193: (1e8, 1, -1e8) triplets, n=3333 -> DS error 0."""
+    x = np.zeros(3 * 3333)
+    x[0::3], x[1::3], x[2::3] = 1e8, 1.0, -1e8
+    assert float(host(ops.ds_sum_f64(cu(x)))) == 3333.0
+
+
+def test_soa_matches_f64_entry(ops, dso):
+    """ds_reduce on split inputs gives the same bits as the fused f64 entry."""
+    x = config2_inputs(100_003, seed=3)
+    sp = dso.ds_from_f64(x)
+    hi, lo = ops.ds_reduce(cu(np.ascontiguousarray(sp[:, 0])), cu(np.ascontiguousarray(sp[:, 1])))
+    got = float(np.float64(host(hi))) + float(np.float64(host(lo)))
+    assert got == float(host(ops.ds_sum_f64(cu(x))))
+
+
+def test_deterministic(ops):
+    x = cu(config2_inputs(1 << 22, seed=9))
+    a = host(ops.ds_sum_f64(x))
+    for _ in range(3):
+        assert_bits_equal(host(ops.ds_sum_f64(x)), a, "repeat")
+
+
+def test_empty_returns_init(ops):
+    import torch
+    x = torch.zeros(0, dtype=torch.float64, device="cuda")
+    assert float(host(ops.ds_reduce_f64(x, init=2.5))) == 2.5
+    assert float(host(ops.ds_reduce_f64(x, init=-0.0))) == 0.0
+
+
+def test_init_and_bodies(ops, dso):
+    rng = np.random.default_rng(11)
+    x = rng.uniform(-1, 1, 50_001)
+    got = float(host(ops.ds_reduce_f64(cu(x), init=3.0)))
+    assert abs(got - (3.0 + exact.exact_sum(x))) < 1e-11
+    got = float(host(ops.ds_reduce_f64(cu(x), init=3.0, body="sub")))
+    assert abs(got - (3.0 - exact.exact_sum(x))) < 1e-11
+    y = 1.0 + 1e-7 * rng.uniform(-1, 1, 20_000)
+    got = float(host(ops.ds_reduce_f64(cu(y), init=1.0, body="mul")))
+    h, l = dso.ds_reduce_f64_seq(y, body="mul", init=(1.0, 0.0))
+    want = float(h) + float(l)
+    assert abs(got - want) / abs(want) < 1e-12
+
+
+def test_nan_inf_propagate(ops):
+    x = np.arange(1000, dtype=np.float64)
+    x[17] = np.nan
+    assert math.isnan(float(host(ops.ds_sum_f64(cu(x)))))
+    x[17] = np.inf
+    r = float(host(ops.ds_sum_f64(cu(x))))
+    assert math.isinf(r) or math.isnan(r)
+
+
+@pytest.mark.parametrize("shape,dims", [((37, 1000), (1,)), ((1000, 37), (0,)),
+                                        ((6, 50, 7), (1,)), ((4, 3, 500), (1, 2)),
+                                        ((300, 2), (0, 1))])
+def test_segmented(ops, shape, dims):
+    rng = np.random.default_rng(sum(shape))
+    x = rng.uniform(-1, 1, shape) * 1e6 + rng.uniform(0, 1, shape) * 1e-6
+    got = host(ops.ds_reduce_f64(cu(x), dimensions=dims))
+    moved = np.moveaxis(x, dims, list(range(x.ndim - len(dims), x.ndim)))
+    flat = moved.reshape(-1, int(np.prod([shape[d] for d in dims])))
+    want = np.array([exact.exact_sum(r) for r in flat]).reshape(got.shape)
+    assert np.max(np.abs(got - want)) < 1e6 * 2.0 ** -40
+
+
+@pytest.mark.slow
+def test_config2_large_property(ops, dso):
+    """N = 2^26 (512 MiB): error vs math.fsum against the sequential DS fold."""
+    n = 1 << 26
+    x = config2_inputs(n)
+    got = float(host(ops.ds_sum_f64(cu(x))))
+    truth = exact.exact_sum(x)
+    h, l = dso.ds_reduce_f64_seq(x)
+    ref_err = abs(float(h) + float(l) - truth)
+    assert abs(got - truth) <= max(4 * ref_err, ds_bound(x))
