@@ -239,8 +239,7 @@ def run_ours(args):
             launches[f] = {"launches": n, "ms_total": round(t, 4)}
     peaks, peak_src = measured_peaks()
     if k_n:
-        from ds_b200 import gemm_info
-        info = gemm_info(GEMM_DIM, GEMM_DIM, GEMM_DIM)
+        info = _lib.gemm_info(GEMM_DIM, GEMM_DIM, GEMM_DIM)
         per_launch_ms = k_ms / k_n
         ops_per_launch = info["tensor_ops_per_launch"]
         achieved = ops_per_launch / (per_launch_ms * 1e-3) / 1e12

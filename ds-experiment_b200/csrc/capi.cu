@@ -250,6 +250,15 @@ const char* ds_last_error(void) { return g_last_error.c_str(); }
 
 const char* ds_version(void) { return "ds_b200 0.1 (sm_100a)"; }
 
+int ds_dot_tensor_plan(int64_t K, int32_t* moduli, int32_t* bits) {
+  if (K < 1) return invalid("ds_dot_tensor_plan: K must be positive");
+  int m = 0, b = 0;
+  dot_ozaki_params(K, &m, &b);
+  if (moduli) *moduli = m;
+  if (bits) *bits = b;
+  return DS_OK;
+}
+
 int ds_from_f64(const ds_buffer* x, const ds_buffer* y, void* stream) {
   if (int st = check_buffers({x, y}, "ds_from_f64")) return st;
   if (y->rank == 0 || last_dim(y) != 2) return invalid("ds_from_f64 output last dim must be 2");
@@ -416,6 +425,27 @@ int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dim
   a.in_f64 = f64p(in);
   a.init_f64 = f64p(init);
   a.out_f64 = static_cast<double*>(out->data);
+  a.body = body;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return reduce_launch(a, as_stream(stream));
+}
+
+int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dimensions,
+                       int64_t n_dimensions, int32_t body, const ds_buffer* out_hi,
+                       const ds_buffer* out_lo, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (int st = check_buffers({in, init, out_hi, out_lo}, "ds_reduce_from_f64")) return st;
+  if (total(init) != 1) return invalid("ds_reduce_from_f64: init value must be a scalar");
+  if (out_hi->rank != out_lo->rank || total(out_hi) != total(out_lo))
+    return invalid("ds_reduce_from_f64: hi and lo outputs must have the same shape");
+  ReduceArgs a;
+  if (int st = reduce_common("ds_reduce_from_f64", in, dimensions, n_dimensions, body, out_hi, a))
+    return st;
+  a.in_f64 = f64p(in);
+  a.init_f64 = f64p(init);
+  a.out_hi = static_cast<float*>(out_hi->data);
+  a.out_lo = static_cast<float*>(out_lo->data);
   a.body = body;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;

@@ -1,17 +1,862 @@
-// Tensor-core DS dot_general (int8 tcgen05, Ozaki scheme II).  Placeholder
-// until the kernel lands: reports itself unsupported so dot_general takes
-// the CUDA-core path.
+// Tensor-core DS dot_general: exact integer-residue GEMM (Ozaki scheme II)
+// on the int8 tcgen05 tensor cores of sm_100a.
+//
+// The DS value of every operand element (hi + lo, i.e. the f64 input after
+// the DS split) is scaled by a power of two per row of A and per column of B,
+//     a_int = rint(a * 2^sa_i),  |a_int| <= 2^P,
+// so the product of the integer matrices is an integer matrix with
+// |C_int| <= K 2^(2P).  C_int is computed exactly through its residues modulo
+// L = 14 pairwise-coprime moduli m_l <= 256 (product Mprod ~ 2^110.2):
+//   1. split:  residues (a_int mod m_l) as int8 planes [L][batch][rows][K]
+//              (K-major, rows padded to the tile, K padded to 128), plus the
+//              per-row scale exponents;
+//   2. gemm:   for every modulus, one int8 x int8 -> int32 GEMM on the
+//              tensor cores (exact: |sum| <= K * 128^2 < 2^31 for K <= 2^17);
+//              the epilogue stores (P mod m_l) as one byte;
+//   3. crt:    C_int from its L residues by the Chinese remainder theorem,
+//              evaluated exactly in three 40-bit f64 limbs, then
+//              C = C_int * 2^-(sa_i + sb_j) in f64.
+// P = min(50, floor((log2 Mprod - 2 - log2 K) / 2)) keeps |C_int| <= Mprod/4,
+// so the quotient in step 3 is exact.  For K = 4096, P = 48: every input is
+// quantised to 49 bits relative to its row (column) maximum, i.e. at least
+// the precision of the DS input itself; the products and sums add no error.
+//
+// GEMM kernel (step 2): persistent, one CTA per SM, warp-specialised.
+//   warp 0      TMA producer: 128x128 (A) and 256x128 (B) int8 tiles, 128B
+//               swizzle, 4-stage mbarrier ring (48 KB per stage);
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::i8 M=128 N=256 K=32 (4 per
+//               stage) into one of two 256-column int32 TMEM accumulators;
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, mod m_l, byte
+//               stores; overlaps the MMAs of the next tile.
+// Work units are (modulus, batch, tile_m, tile_n), modulus outermost, so the
+// planes of one modulus (2 x 16 MB at 4096^2) stay in L2 while all CTAs use
+// them.  Every mbarrier wait is bounded (~2 s of clock64); on timeout the
+// kernel records an error code, unwinds and the CRT step writes NaN.  No TMA
+// multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
+#include "ds_arith.cuh"
 #include "kernels.h"
+#include "profile.h"
 
 namespace dsb {
+namespace {
 
-bool dot_ozaki_supported(int64_t, int64_t, int64_t) { return false; }
+constexpr int kL = 14;
+constexpr int kTileM = 128, kTileN = 256, kTileK = 128;  // int8: 128 bytes of K
+constexpr int kStages = 4;
+constexpr int kStageA = kTileM * kTileK;  // 16 KB
+constexpr int kStageB = kTileN * kTileK;  // 32 KB
+constexpr int kGemmThreads = 192;
+constexpr int kMaxK = 1 << 17;
+constexpr int kShiftNonFinite = INT_MIN;
+constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
-size_t dot_ozaki_workspace_bytes(int64_t, int64_t, int64_t, int64_t) { return 0; }
+__host__ __device__ constexpr int mod_of(int l) {
+  return l == 0 ? 256 : l == 1 ? 255 : l == 2 ? 253 : l == 3 ? 251 : l == 4 ? 247
+       : l == 5 ? 241 : l == 6 ? 239 : l == 7 ? 233 : l == 8 ? 229 : l == 9 ? 227
+       : l == 10 ? 223 : l == 11 ? 217 : l == 12 ? 211 : 199;
+}
 
-int dot_ozaki(const DotProblem&, void*, size_t, cudaStream_t) {
-  return set_error(DS_INTERNAL, "tensor-core dot_general not built");
+// ---------------------------------------------------------------------------
+// Host-side constants: P from K, and the CRT weights in 40-bit limbs.
+
+struct CrtConsts {
+  double w[kL][3];  // W_l = (Mprod/m_l) * ((Mprod/m_l)^-1 mod m_l), limbs of 40 bits
+  double mlimb[3];  // Mprod in 40-bit limbs
+  double inv_m;     // 1 / Mprod
+  double log2_m;
+};
+
+using u128 = unsigned __int128;
+
+const CrtConsts& crt_consts() {
+  static CrtConsts c;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    u128 M = 1;
+    for (int l = 0; l < kL; ++l) M *= static_cast<u128>(mod_of(l));
+    const u128 mask = (static_cast<u128>(1) << 40) - 1;
+    for (int l = 0; l < kL; ++l) {
+      const int m = mod_of(l);
+      const u128 Ml = M / m;
+      const int r = static_cast<int>(Ml % m);
+      int inv = 1;
+      while ((r * inv) % m != 1) ++inv;  // m <= 256: trivial search
+      const u128 W = Ml * static_cast<u128>(inv);  // < M
+      c.w[l][0] = static_cast<double>(static_cast<uint64_t>(W & mask));
+      c.w[l][1] = static_cast<double>(static_cast<uint64_t>((W >> 40) & mask));
+      c.w[l][2] = static_cast<double>(static_cast<uint64_t>(W >> 80));
+    }
+    c.mlimb[0] = static_cast<double>(static_cast<uint64_t>(M & mask));
+    c.mlimb[1] = static_cast<double>(static_cast<uint64_t>((M >> 40) & mask));
+    c.mlimb[2] = static_cast<double>(static_cast<uint64_t>(M >> 80));
+    const double Md = c.mlimb[2] * 0x1p80 + c.mlimb[1] * 0x1p40 + c.mlimb[0];
+    c.inv_m = 1.0 / Md;
+    c.log2_m = std::log2(Md);
+  });
+  return c;
+}
+
+int bits_for_k(int64_t K) {
+  const double lk = std::log2(static_cast<double>(K < 1 ? 1 : K));
+  int P = static_cast<int>(std::floor((crt_consts().log2_m - 2.0 - lk) / 2.0));
+  return P > 50 ? 50 : P;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+struct Layout {
+  int64_t batch, M, N, K, Mp, Np, Kp;
+  size_t off_a, off_b, off_c, off_sa, off_sb, off_err, total;
+};
+
+Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  Layout g{};
+  g.batch = batch;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.Mp = round_up(M, kTileM);
+  g.Np = round_up(N, kTileN);
+  g.Kp = round_up(K < 1 ? 1 : K, kTileK);
+  size_t off = 0;
+  auto take = [&off](size_t bytes) {
+    const size_t at = off;
+    off = static_cast<size_t>(round_up(static_cast<int64_t>(off + bytes), 1024));
+    return at;
+  };
+  g.off_a = take(static_cast<size_t>(kL) * batch * g.Mp * g.Kp);
+  g.off_b = take(static_cast<size_t>(kL) * batch * g.Np * g.Kp);
+  g.off_c = take(static_cast<size_t>(kL) * batch * g.Mp * g.Np);
+  g.off_sa = take(sizeof(int) * batch * g.Mp);
+  g.off_sb = take(sizeof(int) * batch * g.Np);
+  g.off_err = take(sizeof(int) * 4);
+  g.total = off;
+  return g;
+}
+
+// ---------------------------------------------------------------------------
+// Step 1: split.
+
+// The DS value of one operand element as f64 (f64 input: its DS split).
+__device__ __forceinline__ double ds_value(const DotOperand& o, int64_t idx) {
+  ds2 v = o.f64 ? from_f64(o.f64[idx]) : ds2{o.hi[idx], o.lo[idx]};
+  return __dadd_rn(static_cast<double>(v.hi), static_cast<double>(v.lo));
+}
+
+// v * 2^s for any int s (exact unless the result under/overflows).
+__device__ __forceinline__ double scale2(double v, int s) {
+  if (s >= -1000 && s <= 1000) return v * __longlong_as_double(static_cast<long long>(1023 + s) << 52);
+  return ldexp(v, s);
+}
+
+// int8 residue of the integer x (|x| <= 2^50) modulo mod_of(l), symmetric.
+template <int l>
+__device__ __forceinline__ int residue(int h, int mid, int low) {
+  constexpr int m = mod_of(l);
+  constexpr int c16 = 65536 % m;
+  constexpr int c32 = (c16 * c16) % m;
+  const int s = h * c32 + mid * c16 + low;
+  int r = s % m;
+  if (r > (m - 1) / 2) r -= m;
+  else if (r < -(m / 2)) r += m;
+  return r;
+}
+
+struct Limbs {
+  int h, mid, low;
+};
+
+__device__ __forceinline__ Limbs limbs_of(double v, int shift) {
+  const long long t = __double2ll_rn(rint(scale2(v, shift)));
+  return Limbs{static_cast<int>(t >> 32), static_cast<int>((t >> 16) & 0xFFFF),
+               static_cast<int>(t & 0xFFFF)};
+}
+
+// Residues of 16 consecutive values -> one 16-byte store per modulus plane.
+template <int l>
+__device__ __forceinline__ void store_plane(const Limbs (&x)[16], int8_t* plane) {
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const Limbs& v = x[q * 4 + j];
+      acc |= (static_cast<uint32_t>(residue<l>(v.h, v.mid, v.low)) & 0xFFu) << (8 * j);
+    }
+    w[q] = acc;
+  }
+  *reinterpret_cast<uint4*>(plane) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int l = 0>
+__device__ __forceinline__ void store_all_planes(const Limbs (&x)[16], int8_t* base,
+                                                 size_t plane_stride) {
+  if constexpr (l < kL) {
+    store_plane<l>(x, base + l * plane_stride);
+    store_all_planes<l + 1>(x, base, plane_stride);
+  }
+}
+
+__device__ __forceinline__ int shift_for(double mx, bool nonfinite, int P) {
+  if (nonfinite) return kShiftNonFinite;
+  if (mx == 0.0) return 0;
+  return P - (ilogb(mx) + 1);  // |v| <= mx < 2^(ilogb+1)
+}
+
+// Operand rows contiguous in K (s_k == 1): one block per (row, batch).
+__global__ void __launch_bounds__(256)
+split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
+                    int64_t batch, int P, int8_t* __restrict__ planes, int* __restrict__ shifts) {
+  __shared__ double s_max[8];
+  __shared__ int s_bad[8];
+  const int64_t r = blockIdx.x, b = blockIdx.y;
+  const bool live = r < rows;
+  const int64_t base = b * o.s_b + r * o.s_r;
+  double mx = 0.0;
+  bool bad = false;
+  if (live) {
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+      const double v = ds_value(o, base + k * o.s_k);
+      bad |= !isfinite(v);
+      mx = fmax(mx, fabs(v));
+    }
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+    bad |= __shfl_xor_sync(0xffffffffu, static_cast<int>(bad), d) != 0;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_max[threadIdx.x >> 5] = mx;
+    s_bad[threadIdx.x >> 5] = bad;
+  }
+  __syncthreads();
+  mx = 0.0;
+  bad = false;
+  for (int w = 0; w < 8; ++w) {
+    mx = fmax(mx, s_max[w]);
+    bad |= s_bad[w] != 0;
+  }
+  const int shift = live ? shift_for(mx, bad, P) : 0;
+  if (threadIdx.x == 0) shifts[b * rows_pad + r] = shift;
+  const bool zero = !live || shift == kShiftNonFinite;
+  const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
+  int8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
+  for (int64_t k0 = static_cast<int64_t>(threadIdx.x) * 16; k0 < Kp; k0 += 16 * blockDim.x) {
+    Limbs x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t k = k0 + j;
+      const double v = (zero || k >= K) ? 0.0 : ds_value(o, base + k * o.s_k);
+      x[j] = limbs_of(v, shift);
+    }
+    store_all_planes(x, row_out + k0, plane_stride);
+  }
+}
+
+// Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major):
+// one block per 32 rows; K is staged through shared memory 128 at a time and
+// written transposed (K-major).
+__global__ void __launch_bounds__(256)
+split_rowmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
+                      int64_t batch, int P, int8_t* __restrict__ planes,
+                      int* __restrict__ shifts) {
+  __shared__ double tile[kTileK][33];
+  __shared__ double s_max[8][32];
+  __shared__ int s_bad[8][32];
+  __shared__ int s_shift[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, b = blockIdx.y;
+  const int64_t r = r0 + lane;
+  const bool live = r < rows;
+  double mx = 0.0;
+  bool bad = false;
+  if (live) {
+    for (int64_t k = warp; k < K; k += 8) {
+      const double v = ds_value(o, b * o.s_b + r * o.s_r + k * o.s_k);
+      bad |= !isfinite(v);
+      mx = fmax(mx, fabs(v));
+    }
+  }
+  s_max[warp][lane] = mx;
+  s_bad[warp][lane] = bad;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < 8; ++w) {
+      mx = fmax(mx, s_max[w][lane]);
+      bad |= s_bad[w][lane] != 0;
+    }
+    const int shift = live ? shift_for(mx, bad, P) : 0;
+    s_shift[lane] = shift;
+    if (r < rows_pad) shifts[b * rows_pad + r] = shift;
+  }
+  __syncthreads();
+  const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
+  const int my_row = threadIdx.x >> 3, my_grp = threadIdx.x & 7;
+  for (int64_t kc = 0; kc < Kp; kc += kTileK) {
+    for (int idx = threadIdx.x; idx < kTileK * 32; idx += blockDim.x) {
+      const int kk = idx >> 5, rr = idx & 31;
+      const int64_t k = kc + kk, row = r0 + rr;
+      const int sh = s_shift[rr];
+      double v = 0.0;
+      if (row < rows && k < K && sh != kShiftNonFinite)
+        v = ds_value(o, b * o.s_b + row * o.s_r + k * o.s_k);
+      tile[kk][rr] = rint(scale2(v, sh == kShiftNonFinite ? 0 : sh));
+    }
+    __syncthreads();
+    Limbs x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const long long t = __double2ll_rn(tile[my_grp * 16 + j][my_row]);
+      x[j] = Limbs{static_cast<int>(t >> 32), static_cast<int>((t >> 16) & 0xFFFF),
+                   static_cast<int>(t & 0xFFFF)};
+    }
+    const int64_t row = r0 + my_row;
+    if (row < rows_pad)
+      store_all_planes(x, planes + (static_cast<size_t>(b) * rows_pad + row) * Kp + kc + my_grp * 16,
+                       plane_stride);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Step 2: tcgen05 int8 GEMM.
+
+struct GemmParams {
+  int batch, tiles_m, tiles_n, kblocks;
+  int64_t Mp, Np;
+  int64_t units;
+  uint8_t* cres;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and an error code recorded) after ~2 s, or at once if
+// another role of any CTA has already given up.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: rows of 128 B, 8-row atoms of
+// 1024 B (stride byte offset), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;          // leading byte offset (unused here): 16 B
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;          // version
+  d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
+  return d;
+}
+
+// kind::i8, D = s32, A = B = signed 8-bit, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                            (static_cast<uint32_t>(kTileN >> 3) << 17) |
+                            (static_cast<uint32_t>(kTileM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+        "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Unit {
+  int l, b, tm, tn;
+};
+
+__device__ __forceinline__ Unit unit_of(int64_t u, const GemmParams& p) {
+  const int64_t per_l = static_cast<int64_t>(p.batch) * p.tiles_m * p.tiles_n;
+  Unit x;
+  x.l = static_cast<int>(u / per_l);
+  int64_t rem = u - x.l * per_l;
+  const int64_t per_b = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  x.b = static_cast<int>(rem / per_b);
+  rem -= x.b * per_b;
+  x.tm = static_cast<int>(rem / p.tiles_n);
+  x.tn = static_cast<int>(rem - static_cast<int64_t>(x.tm) * p.tiles_n);
+  return x;
+}
+
+__device__ __forceinline__ uint32_t mod_u8(int v, int m, double inv_m) {
+  int r = v - m * static_cast<int>(floor(static_cast<double>(v) * inv_m));
+  if (r < 0) r += m;
+  if (r >= m) r -= m;
+  return static_cast<uint32_t>(r);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                  const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + kStages * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * (kStageA + kStageB));
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drained = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, p);
+        const int ya = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
+                                        static_cast<int64_t>(w.tm) * kTileM);
+        const int yb = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Np +
+                                        static_cast<int64_t>(w.tn) * kTileN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], kStageA + kStageB);
+          tma_load_2d(smem_a + stage * kStageA, &tmap_a, kb * kTileK, ya, &full[stage]);
+          tma_load_2d(smem_b + stage * kStageB, &tmap_b, kb * kTileK, yb, &full[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // After an abort, give copies already issued time to land (a few
+      // microseconds suffice) before the CTA can exit.  On the normal path
+      // the MMA warp has consumed every filled stage.
+      if (!ok) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 200000) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * kTileN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem_a + stage * kStageA);
+          const uint32_t b0 = smem_u32(smem_b + stage * kStageB);
+#pragma unroll
+          for (int k = 0; k < kTileK / 32; ++k) {
+            mma_i8(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32), (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // All issued MMAs complete before TMEM is released.
+      mma_commit(drained);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drained, 0) && clock64() - t0 < kTimeoutCycles) {
+      }
+    }
+  } else {
+    // ---- epilogue (warps 2..5; TMEM lanes 32*(warp%4) ..) ----
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, 4)) break;
+      tc_fence_after();
+      const Unit w = unit_of(u, p);
+      const int m = mod_of(w.l);
+      const double inv_m = 1.0 / static_cast<double>(m);
+      const int64_t row = (static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
+                          static_cast<int64_t>(w.tm) * kTileM + row_in_tile;
+      uint8_t* out = p.cres + row * p.Np + static_cast<int64_t>(w.tn) * kTileN;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * kTileN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kTileN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tbase + c0, v);
+        uint32_t packed[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            word |= mod_u8(static_cast<int>(v[q * 4 + j]), m, inv_m) << (8 * j);
+          packed[q] = word;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + c0);
+        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Step 3: CRT reconstruction and scaling.
+
+struct CrtParams {
+  double w[kL][3];
+  double mlimb[3];
+  double inv_m;
+  int64_t batch, M, N, Mp, Np, K;
+  const uint8_t* cres;
+  const int* sa;  // [batch][Mp]
+  const int* sb;  // [batch][Np]
+  const int* err;
+  DotOperand a, b;
+  DotResult c;
+};
+
+__device__ __forceinline__ void put_result(const DotResult& c, int64_t idx, double v) {
+  if (c.f64) {
+    c.f64[idx] = v;
+  } else {
+    const ds2 d = from_f64(v);
+    c.hi[idx] = d.hi;
+    c.lo[idx] = d.lo;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+crt_kernel(CrtParams p) {
+  const int64_t per_b = p.M * p.N;
+  const int64_t total = p.batch * per_b;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
+  const bool failed = *p.err != 0;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += stride) {
+    const int64_t b = idx / per_b;
+    const int64_t rem = idx - b * per_b;
+    const int64_t i = rem / p.N, j = rem - i * p.N;
+    const int sa = p.sa[b * p.Mp + i], sb = p.sb[b * p.Np + j];
+    double out;
+    if (failed) {
+      out = __longlong_as_double(0x7ff8000000000000LL);
+    } else if (sa == kShiftNonFinite || sb == kShiftNonFinite) {
+      // A non-finite operand: the IEEE sum of the DS-valued products carries
+      // NaN/Inf exactly as a float GEMM would.
+      double s = 0.0;
+      for (int64_t k = 0; k < p.K; ++k)
+        s += ds_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
+             ds_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
+      out = s;
+    } else {
+      const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j;
+      double s0 = 0.0, s1 = 0.0, s2 = 0.0;
+#pragma unroll
+      for (int l = 0; l < kL; ++l) {
+        const double r = static_cast<double>(p.cres[l * plane + at]);
+        s0 = __fma_rn(r, p.w[l][0], s0);
+        s1 = __fma_rn(r, p.w[l][1], s1);
+        s2 = __fma_rn(r, p.w[l][2], s2);
+      }
+      const double approx = __fma_rn(s2, 0x1p80, s1 * 0x1p40);
+      const double q = rint(approx * p.inv_m);
+      const double t0 = __fma_rn(-q, p.mlimb[0], s0);
+      const double t1 = __fma_rn(-q, p.mlimb[1], s1);
+      const double t2 = __fma_rn(-q, p.mlimb[2], s2);
+      const double hi = __fma_rn(t2, 0x1p40, t1);
+      const double cint = __fma_rn(hi, 0x1p40, t0);
+      out = scale2(scale2(cint, -sa), -sb);
+    }
+    put_result(p.c, idx, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+int make_tmap(CUtensorMap* map, const void* base, int64_t Kp, int64_t rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(DS_INTERNAL, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(Kp)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DS_INTERNAL, "cuTensorMapEncodeTiled failed");
+  return DS_OK;
+}
+
+size_t gemm_smem_bytes() {
+  return 1024 + kStages * (kStageA + kStageB) + (2 * kStages + 5) * sizeof(uint64_t) + 16;
+}
+
+int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
+                 int64_t Kp, int P, int8_t* planes, int* shifts, cudaStream_t s) {
+  if (o.s_k == 1 || rows == 1) {
+    dim3 grid(static_cast<unsigned>(rows_pad), static_cast<unsigned>(batch));
+    split_kmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes, shifts);
+  } else {
+    dim3 grid(static_cast<unsigned>((rows_pad + 31) / 32), static_cast<unsigned>(batch));
+    split_rowmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes,
+                                               shifts);
+  }
+  return launch_status();
+}
+
+}  // namespace
+
+bool dot_ozaki_supported(int64_t M, int64_t N, int64_t K) {
+  return M >= 2 && N >= 2 && K >= 1 && K <= kMaxK;
+}
+
+size_t dot_ozaki_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  return layout_of(batch, M, N, K).total;
+}
+
+int dot_ozaki_params(int64_t K, int* moduli, int* bits) {
+  if (moduli) *moduli = kL;
+  if (bits) *bits = bits_for_k(K);
+  return DS_OK;
+}
+
+int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (p.batch == 0 || p.M == 0 || p.N == 0) return ok();
+  const Layout g = layout_of(p.batch, p.M, p.N, p.K);
+  if (workspace_bytes < g.total || !aligned(workspace, 256))
+    return set_error(DS_INVALID_ARGUMENT,
+                     "dot_general: workspace too small (need " + std::to_string(g.total) +
+                         " bytes, 256-byte aligned)");
+  const int64_t max_rows = (1LL << 31) - 1;  // TMA y coordinates are int32
+  if (p.batch > 65535 || kL * p.batch * g.Mp > max_rows || kL * p.batch * g.Np > max_rows ||
+      g.Kp > max_rows)
+    return set_error(DS_INVALID_ARGUMENT, "dot_general: problem too large for the tensor-core path");
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(ozaki_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(gemm_smem_bytes()));
+  });
+  if (attr_err != cudaSuccess) return cuda_status(attr_err);
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int8_t* planes_a = reinterpret_cast<int8_t*>(ws + g.off_a);
+  int8_t* planes_b = reinterpret_cast<int8_t*>(ws + g.off_b);
+  uint8_t* cres = ws + g.off_c;
+  int* sa = reinterpret_cast<int*>(ws + g.off_sa);
+  int* sb = reinterpret_cast<int*>(ws + g.off_sb);
+  int* err = reinterpret_cast<int*>(ws + g.off_err);
+  const int P = bits_for_k(p.K);
+
+  DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+  {
+    ProfileScope prof("ozaki_split", s);
+    if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, s)) return st;
+    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, s)) return st;
+  }
+
+  CUtensorMap ta, tb;
+  if (int st = make_tmap(&ta, planes_a, g.Kp, kL * p.batch * g.Mp, kTileM)) return st;
+  if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np, kTileN)) return st;
+  GemmParams gp{};
+  gp.batch = static_cast<int>(p.batch);
+  gp.tiles_m = static_cast<int>(g.Mp / kTileM);
+  gp.tiles_n = static_cast<int>(g.Np / kTileN);
+  gp.kblocks = static_cast<int>(g.Kp / kTileK);
+  gp.Mp = g.Mp;
+  gp.Np = g.Np;
+  gp.units = static_cast<int64_t>(kL) * p.batch * gp.tiles_m * gp.tiles_n;
+  gp.cres = cres;
+  gp.err = err;
+  const int grid = static_cast<int>(gp.units < sm_count() ? gp.units : sm_count());
+  {
+    ProfileScope prof("ozaki_gemm", s);
+    ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), s>>>(ta, tb, gp);
+    if (int st = launch_status()) return st;
+  }
+
+  const CrtConsts& cc = crt_consts();
+  CrtParams cp{};
+  std::memcpy(cp.w, cc.w, sizeof(cp.w));
+  std::memcpy(cp.mlimb, cc.mlimb, sizeof(cp.mlimb));
+  cp.inv_m = cc.inv_m;
+  cp.batch = p.batch;
+  cp.M = p.M;
+  cp.N = p.N;
+  cp.Mp = g.Mp;
+  cp.Np = g.Np;
+  cp.K = p.K;
+  cp.cres = cres;
+  cp.sa = sa;
+  cp.sb = sb;
+  cp.err = err;
+  cp.a = p.a;
+  cp.b = p.b;
+  cp.c = p.c;
+  ProfileScope prof("ozaki_crt", s);
+  crt_kernel<<<grid_for(p.batch * p.M * p.N, 256, 8), 256, 0, s>>>(cp);
+  return launch_status();
 }
 
 }  // namespace dsb

@@ -3,10 +3,10 @@
 // Every multiply-accumulate takes the exact DS operands a = ah + al and
 // b = bh + bl, forms the exact leading product p + e = ah * bh (p = fl(ah*bh),
 // e = fma(ah, bh, -p)), adds the cross terms ah*bl + al*bh + al*bl into e with
-// FMAs, and accumulates p into a (sum, carry) pair with Knuth's two_sum
-// (Ogita-Rump-Oishi compensated dot).  The result is as accurate as a
-// twice-f32-precision accumulation, far below the reference's f32-accumulated
-// sub-dots (DsTransformPass.cpp:359-365).  13 FP32-pipe instructions per MAC.
+// FMAs, and accumulates p into a DS pair with Knuth's two_sum followed by a
+// fast two_sum renormalisation, so every step rounds at the DS level
+// (~2^-48 of the running sum) -- far below the reference's f32-accumulated
+// sub-dots (DsTransformPass.cpp:359-365).  16 FP32-pipe instructions per MAC.
 //
 // GEMM: 64x64 output tile per 256-thread block, 4x4 outputs per thread, K
 // staged through shared memory 16 at a time as hi/lo planes.  Operands are
@@ -28,7 +28,9 @@ struct Acc {
   float s, c;
 };
 
-// (s, c) += a * b with a = (ah, al), b = (bh, bl).
+// (s, c) += a * b with a = (ah, al), b = (bh, bl); (s, c) is renormalised
+// after every step (fast two_sum), so |c| stays below ulp(s) and its own
+// rounding errors stay at the DS level (~2^-48 |s|) instead of growing with K.
 __device__ __forceinline__ void mac(Acc& acc, float ah, float al, float bh, float bl) {
   const float p = __fmul_rn(ah, bh);
   float t = __fmaf_rn(ah, bh, -p);
@@ -37,8 +39,9 @@ __device__ __forceinline__ void mac(Acc& acc, float ah, float al, float bh, floa
   t = __fmaf_rn(al, bl, t);
   float s, e;
   two_sum(acc.s, p, s, e);
-  acc.s = s;
-  acc.c = __fadd_rn(acc.c, __fadd_rn(e, t));
+  const float c = __fadd_rn(acc.c, __fadd_rn(e, t));
+  acc.s = __fadd_rn(s, c);
+  acc.c = __fsub_rn(c, __fsub_rn(acc.s, s));
 }
 
 __device__ __forceinline__ Acc acc_merge(Acc x, Acc y) {

@@ -79,14 +79,27 @@ SIGNATURES = {
     "ds_reduce": ([_BUF, _BUF, _BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                   ctypes.c_int),
     "ds_reduce_f64": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
+    "ds_reduce_from_f64": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
+                           ctypes.c_int),
     "ds_dot_general_workspace_size": ([_BUF, _BUF, _DIMS, _I32], _SZ),
     "ds_dot_general": ([_BUF, _BUF, _BUF, _BUF, _DIMS, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                        ctypes.c_int),
     "ds_dot_general_f64": ([_BUF, _BUF, _DIMS, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
+    "ds_dot_tensor_plan": ([_I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_profile_enable": ([ctypes.c_int], None),
     "ds_profile_reset": ([], None),
     "ds_profile_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), _I64P], ctypes.c_int),
 }
+
+
+def gemm_info(M: int, N: int, K: int) -> dict:
+    """Plan of the tensor-core dot_general for an M x N x K product: int8 GEMMs
+    (moduli), bits kept per operand, and the int8 tensor ops it performs
+    (2 per MAC, unpadded)."""
+    m, b = ctypes.c_int32(), ctypes.c_int32()
+    check(lib().ds_dot_tensor_plan(int(K), ctypes.byref(m), ctypes.byref(b)), "plan")
+    return {"moduli": m.value, "bits": b.value,
+            "tensor_ops_per_launch": float(m.value) * 2.0 * M * N * K}
 
 
 def profile_enable(on: bool = True) -> None:

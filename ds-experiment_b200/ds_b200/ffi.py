@@ -64,6 +64,8 @@ CONVENTIONS: Dict[str, _Convention] = {
     "ds_reduce": _Convention((F32, F32, F32, F32), ("dimensions", "body"), (F32, F32),
                              "reduce"),
     "ds_reduce_f64": _Convention((F64, F64), ("dimensions", "body"), (F64,), "reduce_f64"),
+    "ds_reduce_from_f64": _Convention((F64, F64), ("dimensions", "body"), (F32, F32),
+                                      "reduce_from_f64"),
     "ds_dot_general": _Convention((F32, F32, F32, F32),
                                   ("lhs_batching_dimensions", "rhs_batching_dimensions",
                                    "lhs_contracting_dimensions",
@@ -95,6 +97,7 @@ REFERENCE_TARGETS = {
     "ds_recurrence_mul_add_to_f64": "ds_recurrence_mul_add_to_f64",
     "ds_reduce": "ds_reduce",
     "ds_reduce_f64": "ds_reduce_f64",
+    "ds_reduce_from_f64": "ds_reduce_from_f64",
     "ds_dot_general": "ds_dot_general",
     "ds_dot_general_f64": "ds_dot_general_f64",
 }
@@ -192,19 +195,22 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
                     call_args.append(int(attrs[name]))
                 call_args += refs[len(args):]
                 status = fn(*call_args, stream)
-            elif conv.kind in ("reduce", "reduce_f64"):
+            elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64"):
                 dims = tuple(int(d) for d in attrs.get("dimensions", ()))
                 body = int(attrs.get("body", _lib.DS_BODY_ADD))
                 cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
                 ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
                 ws = _workspace(ws_bytes, device)
+                wsp = ctypes.c_void_p(ws.data_ptr())
                 if conv.kind == "reduce":
                     status = fn(refs[0], refs[1], refs[2], refs[3], cdims, len(dims), body,
-                                refs[4], refs[5], ctypes.c_void_p(ws.data_ptr()), ws_bytes,
-                                stream)
+                                refs[4], refs[5], wsp, ws_bytes, stream)
+                elif conv.kind == "reduce_f64":
+                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], wsp,
+                                ws_bytes, stream)
                 else:
-                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2],
-                                ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream)
+                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], refs[3],
+                                wsp, ws_bytes, stream)
             else:
                 dd = _dot_dims(attrs, args[0].dim())
                 algorithm = int(attrs.get("algorithm", _lib.DS_DOT_TENSOR_INT8))

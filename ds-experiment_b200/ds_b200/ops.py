@@ -134,6 +134,16 @@ def ds_reduce_f64(x: torch.Tensor, init: float = 0.0,
         x, it, dimensions=dims, body=_BODIES[body])
 
 
+def ds_reduce_from_f64(x: torch.Tensor, init: float = 0.0,
+                       dimensions: Optional[Sequence[int]] = None, body: str = "add"):
+    """DS reduce of an f64 tensor with the result kept as a DS pair (hi, lo)."""
+    dims = _reduce_dims(x.dim(), dimensions)
+    it = torch.tensor(float(init), dtype=F64, device=x.device)
+    out = _sds(_out_shape(x.shape, dims), F32)
+    return ffi_call("ds_reduce_from_f64", (out, out))(x, it, dimensions=dims,
+                                                      body=_BODIES[body])
+
+
 def ds_sum_f64(x: torch.Tensor, dimensions=None) -> torch.Tensor:
     return ds_reduce_f64(x, 0.0, dimensions, "add")
 

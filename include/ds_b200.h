@@ -188,6 +188,15 @@ DS_API int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init,
                   const ds_buffer* out, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* The split fused on input only: f64 input and rank-0 f64 init, SoA DS
+   result (out_hi, out_lo) -- the pass's reduce of an f64 argument whose
+   result stays in DS form (e.g. a partial sum that is combined further). */
+DS_API int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init,
+                              const int64_t* dimensions, int64_t n_dimensions,
+                              int32_t body, const ds_buffer* out_hi,
+                              const ds_buffer* out_lo, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* ---- dot_general (DsTransformPass.cpp:337-370) --------------------------- */
 
 /* DS dot_general of SoA operands (lhs_hi, lhs_lo), (rhs_hi, rhs_lo) f32 with
@@ -217,6 +226,11 @@ DS_API int ds_dot_general_f64(const ds_buffer* lhs, const ds_buffer* rhs,
    "recurrence", "reduce", "dot_simt", "dot_vec", "ozaki_split",
    "ozaki_gemm", "ozaki_crt").  ds_profile_read waits for the recorded
    events and returns the summed milliseconds and the launch count. */
+/* Plan of the tensor-core dot_general for contraction length K: the number
+   of int8 GEMMs (moduli) it runs and the bits each operand keeps relative to
+   its row (column) maximum. */
+DS_API int ds_dot_tensor_plan(int64_t K, int32_t* moduli, int32_t* bits);
+
 DS_API void ds_profile_enable(int on);
 DS_API void ds_profile_reset(void);
 DS_API int ds_profile_read(const char* name, double* total_ms, int64_t* launches);

@@ -1,0 +1,115 @@
+"""Multi-rank host logic with CPU ranks (gloo, world size 2 and 3).
+
+The per-rank GPU reduction and the fold are replaced by the oracle (the
+checker), so what runs here is the sharding, the (hi, lo) all-gather and the
+fixed-order combine that ds_b200.dist performs on GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG_DIR, ROOT
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, n, q):
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        _worker_body(rank, world, n, q)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, None, repr(e), None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _worker_body(rank, world, n, q):
+    if True:
+        from ds_b200 import dist as dsd
+        from oracle import dso
+        rng = np.random.default_rng(1)
+        x = np.where(np.arange(n) % 2 == 0, 1e8, -1e8) + rng.uniform(0, 1, n) * 1e-3
+        start, stop = dsd.shard_range(n, rank, world)
+        local = torch.from_numpy(x[start:stop])
+
+        def local_pair(t):
+            h, l = dso.ds_reduce_f64_seq(t.numpy())
+            return torch.tensor([h, l], dtype=torch.float32)
+
+        def combine(pairs, init):
+            p = pairs.numpy()
+            h, l = dso.ds_reduce_ds_seq(p[:, 0], p[:, 1], init=init)
+            return torch.tensor(float(h) + float(l), dtype=torch.float64)
+
+        r = dsd.ds_sum_f64_sharded(local, init=0.5, local_pair=local_pair, combine=combine)
+        allr = [torch.zeros((), dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(allr, r)
+        q.put((rank, float(r), [float(v) for v in allr], (start, stop)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_sum_gloo(world):
+    n = 100_003
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    errors = [r for r in results if r[1] is None]
+    assert not errors, errors
+    assert all(p.exitcode == 0 for p in procs)
+    results.sort()
+    # every rank holds the same bits
+    vals = {v for _, v, _, _ in results}
+    assert len(vals) == 1
+    for _, v, allv, _ in results:
+        assert len(set(allv)) == 1 and allv[0] == v
+    # the shards tile [0, n)
+    ranges = [rg for *_, rg in results]
+    assert ranges[0][0] == 0 and ranges[-1][1] == n
+    assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    # as close to the exact sum (+ init) as the reference-order DS fold: the
+    # running sum swings through +-1e8, where DS resolves about 1e8 * 2^-48
+    import math
+
+    from oracle import dso
+    rng = np.random.default_rng(1)
+    x = np.where(np.arange(n) % 2 == 0, 1e8, -1e8) + rng.uniform(0, 1, n) * 1e-3
+    truth = math.fsum(x.tolist()) + 0.5
+    h, l = dso.ds_reduce_f64_seq(x, init=(0.5, 0.0))
+    seq_err = abs(float(h) + float(l) - truth)
+    assert abs(results[0][1] - truth) <= 4 * seq_err + 1e-12
+
+
+def test_shard_range_covers():
+    from ds_b200.dist import shard_range
+    for n in (0, 1, 7, 4096, 100_003):
+        for world in (1, 2, 3, 8):
+            parts = [shard_range(n, r, world) for r in range(world)]
+            assert parts[0][0] == 0 and parts[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+            sizes = [b - a for a, b in parts]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(10, 3, 3)
