@@ -259,6 +259,16 @@ def run_ours(args):
                     "note": "CUDA-core path (tensor-core kernel unavailable)",
                     "kernel_ms_per_launch": round(per_launch_ms, 4)}
     gpu_launches = sum(v["launches"] for v in launches.values())
+    if args.kernels_only:
+        # Profiling case: the timed steps alone (no e2e, accuracy or CPU legs).
+        if world > 1:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        return {"metric": METRIC, "value": round(value, 1), "unit": "GFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "roofline": roofline,
+                "kernel_launches": launches, "note": "--kernels-only profiling run"}
 
     # e2e through the public API with pinned host buffers
     hA = torch.from_numpy(A).pin_memory()
@@ -425,6 +435,8 @@ def main():
     ap.add_argument("--workload", default="gemm")
     ap.add_argument("--algorithm", default="tensor", choices=["tensor", "cuda_core"])
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="time the device steps only (the case used for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
