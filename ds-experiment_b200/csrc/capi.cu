@@ -452,6 +452,21 @@ int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init, const int64_t
   return reduce_launch(a, as_stream(stream));
 }
 
+int ds_reduce_f64_noalloc(const ds_buffer* in, const ds_buffer* init,
+                          const int64_t* dimensions, int64_t n_dimensions, int32_t body,
+                          const ds_buffer* out, void* stream) {
+  if (int st = check_buffers({in, init, out}, "ds_reduce_f64_noalloc")) return st;
+  if (total(init) != 1) return invalid("ds_reduce_f64_noalloc: init value must be a scalar");
+  ReduceArgs a;
+  if (int st = reduce_common("ds_reduce_f64_noalloc", in, dimensions, n_dimensions, body, out, a))
+    return st;
+  a.in_f64 = f64p(in);
+  a.init_f64 = f64p(init);
+  a.out_f64 = static_cast<double*>(out->data);
+  a.body = body;
+  return reduce_launch_noalloc(a, as_stream(stream));
+}
+
 size_t ds_dot_general_workspace_size(const ds_buffer* lhs, const ds_buffer* rhs,
                                      const ds_dot_dims* dims, int32_t algorithm) {
   if (!valid_buffer(lhs) || !valid_buffer(rhs) || bad_dims(lhs) || bad_dims(rhs)) return 0;

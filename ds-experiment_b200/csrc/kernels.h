@@ -46,6 +46,8 @@ struct ReduceArgs {
 };
 size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner);
 int reduce_launch(const ReduceArgs& a, cudaStream_t s);
+// The same with the full-reduction partials in a static device array.
+int reduce_launch_noalloc(ReduceArgs a, cudaStream_t s);
 
 // Operand of a dot: element (b, r, k) of a batched [batch, rows, K] view at
 // base[b * s_b + r * s_r + k * s_k], given as f64 or as SoA hi/lo f32.

@@ -15,6 +15,10 @@
 // Add and subtract bodies accumulate with ds_add (subtract: init - sum);
 // multiply accumulates with ds_mul.  Every combine order is fixed by the
 // shape, so results are deterministic.  HBM-bound for long inputs.
+#include <mutex>
+#include <string>
+#include <vector>
+
 #include "common.cuh"
 #include "ds_arith.cuh"
 #include "kernels.h"
@@ -234,6 +238,61 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
   reduce_cols_kernel<<<grid_for(outer * inner, kThreads, 8), kThreads, 0, s>>>(
       src, outer, red, inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
   return launch_status();
+}
+
+// ---- allocation-free variant ------------------------------------------------
+//
+// For callers that cannot allocate device memory (see ds_reduce_f64_noalloc
+// in ds_b200.h), the block partials of a full reduction live in this
+// file-scope device array instead of caller workspace.  Every GPU that loads
+// the library holds it (32 KiB) until the process exits.  Host code cannot
+// use the symbol itself as a pointer (on the host it names a stand-in, not
+// device memory), so its device address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, and passed to the kernels.
+// All calls share the array: stage 1 overwrites every slot that stage 2
+// reads, so nothing needs clearing between calls, but two calls whose
+// kernels overlap on the GPU (different streams, no ordering) race on it.
+
+constexpr int kStaticPartials = 4096;
+static __device__ __align__(256) ds2 g_static_partials[kStaticPartials];
+
+namespace {
+
+int static_partials_address(ds2** out) {
+  static std::mutex mu;
+  static std::vector<ds2*> by_device;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(by_device.size())) by_device.resize(dev + 1, nullptr);
+  if (by_device[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_partials);
+    if (e != cudaSuccess) return cuda_status(e);
+    by_device[dev] = static_cast<ds2*>(p);
+  }
+  *out = by_device[dev];
+  return ok();
+}
+
+}  // namespace
+
+int reduce_launch_noalloc(ReduceArgs a, cudaStream_t s) {
+  if (a.outer == 1 && a.inner == 1 && a.red > 0) {
+    const int g = reduce_full_blocks(a.red);
+    if (g > kStaticPartials) {
+      return set_error(DS_INVALID_ARGUMENT,
+                       "ds_reduce_f64_noalloc: needs " + std::to_string(g) +
+                           " block partials, more than its static maximum of " +
+                           std::to_string(kStaticPartials));
+    }
+    ds2* partials = nullptr;
+    if (int st = static_partials_address(&partials)) return st;
+    a.workspace = partials;
+    a.workspace_bytes = sizeof(g_static_partials);
+  }
+  return reduce_launch(a, s);
 }
 
 }  // namespace dsb

@@ -188,6 +188,32 @@ DS_API int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init,
                   const ds_buffer* out, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* ds_reduce_f64 for callers that cannot allocate device memory.  No
+   counterpart in the reference.
+   Some callers have no way to obtain scratch: an XLA-FFI handler bound
+   without a scratch-allocator context, or code running next to a framework
+   whose caching allocator (XLA's BFC allocator, torch's) has already reserved
+   most of HBM, where a cudaMalloc of its own can fail and, because it may
+   synchronise the device, would also stall every stream.  This entry point
+   takes only inputs and outputs and allocates nothing: the block partials of
+   a full reduction live in a library-owned static device array of 4096
+   partials (32 KiB), which every GPU that loads the library holds until the
+   process exits.  Results are bit-identical to ds_reduce_f64.
+   - A reduction that would need more than 4096 block partials returns
+     DS_INVALID_ARGUMENT (the partial count is at most 4 per SM, so this does
+     not occur on B200).
+   - The first call on each device looks up the array's device address
+     (cudaGetSymbolAddress) with that device current; make that first call
+     before any stream capture.
+   - All calls share the array, which keeps the last call's contents (each
+     call overwrites every slot it reads, so no clearing is needed); calls
+     whose kernels overlap on the GPU race on it and must be ordered (same
+     stream, or events). */
+DS_API int ds_reduce_f64_noalloc(const ds_buffer* in, const ds_buffer* init,
+                                 const int64_t* dimensions, int64_t n_dimensions,
+                                 int32_t body, const ds_buffer* out,
+                                 void* stream);
+
 /* The split fused on input only: f64 input and rank-0 f64 init, SoA DS
    result (out_hi, out_lo) -- the pass's reduce of an f64 argument whose
    result stays in DS form (e.g. a partial sum that is combined further). */
