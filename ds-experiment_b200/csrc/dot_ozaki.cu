@@ -56,7 +56,8 @@ constexpr int kStages = 4;
 constexpr int kStageA = kTileM * kTileK;  // 16 KB
 constexpr int kStageB = kTileN * kTileK;  // 32 KB
 constexpr int kGemmThreads = 192;
-constexpr int kMaxK = 1 << 17;
+// u8 x u8 products summed in int32: K * 255^2 < 2^31 needs K <= 33025.
+constexpr int kMaxK = 1 << 15;
 constexpr int kShiftNonFinite = INT_MIN;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -116,7 +117,7 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 struct Layout {
   int64_t batch, M, N, K, Mp, Np, Kp;
-  size_t off_a, off_b, off_c, off_sa, off_sb, off_err, total;
+  size_t off_a, off_b, off_c, off_sa, off_sb, off_ca, off_cb, off_err, total;
 };
 
 Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
@@ -139,6 +140,8 @@ Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
   g.off_c = take(static_cast<size_t>(kL) * batch * g.Mp * g.Np);
   g.off_sa = take(sizeof(int) * batch * g.Mp);
   g.off_sb = take(sizeof(int) * batch * g.Np);
+  g.off_ca = take(sizeof(int) * batch * g.Mp);
+  g.off_cb = take(sizeof(int) * batch * g.Np);
   g.off_err = take(sizeof(int) * 4);
   g.total = off;
   return g;
@@ -147,10 +150,11 @@ Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
 // ---------------------------------------------------------------------------
 // Step 1: split.
 
-// The DS value of one operand element as f64 (f64 input: its DS split).
-__device__ __forceinline__ double ds_value(const DotOperand& o, int64_t idx) {
-  ds2 v = o.f64 ? from_f64(o.f64[idx]) : ds2{o.hi[idx], o.lo[idx]};
-  return __dadd_rn(static_cast<double>(v.hi), static_cast<double>(v.lo));
+// The value an operand element contributes: an f64 input as it is (it is at
+// least as precise as its DS split), a SoA DS input as hi + lo.
+__device__ __forceinline__ double op_value(const DotOperand& o, int64_t idx) {
+  return o.f64 ? o.f64[idx]
+               : __dadd_rn(static_cast<double>(o.hi[idx]), static_cast<double>(o.lo[idx]));
 }
 
 // v * 2^s for any int s (exact unless the result under/overflows).
@@ -159,48 +163,55 @@ __device__ __forceinline__ double scale2(double v, int s) {
   return ldexp(v, s);
 }
 
-// int8 residue of the integer x (|x| <= 2^50) modulo mod_of(l), symmetric.
-template <int l>
-__device__ __forceinline__ int residue(int h, int mid, int low) {
-  constexpr int m = mod_of(l);
-  constexpr int c16 = 65536 % m;
-  constexpr int c32 = (c16 * c16) % m;
-  const int s = h * c32 + mid * c16 + low;
-  int r = s % m;
-  if (r > (m - 1) / 2) r -= m;
-  else if (r < -(m / 2)) r += m;
-  return r;
+constexpr double kMagic = 6755399441055744.0;  // 1.5 * 2^52
+
+// The biased integer t = rint(v * 2^shift) + 2^51, for |v * 2^shift| <= 2^50:
+// adding 1.5 * 2^52 rounds to an integer (to nearest even) and leaves t in
+// the low 52 bits of the sum, so no conversion instruction is needed.
+__device__ __forceinline__ uint64_t quantise(double v, int shift) {
+  const double y = (shift >= -1000 && shift <= 1000)
+                       ? __fma_rn(v, __longlong_as_double(static_cast<long long>(1023 + shift) << 52), kMagic)
+                       : __dadd_rn(ldexp(v, shift), kMagic);
+  return static_cast<uint64_t>(__double_as_longlong(y)) & ((1ull << 52) - 1);
 }
 
+// t = h * 2^32 + mid * 2^16 + low, all limbs non-negative (h < 2^20).
 struct Limbs {
-  int h, mid, low;
+  uint32_t h, mid, low;
 };
 
-__device__ __forceinline__ Limbs limbs_of(double v, int shift) {
-  const long long t = __double2ll_rn(rint(scale2(v, shift)));
-  return Limbs{static_cast<int>(t >> 32), static_cast<int>((t >> 16) & 0xFFFF),
-               static_cast<int>(t & 0xFFFF)};
+__device__ __forceinline__ Limbs limbs_of(uint64_t t) {
+  const uint32_t lo32 = static_cast<uint32_t>(t);
+  return Limbs{static_cast<uint32_t>(t >> 32), lo32 >> 16, lo32 & 0xFFFFu};
+}
+
+// Residue in [0, m) of the unbiased integer t - 2^51 modulo m = mod_of(l):
+// a linear map of the limbs (< 2^29, no overflow) plus the constant that
+// cancels the bias, then one unsigned modulo by a constant.
+template <int l>
+__device__ __forceinline__ uint32_t residue(const Limbs& x) {
+  constexpr uint32_t m = mod_of(l);
+  constexpr uint32_t c16 = 65536u % m;
+  constexpr uint32_t c32 = (c16 * c16) % m;
+  constexpr uint32_t bias = static_cast<uint32_t>((1ull << 51) % m);
+  constexpr uint32_t unbias = (m - bias) % m;
+  return (x.h * c32 + x.mid * c16 + x.low + unbias) % m;
 }
 
 // Residues of 16 consecutive values -> one 16-byte store per modulus plane.
 template <int l>
-__device__ __forceinline__ void store_plane(const Limbs (&x)[16], int8_t* plane) {
+__device__ __forceinline__ void store_plane(const Limbs (&x)[16], uint8_t* plane) {
   uint32_t w[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    uint32_t acc = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const Limbs& v = x[q * 4 + j];
-      acc |= (static_cast<uint32_t>(residue<l>(v.h, v.mid, v.low)) & 0xFFu) << (8 * j);
-    }
-    w[q] = acc;
+    w[q] = residue<l>(x[q * 4]) | (residue<l>(x[q * 4 + 1]) << 8) |
+           (residue<l>(x[q * 4 + 2]) << 16) | (residue<l>(x[q * 4 + 3]) << 24);
   }
   *reinterpret_cast<uint4*>(plane) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int l = 0>
-__device__ __forceinline__ void store_all_planes(const Limbs (&x)[16], int8_t* base,
+__device__ __forceinline__ void store_all_planes(const Limbs (&x)[16], uint8_t* base,
                                                  size_t plane_stride) {
   if constexpr (l < kL) {
     store_plane<l>(x, base + l * plane_stride);
@@ -214,10 +225,23 @@ __device__ __forceinline__ int shift_for(double mx, bool nonfinite, int P) {
   return P - (ilogb(mx) + 1);  // |v| <= mx < 2^(ilogb+1)
 }
 
-// Operand rows contiguous in K (s_k == 1): one block per (row, batch).
+// Encoded row exponent for atomicMax across blocks: 0 = all zero,
+// kExpNonFinite = a NaN/Inf seen, else ilogb(max) + 1 + kExpBias.
+constexpr int kExpBias = 2048;
+constexpr int kExpNonFinite = 0x7FFFFFFF;
+
+__device__ __forceinline__ int shift_from_code(int code, int P) {
+  if (code == kExpNonFinite) return kShiftNonFinite;
+  if (code == 0) return 0;
+  return P - (code - kExpBias);
+}
+
+// Operand rows contiguous in K (s_k == 1): one block per (row, batch); pass
+// 1 finds the row maximum, pass 2 (reading the row again, mostly from L1/L2)
+// writes 16 residues per thread per modulus.
 __global__ void __launch_bounds__(256)
 split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
-                    int64_t batch, int P, int8_t* __restrict__ planes, int* __restrict__ shifts) {
+                    int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts) {
   __shared__ double s_max[8];
   __shared__ int s_bad[8];
   const int64_t r = blockIdx.x, b = blockIdx.y;
@@ -227,7 +251,7 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   bool bad = false;
   if (live) {
     for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-      const double v = ds_value(o, base + k * o.s_k);
+      const double v = op_value(o, base + k * o.s_k);
       bad |= !isfinite(v);
       mx = fmax(mx, fabs(v));
     }
@@ -252,82 +276,88 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   if (threadIdx.x == 0) shifts[b * rows_pad + r] = shift;
   const bool zero = !live || shift == kShiftNonFinite;
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  int8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
+  uint8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
   for (int64_t k0 = static_cast<int64_t>(threadIdx.x) * 16; k0 < Kp; k0 += 16 * blockDim.x) {
     Limbs x[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int64_t k = k0 + j;
-      const double v = (zero || k >= K) ? 0.0 : ds_value(o, base + k * o.s_k);
-      x[j] = limbs_of(v, shift);
+      const double v = (zero || k >= K) ? 0.0 : op_value(o, base + k * o.s_k);
+      x[j] = limbs_of(quantise(v, zero ? 0 : shift));
     }
     store_all_planes(x, row_out + k0, plane_stride);
   }
 }
 
-// Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major):
-// one block per 32 rows; K is staged through shared memory 128 at a time and
-// written transposed (K-major).
+// Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major),
+// pass 1: per-row maximum over a 256-deep slab of K per block, merged across
+// blocks with atomicMax on an encoded exponent (codes start at 0).
 __global__ void __launch_bounds__(256)
-split_rowmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
-                      int64_t batch, int P, int8_t* __restrict__ planes,
-                      int* __restrict__ shifts) {
-  __shared__ double tile[kTileK][33];
+colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
+              int* __restrict__ codes) {
   __shared__ double s_max[8][32];
   __shared__ int s_bad[8][32];
-  __shared__ int s_shift[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, b = blockIdx.y;
-  const int64_t r = r0 + lane;
-  const bool live = r < rows;
+  const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 32 + lane, b = blockIdx.z;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 256;
+  const int64_t k1 = k0 + 256 < K ? k0 + 256 : K;
   double mx = 0.0;
   bool bad = false;
-  if (live) {
-    for (int64_t k = warp; k < K; k += 8) {
-      const double v = ds_value(o, b * o.s_b + r * o.s_r + k * o.s_k);
+  if (r < rows) {
+    for (int64_t k = k0 + ty; k < k1; k += 8) {
+      const double v = op_value(o, b * o.s_b + r * o.s_r + k * o.s_k);
       bad |= !isfinite(v);
       mx = fmax(mx, fabs(v));
     }
   }
-  s_max[warp][lane] = mx;
-  s_bad[warp][lane] = bad;
+  s_max[ty][lane] = mx;
+  s_bad[ty][lane] = bad;
   __syncthreads();
-  if (warp == 0) {
+  if (ty == 0 && r < rows) {
     for (int w = 1; w < 8; ++w) {
       mx = fmax(mx, s_max[w][lane]);
       bad |= s_bad[w][lane] != 0;
     }
-    const int shift = live ? shift_for(mx, bad, P) : 0;
-    s_shift[lane] = shift;
-    if (r < rows_pad) shifts[b * rows_pad + r] = shift;
+    const int code = bad ? kExpNonFinite : (mx == 0.0 ? 0 : ilogb(mx) + 1 + kExpBias);
+    if (code != 0) atomicMax(&codes[b * rows_pad + r], code);
+  }
+}
+
+// Pass 2: one block per (32 rows, 128 K) tile: values are quantised into a
+// shared-memory tile (loads coalesced along rows), then written transposed
+// (K-major), 16 residues per thread per modulus.
+__global__ void __launch_bounds__(256)
+split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
+                  int64_t batch, int P, const int* __restrict__ codes,
+                  uint8_t* __restrict__ planes, int* __restrict__ shifts) {
+  __shared__ uint64_t tile[kTileK][33];
+  __shared__ int s_shift[32];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, b = blockIdx.z;
+  const int64_t kc = static_cast<int64_t>(blockIdx.y) * kTileK;
+  if (threadIdx.x < 32) {
+    const int64_t r = r0 + threadIdx.x;
+    const int sh = r < rows ? shift_from_code(codes[b * rows_pad + r], P) : 0;
+    s_shift[threadIdx.x] = sh;
+    if (blockIdx.y == 0) shifts[b * rows_pad + r] = sh;
   }
   __syncthreads();
-  const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  const int my_row = threadIdx.x >> 3, my_grp = threadIdx.x & 7;
-  for (int64_t kc = 0; kc < Kp; kc += kTileK) {
-    for (int idx = threadIdx.x; idx < kTileK * 32; idx += blockDim.x) {
-      const int kk = idx >> 5, rr = idx & 31;
-      const int64_t k = kc + kk, row = r0 + rr;
-      const int sh = s_shift[rr];
-      double v = 0.0;
-      if (row < rows && k < K && sh != kShiftNonFinite)
-        v = ds_value(o, b * o.s_b + row * o.s_r + k * o.s_k);
-      tile[kk][rr] = rint(scale2(v, sh == kShiftNonFinite ? 0 : sh));
-    }
-    __syncthreads();
-    Limbs x[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const long long t = __double2ll_rn(tile[my_grp * 16 + j][my_row]);
-      x[j] = Limbs{static_cast<int>(t >> 32), static_cast<int>((t >> 16) & 0xFFFF),
-                   static_cast<int>(t & 0xFFFF)};
-    }
-    const int64_t row = r0 + my_row;
-    if (row < rows_pad)
-      store_all_planes(x, planes + (static_cast<size_t>(b) * rows_pad + row) * Kp + kc + my_grp * 16,
-                       plane_stride);
-    __syncthreads();
+  for (int idx = threadIdx.x; idx < kTileK * 32; idx += blockDim.x) {
+    const int kk = idx >> 5, rr = idx & 31;
+    const int64_t k = kc + kk, row = r0 + rr;
+    const int sh = s_shift[rr];
+    const bool use = row < rows && k < K && sh != kShiftNonFinite;
+    const double v = use ? op_value(o, b * o.s_b + row * o.s_r + k * o.s_k) : 0.0;
+    tile[kk][rr] = quantise(v, use ? sh : 0);
   }
+  __syncthreads();
+  const int my_row = threadIdx.x >> 3, my_grp = threadIdx.x & 7;
+  Limbs x[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) x[j] = limbs_of(tile[my_grp * 16 + j][my_row]);
+  const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
+  store_all_planes(x, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
+                          my_grp * 16,
+                   plane_stride);
 }
 
 // ---------------------------------------------------------------------------
@@ -407,8 +437,9 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   return d;
 }
 
-// kind::i8, D = s32, A = B = signed 8-bit, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+// kind::i8, D = s32, A = B = unsigned 8-bit (residues in [0, m)), both
+// K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (2u << 4) | (0u << 7) | (0u << 10) |
                             (static_cast<uint32_t>(kTileN >> 3) << 17) |
                             (static_cast<uint32_t>(kTileM >> 4) << 24);
 
@@ -671,50 +702,67 @@ __device__ __forceinline__ void put_result(const DotResult& c, int64_t idx, doub
   }
 }
 
-__global__ void __launch_bounds__(256)
+constexpr int kCrtThreads = 128;
+constexpr int kCrtCols = 8;  // consecutive outputs per thread
+
+// blockIdx.y strides over the batch*M output rows, blockIdx.x * 1024 is the
+// first column of the block; each thread rebuilds 8 consecutive outputs from
+// one 8-byte load per residue plane.
+__global__ void __launch_bounds__(kCrtThreads)
 crt_kernel(CrtParams p) {
-  const int64_t per_b = p.M * p.N;
-  const int64_t total = p.batch * per_b;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += stride) {
-    const int64_t b = idx / per_b;
-    const int64_t rem = idx - b * per_b;
-    const int64_t i = rem / p.N, j = rem - i * p.N;
-    const int sa = p.sa[b * p.Mp + i], sb = p.sb[b * p.Np + j];
-    double out;
-    if (failed) {
-      out = __longlong_as_double(0x7ff8000000000000LL);
-    } else if (sa == kShiftNonFinite || sb == kShiftNonFinite) {
-      // A non-finite operand: the IEEE sum of the DS-valued products carries
-      // NaN/Inf exactly as a float GEMM would.
-      double s = 0.0;
-      for (int64_t k = 0; k < p.K; ++k)
-        s += ds_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
-             ds_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
-      out = s;
-    } else {
-      const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j;
-      double s0 = 0.0, s1 = 0.0, s2 = 0.0;
+  const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCrtCols;
+  if (j0 >= p.N) return;
+  const int64_t rows_total = p.batch * p.M;
+  for (int64_t row = blockIdx.y; row < rows_total; row += gridDim.y) {
+    const int64_t b = row / p.M, i = row - b * p.M;
+    const int sa = p.sa[b * p.Mp + i];
+    const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
+    double s0[kCrtCols], s1[kCrtCols], s2[kCrtCols];
 #pragma unroll
-      for (int l = 0; l < kL; ++l) {
-        const double r = static_cast<double>(p.cres[l * plane + at]);
-        s0 = __fma_rn(r, p.w[l][0], s0);
-        s1 = __fma_rn(r, p.w[l][1], s1);
-        s2 = __fma_rn(r, p.w[l][2], s2);
+    for (int q = 0; q < kCrtCols; ++q) s0[q] = s1[q] = s2[q] = 0.0;
+#pragma unroll
+    for (int l = 0; l < kL; ++l) {
+      const uint2 v = *reinterpret_cast<const uint2*>(p.cres + l * plane + at);
+      const double w0 = p.w[l][0], w1 = p.w[l][1], w2 = p.w[l][2];
+#pragma unroll
+      for (int q = 0; q < kCrtCols; ++q) {
+        const uint32_t word = q < 4 ? v.x : v.y;
+        const double r = static_cast<double>((word >> (8 * (q & 3))) & 0xFFu);
+        s0[q] = __fma_rn(r, w0, s0[q]);
+        s1[q] = __fma_rn(r, w1, s1[q]);
+        s2[q] = __fma_rn(r, w2, s2[q]);
       }
-      const double approx = __fma_rn(s2, 0x1p80, s1 * 0x1p40);
-      const double q = rint(approx * p.inv_m);
-      const double t0 = __fma_rn(-q, p.mlimb[0], s0);
-      const double t1 = __fma_rn(-q, p.mlimb[1], s1);
-      const double t2 = __fma_rn(-q, p.mlimb[2], s2);
-      const double hi = __fma_rn(t2, 0x1p40, t1);
-      const double cint = __fma_rn(hi, 0x1p40, t0);
-      out = scale2(scale2(cint, -sa), -sb);
     }
-    put_result(p.c, idx, out);
+#pragma unroll
+    for (int q = 0; q < kCrtCols; ++q) {
+      const int64_t j = j0 + q;
+      if (j >= p.N) break;
+      const int sb = p.sb[b * p.Np + j];
+      double out;
+      if (failed) {
+        out = __longlong_as_double(0x7ff8000000000000LL);
+      } else if (sa == kShiftNonFinite || sb == kShiftNonFinite) {
+        // A non-finite operand: the IEEE sum of the products carries NaN/Inf
+        // as a float GEMM would.
+        double s = 0.0;
+        for (int64_t k = 0; k < p.K; ++k)
+          s += op_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
+               op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
+        out = s;
+      } else {
+        // C = S - round(S / Mprod) * Mprod, limb by limb (every term exact).
+        const double approx = __fma_rn(s2[q], 0x1p80, s1[q] * 0x1p40);
+        const double qt = rint(approx * p.inv_m);
+        const double t0 = __fma_rn(-qt, p.mlimb[0], s0[q]);
+        const double t1 = __fma_rn(-qt, p.mlimb[1], s1[q]);
+        const double t2 = __fma_rn(-qt, p.mlimb[2], s2[q]);
+        const double hi = __fma_rn(t2, 0x1p40, t1);
+        out = scale2(scale2(__fma_rn(hi, 0x1p40, t0), -sa), -sb);
+      }
+      put_result(p.c, row * p.N + j, out);
+    }
   }
 }
 
@@ -753,14 +801,18 @@ size_t gemm_smem_bytes() {
 }
 
 int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
-                 int64_t Kp, int P, int8_t* planes, int* shifts, cudaStream_t s) {
+                 int64_t Kp, int P, uint8_t* planes, int* shifts, int* codes, cudaStream_t s) {
   if (o.s_k == 1 || rows == 1) {
     dim3 grid(static_cast<unsigned>(rows_pad), static_cast<unsigned>(batch));
     split_kmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes, shifts);
   } else {
-    dim3 grid(static_cast<unsigned>((rows_pad + 31) / 32), static_cast<unsigned>(batch));
-    split_rowmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes,
-                                               shifts);
+    DSB_CUDA_TRY(cudaMemsetAsync(codes, 0, sizeof(int) * batch * rows_pad, s));
+    dim3 g1(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>((K + 255) / 256),
+            static_cast<unsigned>(batch));
+    colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
+    dim3 g2(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>(Kp / kTileK),
+            static_cast<unsigned>(batch));
+    split_cols_kernel<<<g2, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
   }
   return launch_status();
 }
@@ -801,19 +853,23 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   if (attr_err != cudaSuccess) return cuda_status(attr_err);
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int8_t* planes_a = reinterpret_cast<int8_t*>(ws + g.off_a);
-  int8_t* planes_b = reinterpret_cast<int8_t*>(ws + g.off_b);
+  uint8_t* planes_a = ws + g.off_a;
+  uint8_t* planes_b = ws + g.off_b;
   uint8_t* cres = ws + g.off_c;
   int* sa = reinterpret_cast<int*>(ws + g.off_sa);
   int* sb = reinterpret_cast<int*>(ws + g.off_sb);
+  int* ca = reinterpret_cast<int*>(ws + g.off_ca);
+  int* cb = reinterpret_cast<int*>(ws + g.off_cb);
   int* err = reinterpret_cast<int*>(ws + g.off_err);
   const int P = bits_for_k(p.K);
 
   DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
   {
     ProfileScope prof("ozaki_split", s);
-    if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, s)) return st;
-    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, s)) return st;
+    if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
+      return st;
+    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, cb, s))
+      return st;
   }
 
   CUtensorMap ta, tb;
@@ -855,7 +911,10 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   cp.b = p.b;
   cp.c = p.c;
   ProfileScope prof("ozaki_crt", s);
-  crt_kernel<<<grid_for(p.batch * p.M * p.N, 256, 8), 256, 0, s>>>(cp);
+  const int64_t rows_total = p.batch * p.M;
+  dim3 cg(static_cast<unsigned>((p.N + kCrtThreads * kCrtCols - 1) / (kCrtThreads * kCrtCols)),
+          static_cast<unsigned>(rows_total < 65535 ? rows_total : 65535));
+  crt_kernel<<<cg, kCrtThreads, 0, s>>>(cp);
   return launch_status();
 }
 

@@ -9,6 +9,8 @@
 //     and a block tree combine threads, and block partials go to the caller's
 //     workspace; a one-block kernel folds the partials with the same fixed
 //     tree and applies init.  With one block the first kernel finishes alone.
+//     For f64 input with an add/subtract body the per-thread fold is an
+//     exact f64 two_sum of the inputs (see reduce_full_kernel).
 //   - inner == 1, outer > 1: one block per row.
 //   - inner > 1: one thread per (outer, inner) column, folding `red`
 //     elements in order (coalesced across the inner index).
@@ -105,7 +107,22 @@ __device__ __forceinline__ ds2 load_init(const double* init_f64, const float* in
   return init_f64 ? from_f64(*init_f64) : ds2{*init_hi, *init_lo};
 }
 
+// Knuth two_sum in f64: s + c += x with the rounding error of s + x kept in c.
+__device__ __forceinline__ void two_sum_acc(double& s, double& c, double x) {
+  const double t = __dadd_rn(s, x);
+  const double bp = __dsub_rn(t, s);
+  c = __dadd_rn(c, __dadd_rn(__dsub_rn(s, __dsub_rn(t, bp)), __dsub_rn(x, bp)));
+  s = t;
+}
+
 // Full reduction, stage 1.
+//
+// f64 input with an add/subtract body: every thread sums its elements
+// exactly in f64 (two_sum, the rounding errors carried in a second f64), and
+// its partial enters the DS trees as the DS split of that sum.  This adds the
+// f64 inputs themselves -- splitting each into (hi, lo) first would only add
+// a rounding per element -- with no f64->f32 conversion per element.  Other
+// inputs and the multiply body fold DS pairs.
 __global__ void __launch_bounds__(kThreads)
 reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
                    const double* init_f64, const float* init_hi, const float* init_lo) {
@@ -113,7 +130,27 @@ reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
   ds2 acc = identity(is_mul);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (src.vec) {
+  if (src.f64 && !is_mul && src.vec) {
+    double s0 = 0.0, c0 = 0.0, s1 = 0.0, c1 = 0.0;
+    const int64_t npairs = n >> 1;
+    const double2* p2 = reinterpret_cast<const double2*>(src.f64);
+    for (int64_t base = tid; base < npairs; base += stride * kUnroll) {
+      double2 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t p = base + u * stride;
+        v[u] = p < npairs ? __ldcs(p2 + p) : make_double2(0.0, 0.0);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        two_sum_acc(s0, c0, v[u].x);
+        two_sum_acc(s1, c1, v[u].y);
+      }
+    }
+    if ((n & 1) && tid == 0) two_sum_acc(s0, c0, src.f64[n - 1]);
+    two_sum_acc(s0, c0, s1);
+    acc = from_f64(__dadd_rn(s0, __dadd_rn(c0, c1)));
+  } else if (src.vec) {
     const int64_t npairs = n >> 1;
     for (int64_t base = tid; base < npairs; base += stride * kUnroll) {
       ds2 x0[kUnroll], x1[kUnroll];
