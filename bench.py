@@ -232,7 +232,8 @@ def run_ours(args):
     fam = "ozaki_gemm"
     k_ms, k_n = _lib.profile_read(fam)
     launches = {}
-    for f in ("ozaki_split", "ozaki_gemm", "ozaki_crt", "dot_simt", "dot_vec", "elementwise",
+    for f in ("ozaki_split", "ozaki_split_rows", "ozaki_split_cols", "ozaki_gemm", "ozaki_crt",
+              "dot_simt", "dot_vec", "elementwise",
               "reduce", "recurrence"):
         t, n = _lib.profile_read(f)
         if n:
@@ -387,6 +388,197 @@ def secondary_metrics(dev):
     return out
 
 
+STREAM_METRICS = {
+    "fused_add_mul": ("DS fused (a+b)*c -> f64 HBM GB/s", "GB/s"),
+    "reduce": ("DS sum of f64 HBM GB/s", "GB/s"),
+    "recurrence": ("DS recurrence x<-x*a+b Gelem-iter/s", "Gelem-iter/s"),
+}
+REC_KS = (1, 4, 16, 64, 256, 1024)
+
+
+def stream_inputs(workload, n, rank):
+    """Seeded inputs of the stream configs (rank r > 0 draws its own shard)."""
+    if workload == "fused_add_mul":     # config 1 distribution, seed 0
+        rng = np.random.default_rng(0 if rank == 0 else (0, rank))
+        return [rng.uniform(-1, 1, n) for _ in range(3)]
+    if workload == "reduce":            # config 2: +-1e8 alternating + U[0,1)*1e-3, seed 1
+        s = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)
+        rng = np.random.default_rng(1 if rank == 0 else (1, rank))
+        return [s * 1e8 + rng.uniform(0, 1, n) * 1e-3]
+    rng = np.random.default_rng(3 if rank == 0 else (3, rank))   # config 4, seed 3
+    x0 = rng.uniform(-1, 1, n)
+    a = rng.uniform(0.999, 1.001, n)
+    b = rng.uniform(-1e-3, 1e-3, n)
+    return [x0, a, b]
+
+
+def run_stream(args):
+    """--workload fused_add_mul | reduce | recurrence: the HBM-bound DS ops.
+
+    Every rank processes its own n elements (weak scaling); the reduce adds
+    the ranks' (hi, lo) partials with one all-gather.  Inputs are 2^26
+    elements per rank by default (>= 512 MiB, above L2); the recurrence uses
+    the config's 2^24 and sweeps k.
+    """
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from ds_b200 import _lib, ops
+    from ds_b200 import dist as dsd
+    wl = args.workload
+    n = args.n or (1 << 24 if wl == "recurrence" else 1 << 26)
+    host_in = stream_inputs(wl, n, rank)
+    dev_in = [torch.from_numpy(v).to(dev) for v in host_in]
+    peaks, peak_src = measured_peaks()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps, profile=False):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize()
+        if profile:
+            _lib.profile_reset()
+            _lib.profile_enable(True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            out = fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps), out
+
+    line = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32x2 (DS) from f64", "data": "synthetic (numpy default_rng, as the configs)"}
+    metric, unit = STREAM_METRICS[wl]
+    line["metric"], line["unit"] = metric, unit
+    clocks = ClockSampler(local)
+    if wl in ("fused_add_mul", "reduce"):
+        if wl == "fused_add_mul":
+            a, b, c = dev_in
+            fn = lambda: ops.ds_fused_add_mul3_to_f64(a, b, c)  # noqa: E731
+            bpe, fam = 32.0, "elementwise"
+        else:
+            x = dev_in[0]
+            fn = (lambda: dsd.ds_sum_f64_sharded(x)) if world > 1 else (lambda: ops.ds_sum_f64(x))
+            bpe, fam = 8.0, "reduce"
+        clocks.start()
+        ms, out = timed(fn, args.steps, profile=True)
+        clk = clocks.stop()
+        _lib.profile_enable(False)
+        k_ms, k_n = _lib.profile_read(fam)
+        per = k_ms / max(k_n, 1)
+        achieved = bpe * n / (per * 1e-3) / 1e9
+        line.update({
+            "value": round(world * bpe * n / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
+            "config": {"workload": f"{wl} n={n} per rank", "bytes_per_elem": bpe,
+                       "l2": "inputs exceed the 126 MB L2" if bpe * n > 126e6 else
+                             "fits in L2 (no flush)"},
+            "roofline": {"bound": "hbm", "kernel": fam, "achieved": round(achieved, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "traffic": ncu_traffic(fam, f"{wl}{n}"),
+                         "peak_source": f"{peak_src} hbm_gbs",
+                         "kernel_ms_per_launch": round(per, 4)},
+            "gpu_launches": int(k_n), "clocks": clk})
+        if rank == 0:
+            got = out.cpu().numpy()
+            from oracle import dso, exact
+            if wl == "fused_add_mul":
+                m = min(n, 1 << 22)
+                want = dso.ds_fused_add_mul3_to_f64(*(v[:m] for v in host_in), dso.max_threads())
+                line["accuracy"] = {"bit_exact_vs_oracle_first_2^22": bool(
+                    np.array_equal(got[:m].view(np.uint64), want.view(np.uint64)))}
+            elif world == 1:
+                truth = exact.exact_sum(host_in[0])
+                h, l = dso.ds_reduce_f64_seq(host_in[0])
+                line["accuracy"] = {"abs_err_vs_fsum": abs(float(got) - truth),
+                                    "reference_ds_seq_abs_err": abs(float(h) + float(l) - truth)}
+    else:
+        x0, a, b = dev_in
+        sweep = []
+        for k in REC_KS:
+            fn = lambda k=k: ops.ds_recurrence_mul_add_to_f64(x0, a, b, k)  # noqa: E731
+            steps = max(1, min(args.steps, int(2000 / max(k, 1))))
+            ms, out = timed(fn, steps)
+            sweep.append({"k": k, "ms": round(ms, 4),
+                          "GB/s": round(32.0 * n / (ms * 1e-3) / 1e9, 1),
+                          "Gelem_iter_per_s": round(world * n * k / (ms * 1e-3) / 1e9, 2)})
+        last = sweep[-1]
+        line.update({"value": last["Gelem_iter_per_s"], "ms_per_step": last["ms"],
+                     "config": {"workload": f"recurrence x<-x*a+b n={n} per rank, k sweep",
+                                "k": list(REC_KS)},
+                     "sweep": sweep,
+                     "roofline": {"bound": "hbm", "kernel": "recurrence",
+                                  "achieved": sweep[0]["GB/s"], "peak": peaks["hbm_gbs"],
+                                  "unit": "GB/s",
+                                  "frac": round(sweep[0]["GB/s"] / peaks["hbm_gbs"], 4),
+                                  "traffic": None, "note": "k=1 (HBM-bound end of the sweep)"},
+                     "gpu_launches": len(REC_KS)})
+        if rank == 0:
+            from oracle import dso
+            m = 1 << 16
+            got = out[:m].cpu().numpy()
+            want = dso.ds_recurrence_mul_add_to_f64(x0[:m].cpu().numpy(), a[:m].cpu().numpy(),
+                                                    b[:m].cpu().numpy(), REC_KS[-1],
+                                                    dso.max_threads())
+            line["accuracy"] = {"bit_exact_vs_oracle_first_2^16_k1024": bool(
+                np.array_equal(got.view(np.uint64), want.view(np.uint64)))}
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline_stream(wl, host_in)
+    if world > 1:
+        dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+def cpu_baseline_stream(wl, host_in, threads=None):
+    """The reference CPU ops (C oracle, OpenMP over the host cores) on a
+    bounded sample of the same inputs."""
+    from oracle import dso
+    threads = threads or dso.max_threads()
+    if wl == "fused_add_mul":
+        m = min(host_in[0].size, 1 << 24)
+        fn = lambda: dso.ds_fused_add_mul3_to_f64(*(v[:m] for v in host_in), threads)  # noqa
+        bpe, unit, count = 32.0, "GB/s", m
+        sample = f"{m} elements of (a+b)*c"
+    elif wl == "reduce":
+        m = min(host_in[0].size, 1 << 24)
+        fn = lambda: dso.ds_reduce_f64_seq(host_in[0][:m])  # noqa: E731
+        bpe, unit, count, threads = 8.0, "GB/s", m, 1
+        sample = f"sequential DS fold of {m} elements (the reference reduce body in order)"
+    else:
+        m = 1 << 18
+        fn = lambda: dso.ds_recurrence_mul_add_to_f64(*(v[:m] for v in host_in), 1024, threads)  # noqa
+        bpe, unit, count = None, "Gelem-iter/s", m * 1024
+        sample = f"{m} elements, k=1024"
+    fn()
+    t = time.perf_counter()
+    fn()
+    dt = time.perf_counter() - t
+    value = bpe * count / dt / 1e9 if bpe else count / dt / 1e9
+    return {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
+            "sample": sample}
+
+
 REF_ROWS = 1024  # rows of A per reference step (a quarter of the GEMM)
 
 
@@ -425,6 +617,27 @@ def run_reference(args):
     }
 
 
+def run_reference_stream(args):
+    """Reference arm of the stream workloads: the reference CPU ops (C oracle)
+    on the host cores, one bounded sample per step (rank 0 only)."""
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return None
+    wl = args.workload
+    n = args.n or (1 << 24 if wl == "recurrence" else 1 << 26)
+    host_in = stream_inputs(wl, min(n, 1 << 24), 0)
+    vals = [cpu_baseline_stream(wl, host_in) for _ in range(max(1, min(args.steps, 5)))]
+    value = statistics.median(v["value"] for v in vals)
+    metric, unit = STREAM_METRICS[wl]
+    cb = dict(vals[0], value=value)
+    return {"impl": "reference", "metric": metric, "value": value, "unit": unit,
+            "n_gpus": world, "steps": len(vals), "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "config": {"workload": f"{wl} (bounded host sample)"}, "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -437,10 +650,17 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--kernels-only", action="store_true",
                     help="time the device steps only (the case used for ncu captures)")
+    ap.add_argument("--n", type=int, default=0,
+                    help="elements per rank for the stream workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.workload not in ("gemm",) + tuple(STREAM_METRICS):
+        raise SystemExit(f"unknown workload {args.workload!r}")
+    if args.impl == "reference":
+        line = run_reference(args) if args.workload == "gemm" else run_reference_stream(args)
+    else:
+        line = run_ours(args) if args.workload == "gemm" else run_stream(args)
     if line is not None:
         print(json.dumps(line))
 

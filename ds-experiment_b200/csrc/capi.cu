@@ -250,6 +250,14 @@ const char* ds_last_error(void) { return g_last_error.c_str(); }
 
 const char* ds_version(void) { return "ds_b200 0.1 (sm_100a)"; }
 
+int ds_dot_tensor_kernel_info(int32_t* cta_pairs, int32_t* query_error) {
+  int p = 0, e = 0;
+  const int st = dot_ozaki_kernel_info(&p, &e);
+  if (cta_pairs) *cta_pairs = p;
+  if (query_error) *query_error = e;
+  return st;
+}
+
 int ds_dot_tensor_plan(int64_t K, int32_t* moduli, int32_t* bits) {
   if (K < 1) return invalid("ds_dot_tensor_plan: K must be positive");
   int m = 0, b = 0;

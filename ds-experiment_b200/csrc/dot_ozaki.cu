@@ -40,7 +40,9 @@
 #include <climits>
 #include <cmath>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "ds_arith.cuh"
@@ -126,7 +128,7 @@ Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
   g.M = M;
   g.N = N;
   g.K = K;
-  g.Mp = round_up(M, kTileM);
+  g.Mp = round_up(M, 2 * kTileM);  // 256: one tile of a CTA pair
   g.Np = round_up(N, kTileN);
   g.Kp = round_up(K < 1 ? 1 : K, kTileK);
   size_t off = 0;
@@ -219,6 +221,26 @@ __device__ __forceinline__ void store_all_planes(const Limbs (&x)[16], uint8_t* 
   }
 }
 
+// The same for N = 4 or 8 consecutive values (one 4- or 8-byte store).
+template <int N, int l = 0>
+__device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* base,
+                                               size_t plane_stride) {
+  if constexpr (l < kL) {
+    uint32_t w[N / 4];
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q)
+      w[q] = residue<l>(x[q * 4]) | (residue<l>(x[q * 4 + 1]) << 8) |
+             (residue<l>(x[q * 4 + 2]) << 16) | (residue<l>(x[q * 4 + 3]) << 24);
+    uint8_t* dst = base + l * plane_stride;
+    if constexpr (N == 4) {
+      *reinterpret_cast<uint32_t*>(dst) = w[0];
+    } else {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    }
+    store_planes_n<N, l + 1>(x, base, plane_stride);
+  }
+}
+
 __device__ __forceinline__ int shift_for(double mx, bool nonfinite, int P) {
   if (nonfinite) return kShiftNonFinite;
   if (mx == 0.0) return 0;
@@ -275,17 +297,32 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   const int shift = live ? shift_for(mx, bad, P) : 0;
   if (threadIdx.x == 0) shifts[b * rows_pad + r] = shift;
   const bool zero = !live || shift == kShiftNonFinite;
+  const int sh = zero ? 0 : shift;
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
   uint8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
-  for (int64_t k0 = static_cast<int64_t>(threadIdx.x) * 16; k0 < Kp; k0 += 16 * blockDim.x) {
-    Limbs x[16];
+  // Four consecutive k per thread: two 16-byte loads (f64, aligned rows) and
+  // one 4-byte store per plane, both coalesced across the warp.
+  const bool vec = o.f64 && o.s_k == 1 && (reinterpret_cast<uintptr_t>(o.f64 + base) & 15) == 0;
+  for (int64_t k0 = static_cast<int64_t>(threadIdx.x) * 4; k0 < Kp; k0 += 4 * blockDim.x) {
+    double v[4];
+    if (!zero && vec && k0 + 4 <= K) {
+      const double2* p = reinterpret_cast<const double2*>(o.f64 + base + k0);
+      const double2 v01 = p[0], v23 = p[1];
+      v[0] = v01.x;
+      v[1] = v01.y;
+      v[2] = v23.x;
+      v[3] = v23.y;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int64_t k = k0 + j;
-      const double v = (zero || k >= K) ? 0.0 : op_value(o, base + k * o.s_k);
-      x[j] = limbs_of(quantise(v, zero ? 0 : shift));
+      for (int j = 0; j < 4; ++j) {
+        const int64_t k = k0 + j;
+        v[j] = (zero || k >= K) ? 0.0 : op_value(o, base + k * o.s_k);
+      }
     }
-    store_all_planes(x, row_out + k0, plane_stride);
+    Limbs x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(v[j], sh));
+    store_planes_n<4>(x, row_out + k0, plane_stride);
   }
 }
 
@@ -323,17 +360,19 @@ colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
   }
 }
 
-// Pass 2: one block per (32 rows, 128 K) tile: values are quantised into a
+// Pass 2: one block per (32 rows, 64 K) tile: values are quantised into a
 // shared-memory tile (loads coalesced along rows), then written transposed
-// (K-major), 16 residues per thread per modulus.
+// (K-major), 8 residues per thread per modulus.
+constexpr int kColTileK = 64;
+
 __global__ void __launch_bounds__(256)
 split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
                   int64_t batch, int P, const int* __restrict__ codes,
                   uint8_t* __restrict__ planes, int* __restrict__ shifts) {
-  __shared__ uint64_t tile[kTileK][33];
+  __shared__ uint64_t tile[kColTileK][33];
   __shared__ int s_shift[32];
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, b = blockIdx.z;
-  const int64_t kc = static_cast<int64_t>(blockIdx.y) * kTileK;
+  const int64_t kc = static_cast<int64_t>(blockIdx.y) * kColTileK;
   if (threadIdx.x < 32) {
     const int64_t r = r0 + threadIdx.x;
     const int sh = r < rows ? shift_from_code(codes[b * rows_pad + r], P) : 0;
@@ -341,7 +380,8 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
     if (blockIdx.y == 0) shifts[b * rows_pad + r] = sh;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < kTileK * 32; idx += blockDim.x) {
+#pragma unroll 4
+  for (int idx = threadIdx.x; idx < kColTileK * 32; idx += blockDim.x) {
     const int kk = idx >> 5, rr = idx & 31;
     const int64_t k = kc + kk, row = r0 + rr;
     const int sh = s_shift[rr];
@@ -351,13 +391,13 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
   }
   __syncthreads();
   const int my_row = threadIdx.x >> 3, my_grp = threadIdx.x & 7;
-  Limbs x[16];
+  Limbs x[8];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) x[j] = limbs_of(tile[my_grp * 16 + j][my_row]);
+  for (int j = 0; j < 8; ++j) x[j] = limbs_of(tile[my_grp * 8 + j][my_row]);
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  store_all_planes(x, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
-                          my_grp * 16,
-                   plane_stride);
+  store_planes_n<8>(x, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
+                           my_grp * 8,
+                    plane_stride);
 }
 
 // ---------------------------------------------------------------------------
@@ -676,6 +716,287 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
   }
 }
 
+// ---- CTA-pair variant (tcgen05 cta_group::2) ---------------------------------
+//
+// A cluster of two CTAs computes 256x256 tiles.  Each CTA stages its own 128
+// rows of A and its 128-row half of the B tile (16 + 16 KB per K-block
+// instead of 16 + 32 KB), the even CTA issues tcgen05.mma.cta_group::2
+// M=256 N=256 K=32 over both CTAs' shared memory, and each CTA drains its
+// own 128 rows from its own TMEM.  Both CTAs' TMA loads complete on the even
+// CTA's "full" barrier (addressed with mapa); the MMA commits arrive on both
+// CTAs' "empty" / "tmem full" barriers (commit multicast); every epilogue warp
+// of the pair arrives on the even CTA's "tmem empty" barrier.  No load uses
+// multicast.
+
+constexpr int kStages2 = 6;
+constexpr int kStage2 = kTileM * kTileK;  // 16 KB: A rows, or half of the B tile
+constexpr uint32_t kIdesc2 = (2u << 4) | (0u << 7) | (0u << 10) | ((256u >> 3) << 17) |
+                             ((256u >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same variable in CTA rank 0 of the cluster.
+__device__ __forceinline__ uint32_t in_rank0(const void* p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __noinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate));
+}
+
+// Arrive (when the prior MMAs complete) on the barrier at this address in
+// both CTAs of the pair.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_self(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + kStages2 * kStage2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages2 * kStage2);
+  uint64_t* empty = full + kStages2;
+  uint64_t* tfull = empty + kStages2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drained = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each of the 2 CTAs
+    }
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int64_t cid = cluster_id_x(), ncl = nclusters_x();
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs) ----
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t u = cid; u < p.units && ok; u += ncl) {
+        const Unit w = unit_of(u, p);
+        const int ya = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
+                                        static_cast<int64_t>(w.tm) * 256 + rank * 128);
+        const int yb = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Np +
+                                        static_cast<int64_t>(w.tn) * 256 + rank * 128);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 11)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[stage], 4 * kStage2);
+          const uint32_t full0 = in_rank0(&full[stage]);
+          tma_load_2d_pair(smem_a + stage * kStage2, &tmap_a, kb * kTileK, ya, full0);
+          tma_load_2d_pair(smem_b + stage * kStage2, &tmap_b, kb * kTileK, yb, full0);
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 200000) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (even CTA only) ----
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t u = cid; u < p.units && ok; u += ncl) {
+        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.err, 12)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * 256);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem_a + stage * kStage2);
+          const uint32_t b0 = smem_u32(smem_b + stage * kStage2);
+#pragma unroll
+          for (int k = 0; k < kTileK / 32; ++k) {
+            mma_i8_pair(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32), (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[stage]);
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      mma_commit_pair_self(drained);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drained, 0) && clock64() - t0 < kTimeoutCycles) {
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs; warps 2..5, TMEM lanes 32*(warp%4) ..) ----
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t tempty0[2] = {in_rank0(&tempty[0]), in_rank0(&tempty[1])};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t u = cid; u < p.units; u += ncl) {
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, 14)) break;
+      tc_fence_after();
+      const Unit w = unit_of(u, p);
+      const int m = mod_of(w.l);
+      const double inv_m = 1.0 / static_cast<double>(m);
+      const int64_t row = (static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
+                          static_cast<int64_t>(w.tm) * 256 + rank * 128 + row_in_tile;
+      uint8_t* out = p.cres + row * p.Np + static_cast<int64_t>(w.tn) * 256;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * 256);
+#pragma unroll 1
+      for (int c0 = 0; c0 < 256; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tbase + c0, v);
+        uint32_t packed[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            word |= mod_u8(static_cast<int>(v[q * 4 + j]), m, inv_m) << (8 * j);
+          packed[q] = word;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + c0);
+        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty0[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Step 3: CRT reconstruction and scaling.
 
@@ -729,6 +1050,8 @@ crt_kernel(CrtParams p) {
 #pragma unroll
       for (int q = 0; q < kCrtCols; ++q) {
         const uint32_t word = q < 4 ? v.x : v.y;
+        // (the integer -> f64 conversions run on the XU pipe, beside the
+        // FP64 FMAs)
         const double r = static_cast<double>((word >> (8 * (q & 3))) & 0xFFu);
         s0[q] = __fma_rn(r, w0, s0[q]);
         s1[q] = __fma_rn(r, w1, s1[q]);
@@ -800,17 +1123,77 @@ size_t gemm_smem_bytes() {
   return 1024 + kStages * (kStageA + kStageB) + (2 * kStages + 5) * sizeof(uint64_t) + 16;
 }
 
+size_t gemm2_smem_bytes() {
+  return 1024 + 2 * kStages2 * kStage2 + (2 * kStages2 + 5) * sizeof(uint64_t) + 16;
+}
+
+// Kernel choice and per-device launch limits, set up once per device.
+struct GemmSetup {
+  cudaError_t err = cudaSuccess;
+  int pair_clusters = 0;  // co-resident CTA pairs (0: use the one-CTA kernel)
+  int query_error = 0;    // cudaError_t of the cluster occupancy query
+};
+
+const GemmSetup& gemm_setup() {
+  static std::mutex mu;
+  static std::vector<GemmSetup> by_device;
+  static std::vector<bool> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(by_device.size())) {
+    by_device.resize(dev + 1);
+    done.resize(dev + 1, false);
+  }
+  if (!done[dev]) {
+    GemmSetup g;
+    g.err = cudaFuncSetAttribute(ozaki_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(gemm_smem_bytes()));
+    if (g.err == cudaSuccess)
+      g.err = cudaFuncSetAttribute(ozaki_gemm2_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(gemm2_smem_bytes()));
+    const char* one = std::getenv("DS_B200_GEMM_1CTA");
+    if (g.err == cudaSuccess && !(one && one[0] == '1')) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * 74);
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = gemm2_smem_bytes();
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      const cudaError_t qe = cudaOccupancyMaxActiveClusters(&n, ozaki_gemm2_kernel, &cfg);
+      if (qe == cudaSuccess) {
+        g.pair_clusters = n;
+      } else {
+        g.query_error = static_cast<int>(qe);
+        cudaGetLastError();  // fall back to the one-CTA kernel
+      }
+    }
+    by_device[dev] = g;
+    done[dev] = true;
+  }
+  return by_device[dev];
+}
+
 int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
                  int64_t Kp, int P, uint8_t* planes, int* shifts, int* codes, cudaStream_t s) {
   if (o.s_k == 1 || rows == 1) {
+    ProfileScope prof("ozaki_split_rows", s);
     dim3 grid(static_cast<unsigned>(rows_pad), static_cast<unsigned>(batch));
     split_kmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes, shifts);
   } else {
+    ProfileScope prof("ozaki_split_cols", s);
     DSB_CUDA_TRY(cudaMemsetAsync(codes, 0, sizeof(int) * batch * rows_pad, s));
     dim3 g1(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>((K + 255) / 256),
             static_cast<unsigned>(batch));
     colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
-    dim3 g2(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>(Kp / kTileK),
+    dim3 g2(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>(Kp / kColTileK),
             static_cast<unsigned>(batch));
     split_cols_kernel<<<g2, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
   }
@@ -833,6 +1216,13 @@ int dot_ozaki_params(int64_t K, int* moduli, int* bits) {
   return DS_OK;
 }
 
+int dot_ozaki_kernel_info(int* cta_pairs, int* query_error) {
+  const GemmSetup& g = gemm_setup();
+  if (cta_pairs) *cta_pairs = g.pair_clusters;
+  if (query_error) *query_error = g.query_error;
+  return g.err == cudaSuccess ? DS_OK : cuda_status(g.err);
+}
+
 int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   if (p.batch == 0 || p.M == 0 || p.N == 0) return ok();
   const Layout g = layout_of(p.batch, p.M, p.N, p.K);
@@ -844,13 +1234,9 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   if (p.batch > 65535 || kL * p.batch * g.Mp > max_rows || kL * p.batch * g.Np > max_rows ||
       g.Kp > max_rows)
     return set_error(DS_INVALID_ARGUMENT, "dot_general: problem too large for the tensor-core path");
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(ozaki_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(gemm_smem_bytes()));
-  });
-  if (attr_err != cudaSuccess) return cuda_status(attr_err);
+  const GemmSetup& setup = gemm_setup();
+  if (setup.err != cudaSuccess) return cuda_status(setup.err);
+  const bool pair = setup.pair_clusters > 0;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint8_t* planes_a = ws + g.off_a;
@@ -874,10 +1260,12 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
 
   CUtensorMap ta, tb;
   if (int st = make_tmap(&ta, planes_a, g.Kp, kL * p.batch * g.Mp, kTileM)) return st;
-  if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np, kTileN)) return st;
+  // The pair kernel loads half of each 256-row B tile per CTA.
+  if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np, pair ? kTileN / 2 : kTileN))
+    return st;
   GemmParams gp{};
   gp.batch = static_cast<int>(p.batch);
-  gp.tiles_m = static_cast<int>(g.Mp / kTileM);
+  gp.tiles_m = static_cast<int>(g.Mp / (pair ? 2 * kTileM : kTileM));
   gp.tiles_n = static_cast<int>(g.Np / kTileN);
   gp.kblocks = static_cast<int>(g.Kp / kTileK);
   gp.Mp = g.Mp;
@@ -885,10 +1273,27 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   gp.units = static_cast<int64_t>(kL) * p.batch * gp.tiles_m * gp.tiles_n;
   gp.cres = cres;
   gp.err = err;
-  const int grid = static_cast<int>(gp.units < sm_count() ? gp.units : sm_count());
   {
     ProfileScope prof("ozaki_gemm", s);
-    ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), s>>>(ta, tb, gp);
+    if (pair) {
+      const int64_t clusters = gp.units < setup.pair_clusters ? gp.units : setup.pair_clusters;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = gemm2_smem_bytes();
+      cfg.stream = s;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel, ta, tb, gp));
+    } else {
+      const int grid = static_cast<int>(gp.units < sm_count() ? gp.units : sm_count());
+      ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), s>>>(ta, tb, gp);
+    }
     if (int st = launch_status()) return st;
   }
 

@@ -81,6 +81,7 @@ int dot_batched_vec(const DotProblem& p, void* workspace, size_t workspace_bytes
 size_t dot_ozaki_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
 bool dot_ozaki_supported(int64_t M, int64_t N, int64_t K);
 int dot_ozaki_params(int64_t K, int* moduli, int* bits);
+int dot_ozaki_kernel_info(int* cta_pairs, int* query_error);
 int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
 }  // namespace dsb

@@ -233,7 +233,7 @@ reduce_cols_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body,
 }  // namespace
 
 int reduce_full_blocks(int64_t n) {
-  return static_cast<int>(grid_for((n + 2 * kUnroll - 1) / (2 * kUnroll), kThreads, 4));
+  return static_cast<int>(grid_for((n + 2 * kUnroll - 1) / (2 * kUnroll), kThreads, 8));
 }
 
 size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {

@@ -87,6 +87,7 @@ SIGNATURES = {
                        ctypes.c_int),
     "ds_dot_general_f64": ([_BUF, _BUF, _DIMS, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
     "ds_dot_tensor_plan": ([_I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
+    "ds_dot_tensor_kernel_info": ([ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_profile_enable": ([ctypes.c_int], None),
     "ds_profile_reset": ([], None),
     "ds_profile_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), _I64P], ctypes.c_int),
@@ -101,6 +102,16 @@ def gemm_info(M: int, N: int, K: int) -> dict:
     check(lib().ds_dot_tensor_plan(int(K), ctypes.byref(m), ctypes.byref(b)), "plan")
     return {"moduli": m.value, "bits": b.value,
             "tensor_ops_per_launch": float(m.value) * 2.0 * M * N * K}
+
+
+def gemm_kernel_info() -> dict:
+    """Tensor-core GEMM kernel of the current device: CTA pairs of the
+    cta_group::2 kernel (0 = the one-CTA kernel) and the occupancy query's
+    CUDA error code."""
+    p, e = ctypes.c_int32(), ctypes.c_int32()
+    check(lib().ds_dot_tensor_kernel_info(ctypes.byref(p), ctypes.byref(e)), "kernel info")
+    return {"cta_pairs": p.value, "query_error": e.value,
+            "kernel": "cta_pair" if p.value > 0 else "single_cta"}
 
 
 def profile_enable(on: bool = True) -> None:
@@ -152,12 +163,16 @@ def check(status: int, what: str = "") -> None:
     raise DsInternal(status, f"{what}: {msg}" if what else msg)
 
 
+_DIMS_TYPES = [ctypes.c_int64 * max(n, 1) for n in range(17)]
+
+
 def make_buffer(ptr: int, shape) -> tuple:
     """A DsBuffer for `shape` at device address `ptr`; returns (buffer, dims)
     (keep `dims` alive while the buffer is used)."""
-    shape = tuple(int(d) for d in shape)
-    dims = (ctypes.c_int64 * max(len(shape), 1))(*shape)
-    return DsBuffer(ptr, dims, len(shape)), dims
+    shape = tuple(shape)
+    n = len(shape)
+    dims = (_DIMS_TYPES[n] if n < 17 else ctypes.c_int64 * n)(*shape)
+    return DsBuffer(ptr, dims, n), dims
 
 
 def make_dot_dims(n_batch=0, lhs_contracting=1, rhs_contracting=0) -> DsDotDims:

@@ -177,55 +177,60 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
         if unknown:
             raise TypeError(f"{target_name}: unknown attribute(s) {sorted(unknown)}")
         device = args[0].device
-        with torch.cuda.device(device):
-            outs = [torch.empty(s.shape, dtype=s.dtype, device=device) for s in results_spec]
-            keep = []
-            bufs = []
-            for t in list(args) + outs:
-                b, d = _buf(t)
-                keep.append(d)
-                bufs.append(b)
-            refs = [ctypes.byref(b) for b in bufs]
-            stream = _stream_handle()
-            if conv.kind == "plain":
-                call_args = refs[:len(args)]
-                for name in conv.attrs:
-                    if name not in attrs:
-                        raise TypeError(f"{target_name}: missing attribute {name!r}")
-                    call_args.append(int(attrs[name]))
-                call_args += refs[len(args):]
-                status = fn(*call_args, stream)
-            elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64"):
-                dims = tuple(int(d) for d in attrs.get("dimensions", ()))
-                body = int(attrs.get("body", _lib.DS_BODY_ADD))
-                cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
-                ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
-                ws = _workspace(ws_bytes, device)
-                wsp = ctypes.c_void_p(ws.data_ptr())
-                if conv.kind == "reduce":
-                    status = fn(refs[0], refs[1], refs[2], refs[3], cdims, len(dims), body,
-                                refs[4], refs[5], wsp, ws_bytes, stream)
-                elif conv.kind == "reduce_f64":
-                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], wsp,
-                                ws_bytes, stream)
-                else:
-                    status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], refs[3],
-                                wsp, ws_bytes, stream)
+        if device.index is not None and device.index != torch.cuda.current_device():
+            with torch.cuda.device(device):
+                return _invoke(args, attrs, device)
+        return _invoke(args, attrs, device)
+
+    def _invoke(args, attrs, device):
+        outs = [torch.empty(s.shape, dtype=s.dtype, device=device) for s in results_spec]
+        keep = []
+        bufs = []
+        for t in list(args) + outs:
+            b, d = _buf(t)
+            keep.append(d)
+            bufs.append(b)
+        refs = [ctypes.byref(b) for b in bufs]
+        stream = _stream_handle()
+        if conv.kind == "plain":
+            call_args = refs[:len(args)]
+            for name in conv.attrs:
+                if name not in attrs:
+                    raise TypeError(f"{target_name}: missing attribute {name!r}")
+                call_args.append(int(attrs[name]))
+            call_args += refs[len(args):]
+            status = fn(*call_args, stream)
+        elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64"):
+            dims = tuple(int(d) for d in attrs.get("dimensions", ()))
+            body = int(attrs.get("body", _lib.DS_BODY_ADD))
+            cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
+            ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
+            ws = _workspace(ws_bytes, device)
+            wsp = ctypes.c_void_p(ws.data_ptr())
+            if conv.kind == "reduce":
+                status = fn(refs[0], refs[1], refs[2], refs[3], cdims, len(dims), body,
+                            refs[4], refs[5], wsp, ws_bytes, stream)
+            elif conv.kind == "reduce_f64":
+                status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], wsp,
+                            ws_bytes, stream)
             else:
-                dd = _dot_dims(attrs, args[0].dim())
-                algorithm = int(attrs.get("algorithm", _lib.DS_DOT_TENSOR_INT8))
-                rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
-                ws_bytes = _lib.lib().ds_dot_general_workspace_size(
-                    refs[0], rhs_ref, ctypes.byref(dd), algorithm)
-                ws = _workspace(ws_bytes, device)
-                wsp = ctypes.c_void_p(ws.data_ptr())
-                if conv.kind == "dot":
-                    status = fn(refs[0], refs[1], refs[2], refs[3], ctypes.byref(dd), algorithm,
-                                refs[4], refs[5], wsp, ws_bytes, stream)
-                else:
-                    status = fn(refs[0], refs[1], ctypes.byref(dd), algorithm, refs[2], wsp,
-                                ws_bytes, stream)
-            _lib.check(status, target_name)
+                status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], refs[3],
+                            wsp, ws_bytes, stream)
+        else:
+            dd = _dot_dims(attrs, args[0].dim())
+            algorithm = int(attrs.get("algorithm", _lib.DS_DOT_TENSOR_INT8))
+            rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
+            ws_bytes = _lib.lib().ds_dot_general_workspace_size(
+                refs[0], rhs_ref, ctypes.byref(dd), algorithm)
+            ws = _workspace(ws_bytes, device)
+            wsp = ctypes.c_void_p(ws.data_ptr())
+            if conv.kind == "dot":
+                status = fn(refs[0], refs[1], refs[2], refs[3], ctypes.byref(dd), algorithm,
+                            refs[4], refs[5], wsp, ws_bytes, stream)
+            else:
+                status = fn(refs[0], refs[1], ctypes.byref(dd), algorithm, refs[2], wsp,
+                            ws_bytes, stream)
+        _lib.check(status, target_name)
         return outs[0] if single else tuple(outs)
 
     return call

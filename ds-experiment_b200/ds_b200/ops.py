@@ -118,8 +118,8 @@ def ds_reduce(hi: torch.Tensor, lo: torch.Tensor, init=(0.0, 0.0),
               dimensions: Optional[Sequence[int]] = None, body: str = "add"):
     """DS reduce of SoA (hi, lo) over `dimensions` (default: all) -> (hi, lo)."""
     dims = _reduce_dims(hi.dim(), dimensions)
-    ih = torch.tensor(float(init[0]), dtype=F32, device=hi.device)
-    il = torch.tensor(float(init[1]), dtype=F32, device=hi.device)
+    ih = torch.full((), float(init[0]), dtype=F32, device=hi.device)
+    il = torch.full((), float(init[1]), dtype=F32, device=hi.device)
     out = _sds(_out_shape(hi.shape, dims), F32)
     return ffi_call("ds_reduce", (out, out))(hi, lo, ih, il, dimensions=dims,
                                              body=_BODIES[body])
@@ -129,7 +129,7 @@ def ds_reduce_f64(x: torch.Tensor, init: float = 0.0,
                   dimensions: Optional[Sequence[int]] = None, body: str = "add"):
     """DS reduce of an f64 tensor (split on load, recombined on store)."""
     dims = _reduce_dims(x.dim(), dimensions)
-    it = torch.tensor(float(init), dtype=F64, device=x.device)
+    it = torch.full((), float(init), dtype=F64, device=x.device)
     return ffi_call("ds_reduce_f64", _sds(_out_shape(x.shape, dims), F64))(
         x, it, dimensions=dims, body=_BODIES[body])
 
@@ -138,7 +138,7 @@ def ds_reduce_from_f64(x: torch.Tensor, init: float = 0.0,
                        dimensions: Optional[Sequence[int]] = None, body: str = "add"):
     """DS reduce of an f64 tensor with the result kept as a DS pair (hi, lo)."""
     dims = _reduce_dims(x.dim(), dimensions)
-    it = torch.tensor(float(init), dtype=F64, device=x.device)
+    it = torch.full((), float(init), dtype=F64, device=x.device)
     out = _sds(_out_shape(x.shape, dims), F32)
     return ffi_call("ds_reduce_from_f64", (out, out))(x, it, dimensions=dims,
                                                       body=_BODIES[body])

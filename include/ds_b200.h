@@ -200,7 +200,7 @@ DS_API int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init,
    partials (32 KiB), which every GPU that loads the library holds until the
    process exits.  Results are bit-identical to ds_reduce_f64.
    - A reduction that would need more than 4096 block partials returns
-     DS_INVALID_ARGUMENT (the partial count is at most 4 per SM, so this does
+     DS_INVALID_ARGUMENT (the partial count is at most 8 per SM, so this does
      not occur on B200).
    - The first call on each device looks up the array's device address
      (cudaGetSymbolAddress) with that device current; make that first call
@@ -249,13 +249,20 @@ DS_API int ds_dot_general_f64(const ds_buffer* lhs, const ds_buffer* rhs,
 
 /* Per-kernel GPU time.  While enabled, each op brackets its main kernel with
    CUDA events on the launch stream under a family name ("elementwise",
-   "recurrence", "reduce", "dot_simt", "dot_vec", "ozaki_split",
-   "ozaki_gemm", "ozaki_crt").  ds_profile_read waits for the recorded
+   "recurrence", "reduce", "dot_simt", "dot_vec", "ozaki_split" (with its
+   parts "ozaki_split_rows" and "ozaki_split_cols"), "ozaki_gemm",
+   "ozaki_crt").  ds_profile_read waits for the recorded
    events and returns the summed milliseconds and the launch count. */
 /* Plan of the tensor-core dot_general for contraction length K: the number
    of int8 GEMMs (moduli) it runs and the bits each operand keeps relative to
    its row (column) maximum. */
 DS_API int ds_dot_tensor_plan(int64_t K, int32_t* moduli, int32_t* bits);
+
+/* Which tensor-core GEMM kernel the current device runs: *cta_pairs is the
+   number of co-resident CTA pairs of the cta_group::2 kernel (0 when the
+   one-CTA kernel is used), *query_error the CUDA error of the cluster
+   occupancy query that decided it (0 if it succeeded). */
+DS_API int ds_dot_tensor_kernel_info(int32_t* cta_pairs, int32_t* query_error);
 
 DS_API void ds_profile_enable(int on);
 DS_API void ds_profile_reset(void);
