@@ -89,6 +89,9 @@ class ClockSampler:
         self.out = None
 
     def start(self):
+        """Start sampling and return once the first sample is in, so that
+        nvidia-smi's start-up (NVML initialisation) lands before the timed
+        region instead of inside it."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
@@ -96,6 +99,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
+            return
+        import select
+        ready, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+        self.first = self.proc.stdout.readline() if ready else ""
 
     def stop(self):
         if self.proc is None:
@@ -107,6 +114,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        # the first sample was taken before the timed region: not counted
         rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
         if not sm:
@@ -477,16 +485,22 @@ def run_stream(args):
             a, b, c = dev_in
             fn = lambda: ops.ds_fused_add_mul3_to_f64(a, b, c)  # noqa: E731
             bpe, fam = 32.0, "elementwise"
+            launches_per_step = 1
         else:
             x = dev_in[0]
             fn = (lambda: dsd.ds_sum_f64_sharded(x)) if world > 1 else (lambda: ops.ds_sum_f64(x))
             bpe, fam = 8.0, "reduce"
+            # block partials + their fold; at N > 1 also the packed combine
+            # and the recombine to f64
+            launches_per_step = 2 if world == 1 else 4
         clocks.start()
         ms, out = timed(fn, args.steps, profile=True)
         clk = clocks.stop()
         _lib.profile_enable(False)
         k_ms, k_n = _lib.profile_read(fam)
-        per = k_ms / max(k_n, 1)
+        # device time of the family per step: at N > 1 the reduce family
+        # also holds the tiny combine of the gathered pairs
+        per = k_ms / max(args.steps, 1)
         achieved = bpe * n / (per * 1e-3) / 1e9
         line.update({
             "value": round(world * bpe * n / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
@@ -498,8 +512,8 @@ def run_stream(args):
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "traffic": ncu_traffic(fam, f"{wl}{n}"),
                          "peak_source": f"{peak_src} hbm_gbs",
-                         "kernel_ms_per_launch": round(per, 4)},
-            "gpu_launches": int(k_n), "clocks": clk})
+                         "kernel_ms_per_step": round(per, 4)},
+            "gpu_launches": int(launches_per_step * args.steps), "clocks": clk})
         if rank == 0:
             got = out.cpu().numpy()
             from oracle import dso, exact

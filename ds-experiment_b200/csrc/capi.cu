@@ -439,6 +439,33 @@ int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dim
   return reduce_launch(a, as_stream(stream));
 }
 
+int ds_reduce_packed(const ds_buffer* in, const ds_buffer* init_hi, const ds_buffer* init_lo,
+                     const int64_t* dimensions, int64_t n_dimensions, int32_t body,
+                     const ds_buffer* out_hi, const ds_buffer* out_lo, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({in, init_hi, init_lo, out_hi, out_lo}, "ds_reduce_packed")) return st;
+  if (in->rank == 0 || last_dim(in) != 2) return invalid("ds_reduce_packed expects last dim == 2");
+  if (total(init_hi) != 1 || total(init_lo) != 1)
+    return invalid("ds_reduce_packed: init values must be scalars");
+  if (out_hi->rank != out_lo->rank || total(out_hi) != total(out_lo))
+    return invalid("ds_reduce_packed: hi and lo outputs must have the same shape");
+  // the logical tensor: the packed shape without its trailing 2
+  const ds_buffer logical{in->data, in->dims, in->rank - 1};
+  ReduceArgs a;
+  if (int st = reduce_common("ds_reduce_packed", &logical, dimensions, n_dimensions, body, out_hi,
+                             a))
+    return st;
+  a.in_packed = static_cast<const float*>(in->data);
+  a.init_hi = static_cast<const float*>(init_hi->data);
+  a.init_lo = static_cast<const float*>(init_lo->data);
+  a.out_hi = static_cast<float*>(out_hi->data);
+  a.out_lo = static_cast<float*>(out_lo->data);
+  a.body = body;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return reduce_launch(a, as_stream(stream));
+}
+
 int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dimensions,
                        int64_t n_dimensions, int32_t body, const ds_buffer* out_hi,
                        const ds_buffer* out_lo, void* workspace, size_t workspace_bytes,

@@ -31,8 +31,9 @@ int ew_recurrence_mul_add(const double* x, const double* a, const double* b, dou
 // reduce.cu
 struct ReduceArgs {
   const double* in_f64 = nullptr;  // either f64 input ...
-  const float* in_hi = nullptr;    // ... or SoA DS input
+  const float* in_hi = nullptr;    // ... or SoA DS input ...
   const float* in_lo = nullptr;
+  const float* in_packed = nullptr;  // ... or packed DS input [..., 2]
   const double* init_f64 = nullptr;  // rank-0 init (f64, or hi/lo)
   const float* init_hi = nullptr;
   const float* init_lo = nullptr;

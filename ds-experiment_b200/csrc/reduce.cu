@@ -68,17 +68,23 @@ __device__ __forceinline__ ds2 finish(int body, ds2 init, ds2 total) {
 
 struct Src {
   const double* f64;  // f64 input (split on load), or
-  const float* hi;    // SoA DS input
+  const float* hi;    // SoA DS input (packed: hi = the [..., 2] array, lo unused)
   const float* lo;
   bool vec;           // 16-byte aligned pair loads allowed
+  bool packed;        // packed DS input: element i at hi[2i], hi[2i + 1]
   __device__ __forceinline__ ds2 at(int64_t i) const {
-    return f64 ? from_f64(f64[i]) : ds2{hi[i], lo[i]};
+    if (f64) return from_f64(f64[i]);
+    return packed ? ds2{hi[2 * i], hi[2 * i + 1]} : ds2{hi[i], lo[i]};
   }
   __device__ __forceinline__ void pair(int64_t p, ds2& x0, ds2& x1) const {
     if (f64) {
       const double2 v = __ldcs(reinterpret_cast<const double2*>(f64) + p);
       x0 = from_f64(v.x);
       x1 = from_f64(v.y);
+    } else if (packed) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(hi) + p);
+      x0 = ds2{v.x, v.y};
+      x1 = ds2{v.z, v.w};
     } else {
       const float2 h = __ldcs(reinterpret_cast<const float2*>(hi) + p);
       const float2 l = __ldcs(reinterpret_cast<const float2*>(lo) + p);
@@ -243,8 +249,10 @@ size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {
 }
 
 int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
-  Src src{a.in_f64, a.in_hi, a.in_lo, false};
-  src.vec = a.in_f64 ? aligned(a.in_f64, 16) : (aligned(a.in_hi, 8) && aligned(a.in_lo, 8));
+  Src src{a.in_f64, a.in_packed ? a.in_packed : a.in_hi, a.in_lo, false, a.in_packed != nullptr};
+  src.vec = a.in_f64      ? aligned(a.in_f64, 16)
+            : src.packed ? aligned(a.in_packed, 16)
+                         : (aligned(a.in_hi, 8) && aligned(a.in_lo, 8));
   Dst dst{a.out_f64, a.out_hi, a.out_lo};
   const int64_t outer = a.outer, red = a.red, inner = a.inner;
   if (outer * inner == 0) return ok();

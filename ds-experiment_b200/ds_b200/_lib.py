@@ -82,6 +82,8 @@ SIGNATURES = {
     "ds_reduce_from_f64": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                            ctypes.c_int),
     "ds_reduce_f64_noalloc": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _VP], ctypes.c_int),
+    "ds_reduce_packed": ([_BUF, _BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
+                         ctypes.c_int),
     "ds_dot_general_workspace_size": ([_BUF, _BUF, _DIMS, _I32], _SZ),
     "ds_dot_general": ([_BUF, _BUF, _BUF, _BUF, _DIMS, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                        ctypes.c_int),

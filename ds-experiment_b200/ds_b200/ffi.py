@@ -66,6 +66,8 @@ CONVENTIONS: Dict[str, _Convention] = {
     "ds_reduce_f64": _Convention((F64, F64), ("dimensions", "body"), (F64,), "reduce_f64"),
     "ds_reduce_from_f64": _Convention((F64, F64), ("dimensions", "body"), (F32, F32),
                                       "reduce_from_f64"),
+    "ds_reduce_packed": _Convention((F32, F32, F32), ("dimensions", "body"), (F32, F32),
+                                    "reduce_packed"),
     "ds_dot_general": _Convention((F32, F32, F32, F32),
                                   ("lhs_batching_dimensions", "rhs_batching_dimensions",
                                    "lhs_contracting_dimensions",
@@ -98,6 +100,7 @@ REFERENCE_TARGETS = {
     "ds_reduce": "ds_reduce",
     "ds_reduce_f64": "ds_reduce_f64",
     "ds_reduce_from_f64": "ds_reduce_from_f64",
+    "ds_reduce_packed": "ds_reduce_packed",
     "ds_dot_general": "ds_dot_general",
     "ds_dot_general_f64": "ds_dot_general_f64",
 }
@@ -168,7 +171,10 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
         if spec.dtype != dt:
             raise TypeError(f"{target_name}: result dtype must be {dt}, got {spec.dtype}")
 
-    def call(*args: torch.Tensor, **attrs):
+    def call(*args: torch.Tensor, out=None, **attrs):
+        """Run the target.  `out`: optional pre-allocated result tensor(s)
+        (contiguous, of the declared shapes and dtypes), as XLA hands a
+        handler its result buffers; otherwise results are allocated."""
         if len(args) != len(conv.args):
             raise TypeError(f"{target_name}: expected {len(conv.args)} operand(s), got {len(args)}")
         for i, (t, dt) in enumerate(zip(args, conv.args)):
@@ -177,13 +183,22 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
         if unknown:
             raise TypeError(f"{target_name}: unknown attribute(s) {sorted(unknown)}")
         device = args[0].device
+        if out is not None:
+            out = [out] if isinstance(out, torch.Tensor) else list(out)
+            if len(out) != len(results_spec):
+                raise ValueError(f"{target_name}: expected {len(results_spec)} output tensor(s)")
+            for i, (t, s) in enumerate(zip(out, results_spec)):
+                _check_tensor(t, s.dtype, f"{target_name} result {i}")
+                if tuple(t.shape) != s.shape:
+                    raise ValueError(f"{target_name} result {i}: shape {tuple(t.shape)} != {s.shape}")
         if device.index is not None and device.index != torch.cuda.current_device():
             with torch.cuda.device(device):
-                return _invoke(args, attrs, device)
-        return _invoke(args, attrs, device)
+                return _invoke(args, attrs, device, out)
+        return _invoke(args, attrs, device, out)
 
-    def _invoke(args, attrs, device):
-        outs = [torch.empty(s.shape, dtype=s.dtype, device=device) for s in results_spec]
+    def _invoke(args, attrs, device, out):
+        outs = out if out is not None else [
+            torch.empty(s.shape, dtype=s.dtype, device=device) for s in results_spec]
         keep = []
         bufs = []
         for t in list(args) + outs:
@@ -200,11 +215,16 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
                 call_args.append(int(attrs[name]))
             call_args += refs[len(args):]
             status = fn(*call_args, stream)
-        elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64"):
+        elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64", "reduce_packed"):
             dims = tuple(int(d) for d in attrs.get("dimensions", ()))
             body = int(attrs.get("body", _lib.DS_BODY_ADD))
             cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
-            ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
+            if conv.kind == "reduce_packed":  # sized on the logical shape [..., 2] -> [...]
+                lb, ld = _lib.make_buffer(args[0].data_ptr(), tuple(args[0].shape[:-1]))
+                keep.append(ld)
+                ws_bytes = _lib.lib().ds_reduce_workspace_size(ctypes.byref(lb), cdims, len(dims))
+            else:
+                ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
             ws = _workspace(ws_bytes, device)
             wsp = ctypes.c_void_p(ws.data_ptr())
             if conv.kind == "reduce":
@@ -213,6 +233,9 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
             elif conv.kind == "reduce_f64":
                 status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], wsp,
                             ws_bytes, stream)
+            elif conv.kind == "reduce_packed":
+                status = fn(refs[0], refs[1], refs[2], cdims, len(dims), body, refs[3], refs[4],
+                            wsp, ws_bytes, stream)
             else:
                 status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], refs[3],
                             wsp, ws_bytes, stream)

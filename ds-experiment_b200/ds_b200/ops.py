@@ -34,8 +34,8 @@ def ds_from_f64(x: torch.Tensor) -> torch.Tensor:
     return ffi_call("ds_from_f64", _sds(tuple(x.shape) + (2,), F32))(x)
 
 
-def ds_to_f64(x: torch.Tensor) -> torch.Tensor:
-    return ffi_call("ds_to_f64", _sds(tuple(x.shape[:-1]), F64))(x)
+def ds_to_f64(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return ffi_call("ds_to_f64", _sds(tuple(x.shape[:-1]), F64))(x, out=out)
 
 
 def ds_from_f32(x: torch.Tensor) -> torch.Tensor:
@@ -114,34 +114,65 @@ def _out_shape(shape, dims):
     return tuple(s for i, s in enumerate(shape) if i not in dims)
 
 
+_SCALARS: dict = {}
+
+
+def _scalar(value: float, dtype, device) -> torch.Tensor:
+    """A 0-d device tensor holding `value`, cached per (device, stream, dtype,
+    value) so that repeated calls launch no fill kernel; the cache key holds
+    the stream because the fill is ordered only on the stream that made it."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream, dtype, float(value).hex())  # hex keeps -0.0 apart
+    t = _SCALARS.get(key)
+    if t is None:
+        if len(_SCALARS) > 256:
+            _SCALARS.clear()
+        t = _SCALARS[key] = torch.full((), float(value), dtype=dtype, device=device)
+    return t
+
+
 def ds_reduce(hi: torch.Tensor, lo: torch.Tensor, init=(0.0, 0.0),
-              dimensions: Optional[Sequence[int]] = None, body: str = "add"):
+              dimensions: Optional[Sequence[int]] = None, body: str = "add", out=None):
     """DS reduce of SoA (hi, lo) over `dimensions` (default: all) -> (hi, lo)."""
     dims = _reduce_dims(hi.dim(), dimensions)
-    ih = torch.full((), float(init[0]), dtype=F32, device=hi.device)
-    il = torch.full((), float(init[1]), dtype=F32, device=hi.device)
-    out = _sds(_out_shape(hi.shape, dims), F32)
-    return ffi_call("ds_reduce", (out, out))(hi, lo, ih, il, dimensions=dims,
-                                             body=_BODIES[body])
+    ih = _scalar(init[0], F32, hi.device)
+    il = _scalar(init[1], F32, hi.device)
+    res = _sds(_out_shape(hi.shape, dims), F32)
+    return ffi_call("ds_reduce", (res, res))(hi, lo, ih, il, dimensions=dims,
+                                             body=_BODIES[body], out=out)
+
+
+def ds_reduce_packed(x: torch.Tensor, init=(0.0, 0.0),
+                     dimensions: Optional[Sequence[int]] = None, body: str = "add", out=None):
+    """DS reduce of a packed DS tensor x[..., 2] over `dimensions` of its
+    logical shape x.shape[:-1] (default: all) -> (hi, lo)."""
+    dims = _reduce_dims(x.dim() - 1, dimensions)
+    ih = _scalar(init[0], F32, x.device)
+    il = _scalar(init[1], F32, x.device)
+    res = _sds(_out_shape(x.shape[:-1], dims), F32)
+    return ffi_call("ds_reduce_packed", (res, res))(x, ih, il, dimensions=dims,
+                                                    body=_BODIES[body], out=out)
 
 
 def ds_reduce_f64(x: torch.Tensor, init: float = 0.0,
-                  dimensions: Optional[Sequence[int]] = None, body: str = "add"):
-    """DS reduce of an f64 tensor (split on load, recombined on store)."""
+                  dimensions: Optional[Sequence[int]] = None, body: str = "add", out=None):
+    """DS reduce of an f64 tensor -> f64.  The combining step is the DS
+    body; with add/sub each thread first accumulates its elements with an
+    exact f64 two_sum before the DS tree."""
     dims = _reduce_dims(x.dim(), dimensions)
-    it = torch.full((), float(init), dtype=F64, device=x.device)
+    it = _scalar(init, F64, x.device)
     return ffi_call("ds_reduce_f64", _sds(_out_shape(x.shape, dims), F64))(
-        x, it, dimensions=dims, body=_BODIES[body])
+        x, it, dimensions=dims, body=_BODIES[body], out=out)
 
 
 def ds_reduce_from_f64(x: torch.Tensor, init: float = 0.0,
-                       dimensions: Optional[Sequence[int]] = None, body: str = "add"):
+                       dimensions: Optional[Sequence[int]] = None, body: str = "add", out=None):
     """DS reduce of an f64 tensor with the result kept as a DS pair (hi, lo)."""
     dims = _reduce_dims(x.dim(), dimensions)
-    it = torch.full((), float(init), dtype=F64, device=x.device)
-    out = _sds(_out_shape(x.shape, dims), F32)
-    return ffi_call("ds_reduce_from_f64", (out, out))(x, it, dimensions=dims,
-                                                      body=_BODIES[body])
+    it = _scalar(init, F64, x.device)
+    res = _sds(_out_shape(x.shape, dims), F32)
+    return ffi_call("ds_reduce_from_f64", (res, res))(x, it, dimensions=dims,
+                                                      body=_BODIES[body], out=out)
 
 
 def ds_sum_f64(x: torch.Tensor, dimensions=None) -> torch.Tensor:

@@ -214,6 +214,17 @@ DS_API int ds_reduce_f64_noalloc(const ds_buffer* in, const ds_buffer* init,
                                  int32_t body, const ds_buffer* out,
                                  void* stream);
 
+/* DS reduce of a packed DS tensor in[..., 2] (the wire format of DsAdd and
+   the other packed targets, cpp/ds_add.cpp:46-49) over `dimensions` of its
+   logical shape in.dims[:-1]; init and result as in ds_reduce.  The
+   workspace size is that of ds_reduce on the logical shape. */
+DS_API int ds_reduce_packed(const ds_buffer* in, const ds_buffer* init_hi,
+                            const ds_buffer* init_lo, const int64_t* dimensions,
+                            int64_t n_dimensions, int32_t body,
+                            const ds_buffer* out_hi, const ds_buffer* out_lo,
+                            void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* The split fused on input only: f64 input and rank-0 f64 init, SoA DS
    result (out_hi, out_lo) -- the pass's reduce of an f64 argument whose
    result stays in DS form (e.g. a partial sum that is combined further). */

@@ -82,6 +82,57 @@ def test_soa_entry_and_f64_entry(ops, dso):
     assert abs(f64 - truth) <= abs(soa - truth) + ds_bound(x) * 2.0 ** -8
 
 
+@pytest.mark.parametrize("n", [1, 2, 7, 4096, 100_003])
+@pytest.mark.parametrize("aligned", [True, False])
+def test_packed_entry_matches_soa(ops, dso, n, aligned):
+    """ds_reduce_packed on x[..., 2] is the SoA ds_reduce of the same pairs,
+    bit for bit (same fold order, vector or scalar loads alike)."""
+    from gpu_util import misaligned
+    x = config2_inputs(n, seed=n)
+    sp = np.ascontiguousarray(dso.ds_from_f64(x))
+    put = cu if aligned else misaligned
+    hi, lo = ops.ds_reduce(put(np.ascontiguousarray(sp[:, 0])),
+                           put(np.ascontiguousarray(sp[:, 1])), init=(0.5, 2.0 ** -30))
+    ph, pl = ops.ds_reduce_packed(put(sp), init=(0.5, 2.0 ** -30))
+    assert_bits_equal(host(ph), host(hi), "hi")
+    assert_bits_equal(host(pl), host(lo), "lo")
+
+
+def test_packed_entry_segmented(ops, dso):
+    x = np.random.default_rng(5).uniform(-1, 1, (37, 300))
+    sp = np.ascontiguousarray(dso.ds_from_f64(x.ravel()).reshape(37, 300, 2))
+    hi, lo = ops.ds_reduce(cu(np.ascontiguousarray(sp[..., 0])),
+                           cu(np.ascontiguousarray(sp[..., 1])), dimensions=(1,))
+    ph, pl = ops.ds_reduce_packed(cu(sp), dimensions=(1,))
+    assert ph.shape == (37,)
+    assert_bits_equal(host(ph), host(hi), "hi")
+    assert_bits_equal(host(pl), host(lo), "lo")
+
+
+def test_packed_entry_rejects_bad_last_dim(ops):
+    import torch
+    from ds_b200 import _lib
+    with pytest.raises(_lib.DsInvalidArgument, match="last dim == 2"):
+        ops.ds_reduce_packed(torch.zeros(8, 3, dtype=torch.float32, device="cuda"))
+
+
+def test_out_argument(ops):
+    """Results written into caller-given views equal the allocated results;
+    a wrong result shape is rejected before the launch."""
+    import torch
+    x = cu(config2_inputs(10_000, seed=4))
+    hi, lo = ops.ds_reduce_from_f64(x)
+    pair = torch.full((2,), 7.0, dtype=torch.float32, device="cuda")
+    r = ops.ds_reduce_from_f64(x, out=(pair[0], pair[1]))
+    assert r[0].data_ptr() == pair.data_ptr()
+    assert_bits_equal(host(pair), np.array([host(hi), host(lo)], np.float32).ravel(), "pair")
+    f = torch.empty((), dtype=torch.float64, device="cuda")
+    ops.ds_to_f64(pair, out=f)
+    assert float(host(f)) == float(np.float64(host(hi))) + float(np.float64(host(lo)))
+    with pytest.raises(ValueError, match="shape"):
+        ops.ds_reduce_from_f64(x, out=(pair, pair))
+
+
 def test_deterministic(ops):
     x = cu(config2_inputs(1 << 22, seed=9))
     a = host(ops.ds_sum_f64(x))
