@@ -466,6 +466,55 @@ int ds_reduce_packed(const ds_buffer* in, const ds_buffer* init_hi, const ds_buf
   return reduce_launch(a, as_stream(stream));
 }
 
+size_t ds_exchange_bytes(void) { return kExchangeBytes; }
+
+size_t ds_exchange_handle_bytes(void) { return peer_handle_bytes(); }
+
+int ds_exchange_alloc(void** buffer, void* handle) {
+  return peer_alloc(kExchangeBytes, buffer, handle);
+}
+
+int ds_exchange_open(const void* handle, void** buffer) { return peer_open(handle, buffer); }
+
+int ds_exchange_close(void* buffer) { return peer_close(buffer); }
+
+int ds_exchange_free(void* buffer) { return peer_free(buffer); }
+
+int ds_exchange_error(const void* buffer, uint32_t* code) { return peer_read_error(buffer, code); }
+
+size_t ds_reduce_f64_sharded_workspace_size(const ds_buffer* in) {
+  if (!valid_buffer(in) || bad_dims(in)) return 0;
+  return reduce_sharded_workspace_bytes(total(in));
+}
+
+int ds_reduce_f64_sharded(const ds_buffer* in, const ds_buffer* init, int32_t body,
+                          const ds_buffer* out, void* const* buffers, int32_t world,
+                          int32_t rank, uint64_t epoch, int32_t timeout_ms, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (int st = check_buffers({in, init, out}, "ds_reduce_f64_sharded")) return st;
+  if (total(init) != 1) return invalid("ds_reduce_f64_sharded: init value must be a scalar");
+  if (total(out) != 1) return invalid("ds_reduce_f64_sharded: output must have one element");
+  if (body < DS_BODY_ADD || body > DS_BODY_MUL)
+    return invalid("ds_reduce_f64_sharded: unknown body");
+  if (buffers == nullptr) return invalid("ds_reduce_f64_sharded: null exchange buffer list");
+  if (epoch == 0) return invalid("ds_reduce_f64_sharded: epochs start at 1");
+  if (timeout_ms <= 0) return invalid("ds_reduce_f64_sharded: timeout_ms must be positive");
+  ShardedReduceArgs a;
+  a.in = f64p(in);
+  a.n = total(in);
+  a.init = f64p(init);
+  a.out = static_cast<double*>(out->data);
+  a.body = body;
+  a.buffers = buffers;
+  a.world = world;
+  a.rank = rank;
+  a.epoch = epoch;
+  a.timeout_ns = static_cast<int64_t>(timeout_ms) * 1000000;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return reduce_sharded_launch(a, as_stream(stream));
+}
+
 int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dimensions,
                        int64_t n_dimensions, int32_t body, const ds_buffer* out_hi,
                        const ds_buffer* out_lo, void* workspace, size_t workspace_bytes,

@@ -50,6 +50,35 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s);
 // The same with the full-reduction partials in a static device array.
 int reduce_launch_noalloc(ReduceArgs a, cudaStream_t s);
 
+// Sharded full reduction of f64 shards, one per rank, with the DS totals
+// exchanged through peer-mapped exchange buffers (layout in reduce.cu).
+constexpr int kExchangeMaxRanks = 8;
+constexpr size_t kExchangeBytes = 1024;
+constexpr size_t kExchangeErrorOffset = 512;
+struct ShardedReduceArgs {
+  const double* in = nullptr;
+  int64_t n = 0;
+  const double* init = nullptr;
+  double* out = nullptr;
+  int body = 0;
+  void* const* buffers = nullptr;  // host array: rank r's exchange buffer, as mapped here
+  int world = 1, rank = 0;
+  uint64_t epoch = 1;
+  int64_t timeout_ns = 1000000000;
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
+};
+size_t reduce_sharded_workspace_bytes(int64_t n);
+int reduce_sharded_launch(const ShardedReduceArgs& a, cudaStream_t s);
+
+// peer.cu: exchange buffers shared between processes (CUDA IPC).
+size_t peer_handle_bytes();
+int peer_alloc(size_t bytes, void** buf, void* handle);
+int peer_open(const void* handle, void** buf);
+int peer_close(void* buf);
+int peer_free(void* buf);
+int peer_read_error(const void* buf, uint32_t* code);
+
 // Operand of a dot: element (b, r, k) of a batched [batch, rows, K] view at
 // base[b * s_b + r * s_r + k * s_k], given as f64 or as SoA hi/lo f32.
 struct DotOperand {

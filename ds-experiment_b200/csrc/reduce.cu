@@ -131,7 +131,8 @@ __device__ __forceinline__ void two_sum_acc(double& s, double& c, double x) {
 // inputs and the multiply body fold DS pairs.
 __global__ void __launch_bounds__(kThreads)
 reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
-                   const double* init_f64, const float* init_hi, const float* init_lo) {
+                   const double* init_f64, const float* init_hi, const float* init_lo,
+                   bool always_partials = false) {
   const bool is_mul = body == 2;
   ds2 acc = identity(is_mul);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -180,7 +181,7 @@ reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
   }
   acc = block_combine(is_mul, acc);
   if (threadIdx.x == 0) {
-    if (gridDim.x == 1) {
+    if (gridDim.x == 1 && !always_partials) {
       // An empty reduction returns init unchanged (bits included).
       const ds2 init = load_init(init_f64, init_hi, init_lo);
       dst.put(0, n == 0 ? init : finish(body, init, acc));
@@ -338,6 +339,165 @@ int reduce_launch_noalloc(ReduceArgs a, cudaStream_t s) {
     a.workspace_bytes = sizeof(g_static_partials);
   }
   return reduce_launch(a, s);
+}
+
+// ---- sharded full reduction: the totals exchanged over peer memory ----------
+//
+// Every rank (one process per GPU) reduces its own shard to a DS total, and
+// one kernel then publishes that total to every rank's exchange buffer with
+// plain stores through peer (NVLink P2P) mappings, waits -- bounded -- until
+// the totals of all ranks have arrived in its own buffer, and folds them in
+// rank order, so every rank writes the same bits.  No collective library and
+// no host round trip sit between the local reduce and the result.
+//
+// Exchange buffer of one rank (kExchangeBytes, zeroed at allocation):
+//   records[2][kExchangeMaxRanks] of 32 bytes at offset (parity * 8 + r) * 32:
+//     f32 hi, f32 lo, i64 n (elements of rank r's shard), u64 epoch, u64 pad
+//   u32 error word at kExchangeErrorOffset (sticky; 1 = a wait timed out).
+// Call number `epoch` (1, 2, ... -- the same sequence on every rank) uses the
+// records of parity epoch & 1.  A rank reaches call e + 2, and overwrites
+// those records again, only after every other rank has published call e + 1,
+// which each does only after it finished reading call e: two parities keep a
+// fast rank from overwriting records a slow one still has to read.
+// The writer stores hi, lo, n, then a system-scope fence, then the epoch with
+// a release store; the reader acquires the epoch before reading the rest.
+
+namespace {
+
+struct __align__(16) ExchangeRecord {
+  float hi, lo;
+  long long n;
+  unsigned long long epoch;
+  unsigned long long pad;
+};
+static_assert(sizeof(ExchangeRecord) == 32, "exchange record layout");
+static_assert(2 * kExchangeMaxRanks * sizeof(ExchangeRecord) <= kExchangeErrorOffset,
+              "exchange records overlap the error word");
+
+struct ExchangePeers {
+  unsigned char* buf[kExchangeMaxRanks];
+};
+
+__device__ __forceinline__ ExchangeRecord* exchange_record(unsigned char* buf, int parity,
+                                                           int r) {
+  return reinterpret_cast<ExchangeRecord*>(buf) + parity * kExchangeMaxRanks + r;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void store_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Stage 2 of a sharded full reduction (one block): fold this rank's block
+// partials (the same fixed tree as reduce_partials_kernel), exchange the
+// totals, fold the non-empty ranks' totals in rank order and apply init.
+// On a timed-out wait the result is NaN and the error word is set.
+__global__ void __launch_bounds__(kThreads)
+reduce_exchange_kernel(const ds2* __restrict__ partials, int g, long long n_local, int body,
+                       Dst dst, const double* init_f64, ExchangePeers peers, int world, int rank,
+                       unsigned long long epoch, long long timeout_ns) {
+  __shared__ ds2 totals[kExchangeMaxRanks];
+  __shared__ long long counts[kExchangeMaxRanks];
+  __shared__ int failed;
+  const bool is_mul = body == 2;
+  ds2 acc = identity(is_mul);
+  for (int i = threadIdx.x; i < g; i += blockDim.x) acc = combine(is_mul, acc, partials[i]);
+  acc = block_combine(is_mul, acc);
+  const int parity = static_cast<int>(epoch & 1ull);
+  if (threadIdx.x == 0) {
+    failed = 0;
+    for (int r = 0; r < world; ++r) {
+      volatile ExchangeRecord* rec = exchange_record(peers.buf[r], parity, rank);
+      rec->hi = acc.hi;
+      rec->lo = acc.lo;
+      rec->n = n_local;
+    }
+    __threadfence_system();
+    for (int r = 0; r < world; ++r)
+      store_release_sys(&exchange_record(peers.buf[r], parity, rank)->epoch, epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    ExchangeRecord* rec = exchange_record(peers.buf[rank], parity, threadIdx.x);
+    const unsigned long long t0 = global_ns();
+    bool arrived = true;
+    while (load_acquire_sys(&rec->epoch) != epoch) {
+      if (static_cast<long long>(global_ns() - t0) > timeout_ns) {
+        arrived = false;
+        break;
+      }
+      __nanosleep(128);
+    }
+    if (arrived) {
+      const volatile ExchangeRecord* v = rec;
+      totals[threadIdx.x] = ds2{v->hi, v->lo};
+      counts[threadIdx.x] = v->n;
+    } else {
+      failed = 1;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (failed) {
+      atomicOr(reinterpret_cast<unsigned*>(peers.buf[rank] + kExchangeErrorOffset), 1u);
+      const float nan = __int_as_float(0x7fffffff);
+      dst.put(0, ds2{nan, nan});
+      return;
+    }
+    const ds2 init = load_init(init_f64, nullptr, nullptr);
+    bool any = false;
+    ds2 total = identity(is_mul);
+    for (int r = 0; r < world; ++r) {
+      if (counts[r] == 0) continue;
+      total = any ? combine(is_mul, total, totals[r]) : totals[r];
+      any = true;
+    }
+    dst.put(0, any ? finish(body, init, total) : init);
+  }
+}
+
+}  // namespace
+
+size_t reduce_sharded_workspace_bytes(int64_t n) {
+  return static_cast<size_t>(n > 0 ? reduce_full_blocks(n) : 1) * sizeof(ds2);
+}
+
+int reduce_sharded_launch(const ShardedReduceArgs& a, cudaStream_t s) {
+  if (a.world < 1 || a.world > kExchangeMaxRanks || a.rank < 0 || a.rank >= a.world)
+    return set_error(DS_INVALID_ARGUMENT, "ds_reduce_f64_sharded: invalid rank/world");
+  const int g = a.n > 0 ? reduce_full_blocks(a.n) : 1;
+  const size_t need = static_cast<size_t>(g) * sizeof(ds2);
+  if (need > a.workspace_bytes || !aligned(a.workspace, alignof(ds2)))
+    return set_error(DS_INVALID_ARGUMENT,
+                     "ds_reduce_f64_sharded: workspace too small (need " +
+                         std::to_string(need) + " bytes, 8-byte aligned)");
+  ExchangePeers peers{};
+  for (int r = 0; r < a.world; ++r) {
+    if (a.buffers[r] == nullptr || !aligned(a.buffers[r], 16))
+      return set_error(DS_INVALID_ARGUMENT,
+                       "ds_reduce_f64_sharded: exchange buffers must be 16-byte aligned");
+    peers.buf[r] = static_cast<unsigned char*>(a.buffers[r]);
+  }
+  Src src{a.in, nullptr, nullptr, aligned(a.in, 16), false};
+  Dst dst{a.out, nullptr, nullptr};
+  ds2* partials = static_cast<ds2*>(a.workspace);
+  ProfileScope prof("reduce", s);
+  reduce_full_kernel<<<g, kThreads, 0, s>>>(src, a.n, a.body, partials, dst, nullptr, nullptr,
+                                            nullptr, true);
+  reduce_exchange_kernel<<<1, kThreads, 0, s>>>(partials, g, a.n, a.body, dst, a.init, peers,
+                                                a.world, a.rank, a.epoch, a.timeout_ns);
+  return launch_status();
 }
 
 }  // namespace dsb

@@ -84,6 +84,16 @@ SIGNATURES = {
     "ds_reduce_f64_noalloc": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _VP], ctypes.c_int),
     "ds_reduce_packed": ([_BUF, _BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                          ctypes.c_int),
+    "ds_exchange_bytes": ([], _SZ),
+    "ds_exchange_handle_bytes": ([], _SZ),
+    "ds_exchange_alloc": ([ctypes.POINTER(_VP), _VP], ctypes.c_int),
+    "ds_exchange_open": ([_VP, ctypes.POINTER(_VP)], ctypes.c_int),
+    "ds_exchange_close": ([_VP], ctypes.c_int),
+    "ds_exchange_free": ([_VP], ctypes.c_int),
+    "ds_exchange_error": ([_VP, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "ds_reduce_f64_sharded_workspace_size": ([_BUF], _SZ),
+    "ds_reduce_f64_sharded": ([_BUF, _BUF, _I32, _BUF, ctypes.POINTER(_VP), _I32, _I32,
+                               ctypes.c_uint64, _I32, _VP, _SZ, _VP], ctypes.c_int),
     "ds_dot_general_workspace_size": ([_BUF, _BUF, _DIMS, _I32], _SZ),
     "ds_dot_general": ([_BUF, _BUF, _BUF, _BUF, _DIMS, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                        ctypes.c_int),

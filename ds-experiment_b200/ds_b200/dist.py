@@ -3,10 +3,13 @@
 The reference has no multi-GPU code; this is the partitioning the ops allow:
 - elementwise chains, split/recombine and the recurrences: contiguous ranges
   of the element index per rank, no collective (shard_range / shard);
-- reduce: every rank reduces its range to a DS pair on its own GPU; the pairs
-  are all-gathered as (hi, lo) f32 (8 bytes per rank) and folded in rank
-  order on every rank with the DS reduce kernel, so all ranks hold the same
-  bits.  A plain sum all-reduce would drop the lo word;
+- reduce: every rank reduces its range to a DS pair on its own GPU and the
+  pairs are folded in rank order on every rank, so all ranks hold the same
+  bits (a plain sum all-reduce would drop the lo word).  Within one node the
+  exchange runs inside the reduce itself (PeerExchange: the final block
+  stores its pair into every peer's exchange buffer over NVLink and folds
+  what arrives in its own); otherwise the pairs are all-gathered as (hi, lo)
+  f32, 8 bytes per rank, and folded by one packed DS reduce launch;
 - dot_general: rows of A per rank with B replicated once into every GPU's
   own memory (replicate); no collective inside the product.  Batched dots
   shard the batch dimension.
@@ -65,15 +68,153 @@ def _combine_cuda(pairs: torch.Tensor, init: Tuple[float, float]) -> torch.Tenso
     return ops.ds_to_f64(res)
 
 
+class _CudaExchangeBackend:
+    """The exchange-buffer calls of libds_b200 (CUDA IPC)."""
+
+    def __init__(self):
+        from . import _lib
+        self._lib = _lib
+        self.L = _lib.lib()
+        self.handle_bytes = int(self.L.ds_exchange_handle_bytes())
+
+    def alloc(self):
+        import ctypes
+        buf = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(self.handle_bytes)
+        self._lib.check(self.L.ds_exchange_alloc(ctypes.byref(buf), handle), "exchange alloc")
+        return int(buf.value), handle.raw
+
+    def open(self, handle: bytes) -> int:
+        import ctypes
+        buf = ctypes.c_void_p()
+        self._lib.check(self.L.ds_exchange_open(handle, ctypes.byref(buf)), "exchange open")
+        return int(buf.value)
+
+    def close(self, ptr: int) -> None:
+        self._lib.check(self.L.ds_exchange_close(ptr), "exchange close")
+
+    def free(self, ptr: int) -> None:
+        self._lib.check(self.L.ds_exchange_free(ptr), "exchange free")
+
+    def error(self, ptr: int) -> int:
+        import ctypes
+        code = ctypes.c_uint32()
+        self._lib.check(self.L.ds_exchange_error(ptr, ctypes.byref(code)), "exchange error")
+        return int(code.value)
+
+
+class PeerExchange:
+    """Exchange buffers of one node's ranks, each mapped into every rank.
+
+    Construction is collective: every rank allocates its buffer, the CUDA
+    IPC handles are all-gathered through the process group, every rank maps
+    the others' buffers, and a barrier ends it.  Every use (`next_epoch`)
+    must happen on all ranks in the same order, like a collective.
+    `close()` is collective too.  At most 8 ranks.
+    """
+
+    MAX_RANKS = 8
+
+    def __init__(self, group=None, timeout_ms: int = 1000, backend=None):
+        self.group = group
+        self.world, self.rank = _world(group)
+        if self.world > self.MAX_RANKS:
+            raise ValueError(f"PeerExchange supports at most {self.MAX_RANKS} ranks")
+        if timeout_ms <= 0:
+            raise ValueError("timeout_ms must be positive")
+        self.timeout_ms = int(timeout_ms)
+        self.backend = backend or _CudaExchangeBackend()
+        self.own, handle = self.backend.alloc()
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs = []
+        self._opened = []
+        try:
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self.own)
+                else:
+                    p = self.backend.open(h)
+                    self._opened.append(p)
+                    self.ptrs.append(p)
+        except Exception:
+            for p in self._opened:
+                self.backend.close(p)
+            self.backend.free(self.own)
+            raise
+        self.epoch = 0
+        self.closed = False
+        dist.barrier(group=group)
+
+    def next_epoch(self) -> int:
+        if self.closed:
+            raise RuntimeError("PeerExchange is closed")
+        self.epoch += 1
+        return self.epoch
+
+    def error(self) -> int:
+        """The own buffer's sticky error word (waits for the device)."""
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        return self.backend.error(self.own)
+
+    def check(self) -> None:
+        code = self.error()
+        if code:
+            raise RuntimeError(f"PeerExchange rank {self.rank}: a wait for another rank "
+                               f"timed out (error word {code}); rebuild the exchange")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free the own one, after every rank
+        has finished using them (two barriers)."""
+        if self.closed:
+            return
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            self.backend.close(p)
+        dist.barrier(group=self.group)
+        self.backend.free(self.own)
+        self.closed = True
+
+
+def _sum_exchange_cuda(x_local: torch.Tensor, init: float, exchange: PeerExchange,
+                       body: int) -> torch.Tensor:
+    import ctypes
+    from . import _lib, ops
+    x = x_local.contiguous()
+    L = _lib.lib()
+    ib, idims = _lib.make_buffer(x.data_ptr(), tuple(x.shape))
+    it = ops._scalar(init, torch.float64, x.device)
+    tb, tdims = _lib.make_buffer(it.data_ptr(), ())
+    out = torch.empty((), dtype=torch.float64, device=x.device)
+    ob, odims = _lib.make_buffer(out.data_ptr(), ())
+    ws_bytes = L.ds_reduce_f64_sharded_workspace_size(ctypes.byref(ib))
+    ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=x.device)
+    ptrs = (ctypes.c_void_p * exchange.world)(*exchange.ptrs)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(L.ds_reduce_f64_sharded(
+        ctypes.byref(ib), ctypes.byref(tb), body, ctypes.byref(ob), ptrs, exchange.world,
+        exchange.rank, exchange.next_epoch(), exchange.timeout_ms,
+        ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream), "ds_reduce_f64_sharded")
+    return out
+
+
 def ds_sum_f64_sharded(x_local: torch.Tensor, init: float = 0.0, group=None,
                        local_pair: Optional[Callable] = None,
-                       combine: Optional[Callable] = None) -> torch.Tensor:
+                       combine: Optional[Callable] = None,
+                       exchange: Optional[PeerExchange] = None) -> torch.Tensor:
     """DS sum of the concatenation of every rank's x_local, in rank order.
 
     Returns the f64 result (0-d) on every rank, bit-identical across ranks.
-    Per call: the local reduce, one all-gather of 8 bytes per rank, one
-    packed reduce of the [world, 2] pairs and one recombine.
+    With `exchange` (one node): two kernels, the local block partials and
+    one block that folds them, trades the totals over peer memory and folds
+    those.  Without: the local reduce, one all-gather of 8 bytes per rank,
+    one packed reduce of the [world, 2] pairs and one recombine.
     """
+    if exchange is not None:
+        return _sum_exchange_cuda(x_local, init, exchange, 0)
     world, _ = _world(group)
     local_pair = local_pair or _local_pair_cuda
     combine = combine or _combine_cuda

@@ -234,6 +234,42 @@ DS_API int ds_reduce_from_f64(const ds_buffer* in, const ds_buffer* init,
                               const ds_buffer* out_lo, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* ---- sharded reduce over the GPUs of one node ---------------------------- */
+
+/* The reference reduces on one device (DsTransformPass.cpp:376-448); these
+   entry points shard a full DS reduction of f64 data over one process per
+   GPU.  Each rank owns one exchange buffer of ds_exchange_bytes() bytes
+   (ds_exchange_alloc, which zeroes it and exports a CUDA IPC handle of
+   ds_exchange_handle_bytes() bytes) and maps every other rank's buffer with
+   ds_exchange_open.  Layout of a buffer: records[2][8] of 32 bytes at
+   offset (parity * 8 + r) * 32 -- f32 hi, f32 lo, i64 n, u64 epoch, u64 pad
+   -- and a sticky u32 error word at offset 512 (1 = a wait timed out). */
+DS_API size_t ds_exchange_bytes(void);
+DS_API size_t ds_exchange_handle_bytes(void);
+DS_API int ds_exchange_alloc(void** buffer, void* handle);
+DS_API int ds_exchange_open(const void* handle, void** buffer);
+DS_API int ds_exchange_close(void* buffer);
+DS_API int ds_exchange_free(void* buffer);
+/* Reads the error word of this rank's own buffer (synchronous copy). */
+DS_API int ds_exchange_error(const void* buffer, uint32_t* code);
+
+/* Full DS reduction of this rank's f64 shard `in` (all dimensions), the
+   ranks' DS totals exchanged through the exchange buffers, folded in rank
+   order (ranks with empty shards skipped) and combined with the rank-0 f64
+   init by `body`: every rank writes the same f64 bits to `out` (one
+   element).  buffers[r] is rank r's exchange buffer as mapped in this
+   process (buffers[rank] its own); world <= 8.  `epoch` numbers the calls
+   1, 2, 3, ... in the same sequence on every rank.  A rank that waits more
+   than timeout_ms for another writes NaN, sets the error word and returns
+   (read it with ds_exchange_error); the exchange must then be rebuilt.
+   Workspace: ds_reduce_f64_sharded_workspace_size(in) bytes, 8-byte
+   aligned. */
+DS_API size_t ds_reduce_f64_sharded_workspace_size(const ds_buffer* in);
+DS_API int ds_reduce_f64_sharded(const ds_buffer* in, const ds_buffer* init, int32_t body,
+                                 const ds_buffer* out, void* const* buffers, int32_t world,
+                                 int32_t rank, uint64_t epoch, int32_t timeout_ms,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- dot_general (DsTransformPass.cpp:337-370) --------------------------- */
 
 /* DS dot_general of SoA operands (lhs_hi, lhs_lo), (rhs_hi, rhs_lo) f32 with

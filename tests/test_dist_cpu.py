@@ -113,3 +113,104 @@ def test_shard_range_covers():
             assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         shard_range(10, 3, 3)
+
+
+class _FakeExchangeBackend:
+    """Stands in for the CUDA IPC calls: 'addresses' are integers, a handle
+    names its owner, and every call is logged.  `fail_open` makes opening
+    that rank's handle raise, as a failing cudaIpcOpenMemHandle would."""
+
+    def __init__(self, rank, fail_open=None, error_word=0):
+        self.rank, self.fail_open, self.error_word = rank, fail_open, error_word
+        self.log = []
+
+    def alloc(self):
+        self.log.append(("alloc",))
+        return 1000 + self.rank, f"h{self.rank}".encode()
+
+    def open(self, handle):
+        owner = int(handle.decode()[1:])
+        if owner == self.fail_open:
+            raise RuntimeError("open failed")
+        self.log.append(("open", owner))
+        return 2000 + owner
+
+    def close(self, ptr):
+        self.log.append(("close", ptr))
+
+    def free(self, ptr):
+        self.log.append(("free", ptr))
+
+    def error(self, ptr):
+        return self.error_word
+
+
+def _exchange_worker(rank, world, port, q):
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from ds_b200 import dist as dsd
+        fake = _FakeExchangeBackend(rank)
+        ex = dsd.PeerExchange(backend=fake, timeout_ms=250)
+        epochs = [ex.next_epoch() for _ in range(3)]
+        ptrs = list(ex.ptrs)
+        ex.close()
+        ex.close()  # idempotent
+        try:
+            ex.next_epoch()
+            after_close = "no error"
+        except RuntimeError:
+            after_close = "raised"
+        # an open that fails frees what was set up and raises
+        bad = _FakeExchangeBackend(rank, fail_open=(rank + 1) % world)
+        try:
+            dsd.PeerExchange(backend=bad)
+            failed = "no error"
+        except RuntimeError:
+            failed = "raised"
+        # a timed-out wait recorded in the error word surfaces in check()
+        ex2 = dsd.PeerExchange(backend=_FakeExchangeBackend(rank, error_word=1))
+        try:
+            ex2.check()
+            checked = "no error"
+        except RuntimeError as e:
+            checked = str(e)
+        ex2.close()
+        q.put((rank, epochs, ptrs, fake.log, after_close, failed, bad.log, checked))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, None, repr(e), None, None, None, None, None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_exchange_host_logic(world):
+    """Handles gathered in rank order, the own buffer in its own slot, every
+    peer mapped once and unmapped before the free; epochs count 1, 2, 3."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] is not None for r in results), results
+    for rank, epochs, ptrs, log, after_close, failed, bad_log, checked in results:
+        assert epochs == [1, 2, 3]
+        assert ptrs == [1000 + r if r == rank else 2000 + r for r in range(world)]
+        peers = [r for r in range(world) if r != rank]
+        assert log == [("alloc",)] + [("open", r) for r in peers] + \
+            [("close", 2000 + r) for r in peers] + [("free", 1000 + rank)]
+        assert after_close == "raised"
+        assert failed == "raised"
+        assert bad_log[-1] == ("free", 1000 + rank)  # own buffer released on failure
+        assert "timed out" in checked

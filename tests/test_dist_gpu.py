@@ -2,7 +2,9 @@
 
 - reduce: every rank sums its range, the (hi, lo) partials are all-gathered
   and folded in rank order; all ranks must hold the same bits, close to the
-  exact sum of the whole array.
+  exact sum of the whole array.  The same through the peer-memory exchange
+  (PeerExchange, NVLink P2P stores inside the reduce kernel; NVLS off), call
+  after call, with no error word set.
 - dot_general: rows of A per rank with B replicated by broadcast; each
   rank's block must equal the single-GPU product of those rows (the
   tensor-core product is exact up to its final rounding, so bit-equal).
@@ -44,9 +46,15 @@ def _worker(rank, world, port, q):
         x = np.where(np.arange(n) % 2 == 0, 1e8, -1e8) + \
             np.random.default_rng(1).uniform(0, 1, n) * 1e-3
         lo, hi = dsd.shard_range(n, rank, world)
-        r = dsd.ds_sum_f64_sharded(torch.from_numpy(x[lo:hi]).to(dev), init=0.25)
+        xl = torch.from_numpy(x[lo:hi]).to(dev)
+        r = dsd.ds_sum_f64_sharded(xl, init=0.25)
         sums = [torch.zeros((), dtype=torch.float64, device=dev) for _ in range(world)]
         dist.all_gather(sums, r)
+        ex = dsd.PeerExchange(timeout_ms=2000)
+        peer_vals = [float(dsd.ds_sum_f64_sharded(xl, init=0.25, exchange=ex))
+                     for _ in range(5)]
+        ex.check()
+        ex.close()
         # row-sharded GEMM with B broadcast from rank 0
         rng = np.random.default_rng(2)
         A = rng.uniform(-1, 1, (512, 768))
@@ -56,9 +64,10 @@ def _worker(rank, world, port, q):
         a0, a1 = dsd.shard_range(A.shape[0], rank, world)
         C_local = dsd.ds_matmul_f64_row_sharded(torch.from_numpy(A[a0:a1]).to(dev), B)
         torch.cuda.synchronize()
-        q.put((rank, float(r), [float(s) for s in sums], C_local.cpu().numpy(), (a0, a1)))
+        q.put((rank, float(r), [float(s) for s in sums], C_local.cpu().numpy(), (a0, a1),
+               peer_vals))
     except Exception as e:  # report instead of leaving the parent waiting
-        q.put((rank, None, repr(e), None, None))
+        q.put((rank, None, repr(e), None, None, None))
         raise
     finally:
         dist.destroy_process_group()
@@ -81,10 +90,13 @@ def test_sharded_sum_and_gemm():
     assert not errors, errors
     assert all(p.exitcode == 0 for p in procs)
     # identical bits on every rank
-    vals = {v for _, v, _, _, _ in results}
+    vals = {v for _, v, _, _, _, _ in results}
     assert len(vals) == 1
-    for _, v, allv, _, _ in results:
+    for _, v, allv, _, _, _ in results:
         assert set(allv) == {v}
+    peer = {pv for *_, pvs in results for pv in pvs}
+    assert len(peer) == 1  # every rank, every call
+    peer_val = peer.pop()
     import math
     n = 3_000_017
     x = np.where(np.arange(n) % 2 == 0, 1e8, -1e8) + np.random.default_rng(1).uniform(0, 1, n) * 1e-3
@@ -93,11 +105,12 @@ def test_sharded_sum_and_gemm():
     h, l = dso.ds_reduce_f64_seq(x, init=(0.25, 0.0))
     seq_err = abs(float(h) + float(l) - truth)
     assert abs(results[0][1] - truth) <= 4 * seq_err + 1e-9
+    assert abs(peer_val - truth) <= 4 * seq_err + 1e-9
     # the row blocks reassemble the single-GPU product
     from ds_b200 import ops
     rng = np.random.default_rng(2)
     A = rng.uniform(-1, 1, (512, 768))
     B = rng.uniform(-1, 1, (768, 384))
     full = ops.ds_matmul_f64(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()).cpu().numpy()
-    for _, _, _, C_local, (a0, a1) in results:
+    for _, _, _, C_local, (a0, a1), _ in results:
         assert np.array_equal(C_local, full[a0:a1])
