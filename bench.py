@@ -1,7 +1,8 @@
 """Benchmark of the DS hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemm|fused_add_mul|reduce|recurrence]
+                    [--workload gemm|fused_add_mul|reduce|recurrence|
+                                gemm_large|batched_dot]
 
 Default workload (the headline metric): DS dot_general C = A @ B with
 M = N = K = 4096, A and B float64 ~ U[-1, 1] drawn from default_rng(2) (A
@@ -240,7 +241,8 @@ def run_ours(args):
     fam = "ozaki_gemm"
     k_ms, k_n = _lib.profile_read(fam)
     launches = {}
-    for f in ("ozaki_split", "ozaki_split_rows", "ozaki_split_cols", "ozaki_gemm", "ozaki_crt",
+    for f in ("ozaki_split", "ozaki_split_rows", "ozaki_colmax", "ozaki_split_cols",
+              "ozaki_gemm", "ozaki_crt",
               "dot_simt", "dot_vec", "elementwise",
               "reduce", "recurrence"):
         t, n = _lib.profile_read(f)
@@ -664,6 +666,224 @@ def run_reference_stream(args):
                     "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# the large configuration: 65536 x 8192 x 8192 GEMM and the batched dot
+
+LARGE_M, LARGE_N, LARGE_K = 65536, 8192, 8192
+BATCH_DOTS, DOT_LEN = 4096, 65536
+LARGE_METRICS = {
+    "gemm_large": ("DS-GEMM GFLOP/s 65536x8192x8192 near-cancellation (rows of A sharded)",
+                   "GFLOP/s"),
+    "batched_dot": ("DS batched dot 4096 x 65536 HBM GB/s", "GB/s"),
+}
+
+
+def large_draw(offset, shape):
+    """Values 1 + 1e-7 u, u = default_rng(4).uniform(-1, 1) at stream position
+    `offset` onwards (one 64-bit draw per value, so any block of the A, B, X,
+    Y sequence is generated without the values before it)."""
+    bg = np.random.PCG64(4)
+    bg.advance(int(offset))
+    return 1.0 + 1e-7 * np.random.Generator(bg).uniform(-1.0, 1.0, shape)
+
+
+def large_inputs(workload, rank, world):
+    """This rank's share of the configuration drawn in the order A, B, X, Y:
+    gemm_large -> (A rows, B, first row); batched_dot -> (X rows, Y rows, first row)."""
+    if workload == "gemm_large":
+        r0, r1 = shard_rows(LARGE_M, rank, world)
+        A = large_draw(r0 * LARGE_K, (r1 - r0, LARGE_K))
+        B = large_draw(LARGE_M * LARGE_K, (LARGE_K, LARGE_N))
+        return A, B, r0
+    r0, r1 = shard_rows(BATCH_DOTS, rank, world)
+    base = LARGE_M * LARGE_K + LARGE_K * LARGE_N
+    X = large_draw(base + r0 * DOT_LEN, (r1 - r0, DOT_LEN))
+    Y = large_draw(base + BATCH_DOTS * DOT_LEN + r0 * DOT_LEN, (r1 - r0, DOT_LEN))
+    return X, Y, r0
+
+
+def shard_rows(n, rank, world):
+    base, rem = divmod(n, world)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def run_large(args):
+    """--workload gemm_large | batched_dot (strong scaling: the rows of A, or
+    the batch of dot products, are split across the ranks; B is replicated)."""
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from ds_b200 import _lib, ops
+    from oracle import exact
+    wl = args.workload
+    L, R, r0 = large_inputs(wl, rank, world)
+    dL = torch.from_numpy(L).to(dev)
+    dR = torch.from_numpy(R).to(dev)
+    stream = torch.cuda.current_stream()
+    if wl == "gemm_large":
+        step = lambda: ops.ds_matmul_f64(dL, dR)  # noqa: E731
+        fam = "ozaki_gemm"
+    else:
+        step = lambda: ops.ds_dot_general_f64(dL, dR, lhs_contracting=1,  # noqa: E731
+                                              rhs_contracting=1, lhs_batch=(0,),
+                                              rhs_batch=(0,))
+        fam = "dot_vec"
+    out = None
+    for _ in range(args.warmup):
+        out = step()
+    del out
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    _lib.profile_enable(False)
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    k_ms, k_n = _lib.profile_read(fam)
+    per = k_ms / max(k_n, 1)
+    launches = {}
+    for f in ("ozaki_split_rows", "ozaki_colmax", "ozaki_split_cols", "ozaki_gemm",
+              "ozaki_crt", "dot_vec"):
+        t_, n_ = _lib.profile_read(f)
+        if n_:
+            launches[f] = {"launches": n_, "ms_total": round(t_, 4)}
+    peaks, peak_src = measured_peaks()
+    metric, unit = LARGE_METRICS[wl]
+    line = {"metric": metric, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic: 1 + 1e-7 u, u = default_rng(4) U[-1,1] in the order A, B, X, Y",
+            "clocks": clk, "kernel_launches": launches,
+            "gpu_launches": int(sum(v["launches"] for v in launches.values()))}
+    if wl == "gemm_large":
+        flops = 2.0 * LARGE_M * LARGE_N * LARGE_K
+        line["value"] = round(flops / (ms * 1e-3) / 1e9, 1)
+        info = _lib.gemm_info(L.shape[0], LARGE_N, LARGE_K)
+        ach = info["tensor_ops_per_launch"] / (per * 1e-3) / 1e12
+        peak = 2.0 * peaks["bf16_tflops"]
+        line["roofline"] = {"bound": "tensor", "kernel": fam, "achieved": round(ach, 1),
+                            "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4),
+                            "traffic": None, "kernel_ms_per_launch": round(per, 4),
+                            "peak_source": f"2 x {peak_src} bf16_tflops"}
+        line["config"] = {"workload": "ds_dot_general_f64 65536x8192x8192, A rows sharded, "
+                                      "B replicated", "M": LARGE_M, "N": LARGE_N, "K": LARGE_K,
+                          "rows_per_rank": int(L.shape[0]), "parallelism": f"rows{world}",
+                          "l2": "inputs and output exceed the 126 MB L2"}
+        if rank == 0:
+            C = out.cpu().numpy()
+            rows, cols = exact.sample_indices(L.shape[0], LARGE_N, 64, seed=5)
+            truth = exact.exact_gemm_entries(L, R, rows, cols)
+            err = np.abs(C[rows, cols] - truth)
+            ref_err = reference_gemm_error(L, R, rows, cols, truth)
+            line["accuracy"] = {"max_abs_err_vs_exact": float(err.max()),
+                                "median_abs_err": float(np.median(err)),
+                                "reference_ds_path_max_abs_err": ref_err,
+                                "sampled_entries": int(len(rows)),
+                                "truth": "exact products summed with math.fsum"}
+    else:
+        nbytes = 2.0 * BATCH_DOTS * DOT_LEN * 8
+        line["value"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+        local_bytes = 2.0 * L.shape[0] * DOT_LEN * 8
+        ach = local_bytes / (per * 1e-3) / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": fam, "achieved": round(ach, 1),
+                            "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+                            "kernel_ms_per_launch": round(per, 4),
+                            "peak_source": f"{peak_src} hbm_gbs"}
+        line["config"] = {"workload": "ds_dot_general_f64 batched dot, batch 4096 x length "
+                                      "65536 (batch sharded)", "bytes_per_mac": 16,
+                          "dots_per_rank": int(L.shape[0]), "parallelism": f"batch{world}",
+                          "l2": "4 GiB of operands per step exceed the 126 MB L2"}
+        if rank == 0:
+            got = out.cpu().numpy()
+            idx = np.arange(0, L.shape[0], max(1, L.shape[0] // 16))
+            truth = np.array([exact.exact_dot(L[i], R[i]) for i in idx])
+            from oracle import ds_pass_ref
+            ah, al = ds_pass_ref.from_float(L[idx])
+            bh, bl = ds_pass_ref.from_float(R[idx])
+            p = np.einsum("ik,ik->i", ah, bh)
+            e = (np.einsum("ik,ik->i", ah, bl) + np.einsum("ik,ik->i", al, bh)) + \
+                np.einsum("ik,ik->i", al, bl)
+            h, l_ = ds_pass_ref.two_sum(p, e)
+            ref = ds_pass_ref.to_float(h, l_)
+            line["accuracy"] = {"max_abs_err_vs_exact": float(np.abs(got[idx] - truth).max()),
+                                "reference_ds_path_max_abs_err": float(np.abs(ref - truth).max()),
+                                "sampled_dots": int(len(idx))}
+    if world > 1:
+        dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+def run_reference_large(args):
+    """Reference arm of the large configuration on the host (rank 0 only):
+    the DS pass restated in NumPy on a bounded block per step (256 rows of A
+    times B, or 256 of the dot products)."""
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return None
+    from oracle import ds_pass_ref
+    wl = args.workload
+    m = 256
+    if wl == "gemm_large":
+        A = large_draw(0, (m, LARGE_K))
+        B = large_draw(LARGE_M * LARGE_K, (LARGE_K, LARGE_N))
+        fn = lambda: ds_pass_ref.dot_general_f64(A, B)  # noqa: E731
+        work, unit = 2.0 * m * LARGE_N * LARGE_K, "GFLOP/s"
+        sample = f"{m} rows of A times B (8192^2) per step"
+    else:
+        base = LARGE_M * LARGE_K + LARGE_K * LARGE_N
+        X = large_draw(base, (m, DOT_LEN))
+        Y = large_draw(base + BATCH_DOTS * DOT_LEN, (m, DOT_LEN))
+
+        def fn():
+            ah, al = ds_pass_ref.from_float(X)
+            bh, bl = ds_pass_ref.from_float(Y)
+            p = np.einsum("ik,ik->i", ah, bh)
+            e = (np.einsum("ik,ik->i", ah, bl) + np.einsum("ik,ik->i", al, bh)) + \
+                np.einsum("ik,ik->i", al, bl)
+            return ds_pass_ref.to_float(*ds_pass_ref.two_sum(p, e))
+        work, unit = 2.0 * m * DOT_LEN * 8, "GB/s"
+        sample = f"{m} of the 4096 dot products per step"
+    for _ in range(min(args.warmup, 1)):
+        fn()
+    steps = max(1, min(args.steps, 5))
+    t = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    dt = (time.perf_counter() - t) / steps
+    value = round(work / dt / 1e9, 2)
+    metric, _ = LARGE_METRICS[wl]
+    cb = {"value": value, "unit": unit, "cores": host_cores(), "kind": "port",
+          "sample": sample + ": the DS pass restated in NumPy (split, four float32 products "
+                             "with f32 accumulation, two_sum, recombine)"}
+    return {"impl": "reference", "metric": metric, "value": value, "unit": unit,
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "config": {"workload": f"{wl} (bounded host sample)"},
+            "cpu_baseline": cb, "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -681,12 +901,21 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload not in ("gemm",) + tuple(STREAM_METRICS):
+    if args.workload not in ("gemm",) + tuple(STREAM_METRICS) + tuple(LARGE_METRICS):
         raise SystemExit(f"unknown workload {args.workload!r}")
     if args.impl == "reference":
-        line = run_reference(args) if args.workload == "gemm" else run_reference_stream(args)
+        if args.workload == "gemm":
+            line = run_reference(args)
+        elif args.workload in LARGE_METRICS:
+            line = run_reference_large(args)
+        else:
+            line = run_reference_stream(args)
+    elif args.workload == "gemm":
+        line = run_ours(args)
+    elif args.workload in LARGE_METRICS:
+        line = run_large(args)
     else:
-        line = run_ours(args) if args.workload == "gemm" else run_stream(args)
+        line = run_stream(args)
     if line is not None:
         print(json.dumps(line))
 

@@ -72,9 +72,14 @@ __host__ __device__ constexpr int mod_of(int l) {
 // ---------------------------------------------------------------------------
 // Host-side constants: P from K, and the CRT weights in 40-bit limbs.
 
+// The weights and the modulus product split at bit kCrtSplit: W = W_hi 2^70 +
+// W_lo.  W_hi < 2^40.2, so the 14 products r W_hi (r < 2^8) sum exactly in
+// f64 (< 2^53); W_lo < 2^70 is rounded to 53 bits.
+constexpr int kCrtSplit = 70;
+
 struct CrtConsts {
-  double w[kL][3];  // W_l = (Mprod/m_l) * ((Mprod/m_l)^-1 mod m_l), limbs of 40 bits
-  double mlimb[3];  // Mprod in 40-bit limbs
+  double w[kL][2];  // W_l = (Mprod/m_l) * ((Mprod/m_l)^-1 mod m_l): {W_hi, W_lo}
+  double mlimb[2];  // Mprod: {hi, lo}
   double inv_m;     // 1 / Mprod
   double log2_m;
 };
@@ -87,7 +92,8 @@ const CrtConsts& crt_consts() {
   std::call_once(once, [] {
     u128 M = 1;
     for (int l = 0; l < kL; ++l) M *= static_cast<u128>(mod_of(l));
-    const u128 mask = (static_cast<u128>(1) << 40) - 1;
+    const u128 lo_mask = (static_cast<u128>(1) << kCrtSplit) - 1;
+    auto to_double = [](u128 v) { return static_cast<double>(v); };  // rounded to nearest
     for (int l = 0; l < kL; ++l) {
       const int m = mod_of(l);
       const u128 Ml = M / m;
@@ -95,14 +101,12 @@ const CrtConsts& crt_consts() {
       int inv = 1;
       while ((r * inv) % m != 1) ++inv;  // m <= 256: trivial search
       const u128 W = Ml * static_cast<u128>(inv);  // < M
-      c.w[l][0] = static_cast<double>(static_cast<uint64_t>(W & mask));
-      c.w[l][1] = static_cast<double>(static_cast<uint64_t>((W >> 40) & mask));
-      c.w[l][2] = static_cast<double>(static_cast<uint64_t>(W >> 80));
+      c.w[l][0] = static_cast<double>(static_cast<uint64_t>(W >> kCrtSplit));
+      c.w[l][1] = to_double(W & lo_mask);
     }
-    c.mlimb[0] = static_cast<double>(static_cast<uint64_t>(M & mask));
-    c.mlimb[1] = static_cast<double>(static_cast<uint64_t>((M >> 40) & mask));
-    c.mlimb[2] = static_cast<double>(static_cast<uint64_t>(M >> 80));
-    const double Md = c.mlimb[2] * 0x1p80 + c.mlimb[1] * 0x1p40 + c.mlimb[0];
+    c.mlimb[0] = static_cast<double>(static_cast<uint64_t>(M >> kCrtSplit));
+    c.mlimb[1] = to_double(M & lo_mask);
+    const double Md = to_double(M);
     c.inv_m = 1.0 / Md;
     c.log2_m = std::log2(Md);
   });
@@ -177,51 +181,57 @@ __device__ __forceinline__ uint64_t quantise(double v, int shift) {
   return static_cast<uint64_t>(__double_as_longlong(y)) & ((1ull << 52) - 1);
 }
 
-// t = h * 2^32 + mid * 2^16 + low, all limbs non-negative (h < 2^20).
+// t = hi * 2^32 + lo (hi < 2^20): the seven bytes of t in two words.
 struct Limbs {
-  uint32_t h, mid, low;
+  uint32_t lo, hi;
 };
 
 __device__ __forceinline__ Limbs limbs_of(uint64_t t) {
-  const uint32_t lo32 = static_cast<uint32_t>(t);
-  return Limbs{static_cast<uint32_t>(t >> 32), lo32 >> 16, lo32 & 0xFFFFu};
+  return Limbs{static_cast<uint32_t>(t), static_cast<uint32_t>(t >> 32)};
 }
 
-// Residue in [0, m) of the unbiased integer t - 2^51 modulo m = mod_of(l):
-// a linear map of the limbs (< 2^29, no overflow) plus the constant that
-// cancels the bias, then one unsigned modulo by a constant.
+// 2^e mod m, for the byte weights below.
+__host__ __device__ constexpr uint32_t pow2_mod(int e, uint32_t m) {
+  uint32_t r = 1 % m;
+  for (int i = 0; i < e; ++i) r = (r * 2u) % m;
+  return r;
+}
+
+// Four byte weights packed for __dp4a: byte j of the word is 2^(8 (j + j0)) mod m.
+__host__ __device__ constexpr uint32_t byte_weights(int j0, int count, uint32_t m) {
+  uint32_t w = 0;
+  for (int j = 0; j < count; ++j) w |= pow2_mod(8 * (j0 + j), m) << (8 * j);
+  return w;
+}
+
+// Residue in [0, m) of the unbiased integer t - 2^51 modulo m = mod_of(l).
+// The bytes of t dotted with the weights 2^(8j) mod m (two byte dot
+// products), plus the constant that cancels the bias, give s < 2^19 with
+// s = t - 2^51 (mod m); then s mod m = s - m * umulhi(s, ceil(2^32 / m)),
+// exact because s * (ceil(2^32 / m) * m - 2^32) < 2^19 * 2^8 < 2^32.
+// m = 256 is the low byte of t (2^51 = 0 mod 256).
 template <int l>
 __device__ __forceinline__ uint32_t residue(const Limbs& x) {
   constexpr uint32_t m = mod_of(l);
-  constexpr uint32_t c16 = 65536u % m;
-  constexpr uint32_t c32 = (c16 * c16) % m;
-  constexpr uint32_t bias = static_cast<uint32_t>((1ull << 51) % m);
-  constexpr uint32_t unbias = (m - bias) % m;
-  return (x.h * c32 + x.mid * c16 + x.low + unbias) % m;
-}
-
-// Residues of 16 consecutive values -> one 16-byte store per modulus plane.
-template <int l>
-__device__ __forceinline__ void store_plane(const Limbs (&x)[16], uint8_t* plane) {
-  uint32_t w[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    w[q] = residue<l>(x[q * 4]) | (residue<l>(x[q * 4 + 1]) << 8) |
-           (residue<l>(x[q * 4 + 2]) << 16) | (residue<l>(x[q * 4 + 3]) << 24);
-  }
-  *reinterpret_cast<uint4*>(plane) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-template <int l = 0>
-__device__ __forceinline__ void store_all_planes(const Limbs (&x)[16], uint8_t* base,
-                                                 size_t plane_stride) {
-  if constexpr (l < kL) {
-    store_plane<l>(x, base + l * plane_stride);
-    store_all_planes<l + 1>(x, base, plane_stride);
+  if constexpr (m == 256u) {
+    return x.lo & 0xFFu;
+  } else {
+    constexpr uint32_t w_lo = byte_weights(0, 4, m);
+    constexpr uint32_t w_hi = byte_weights(4, 3, m);
+    constexpr uint32_t unbias = (m - pow2_mod(51, m)) % m;
+    constexpr uint32_t magic = 0xFFFFFFFFu / m + 1u;  // ceil(2^32 / m), m not a power of 2
+    const uint32_t s = __dp4a(x.lo, w_lo, __dp4a(x.hi, w_hi, unbias));
+    return s - __umulhi(s, magic) * m;
   }
 }
 
-// The same for N = 4 or 8 consecutive values (one 4- or 8-byte store).
+// Four residues (each < 256) as the bytes of one word: three byte permutes.
+__device__ __forceinline__ uint32_t pack4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  return __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
+}
+
+// Residues of N = 4, 8 or 16 consecutive values -> one 4-, 8- or 16-byte
+// store per modulus plane.
 template <int N, int l = 0>
 __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* base,
                                                size_t plane_stride) {
@@ -229,13 +239,15 @@ __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* bas
     uint32_t w[N / 4];
 #pragma unroll
     for (int q = 0; q < N / 4; ++q)
-      w[q] = residue<l>(x[q * 4]) | (residue<l>(x[q * 4 + 1]) << 8) |
-             (residue<l>(x[q * 4 + 2]) << 16) | (residue<l>(x[q * 4 + 3]) << 24);
+      w[q] = pack4(residue<l>(x[q * 4]), residue<l>(x[q * 4 + 1]), residue<l>(x[q * 4 + 2]),
+                   residue<l>(x[q * 4 + 3]));
     uint8_t* dst = base + l * plane_stride;
     if constexpr (N == 4) {
       *reinterpret_cast<uint32_t*>(dst) = w[0];
-    } else {
+    } else if constexpr (N == 8) {
       *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
     store_planes_n<N, l + 1>(x, base, plane_stride);
   }
@@ -258,24 +270,61 @@ __device__ __forceinline__ int shift_from_code(int code, int P) {
   return P - (code - kExpBias);
 }
 
-// Operand rows contiguous in K (s_k == 1): one block per (row, batch); pass
-// 1 finds the row maximum, pass 2 (reading the row again, mostly from L1/L2)
-// writes 16 residues per thread per modulus.
-__global__ void __launch_bounds__(256)
+// Operand rows contiguous in K (s_k == 1): one block per (row, batch), of
+// 256 threads, or 512 for rows longer than 4096.  An f64 row of at most 16
+// values per thread at a 16-byte aligned address is read once into
+// registers (four groups of four consecutive k, 4 * blockDim.x apart, so
+// every load is coalesced), reduced to the row maximum and quantised from
+// registers.  Other rows take two passes: the maximum, then the values again
+// (mostly from L2).  Four residues per thread per modulus make one coalesced
+// 4-byte store.
+constexpr int kSplitRowsMaxThreads = 512;
+
+__host__ __device__ constexpr int split_rows_threads(int64_t K) {
+  return K > 4096 && K <= 16 * kSplitRowsMaxThreads ? kSplitRowsMaxThreads : 256;
+}
+
+__global__ void __launch_bounds__(kSplitRowsMaxThreads)
 split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
                     int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts) {
-  __shared__ double s_max[8];
-  __shared__ int s_bad[8];
+  __shared__ double s_max[kSplitRowsMaxThreads / 32];
+  __shared__ int s_bad[kSplitRowsMaxThreads / 32];
   const int64_t r = blockIdx.x, b = blockIdx.y;
   const bool live = r < rows;
   const int64_t base = b * o.s_b + r * o.s_r;
+  const bool vec = o.f64 && o.s_k == 1 && (reinterpret_cast<uintptr_t>(o.f64 + base) & 15) == 0;
+  const int64_t group = 4 * static_cast<int64_t>(blockDim.x);  // k covered by one group
+  const bool in_regs = vec && K <= 4 * group;
+  double v[16];
   double mx = 0.0;
   bool bad = false;
-  if (live) {
+  if (in_regs) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int64_t k0 = g * group + threadIdx.x * 4;
+      if (live && k0 + 4 <= K) {
+        const double2* p = reinterpret_cast<const double2*>(o.f64 + base + k0);
+        const double2 v01 = __ldcs(p), v23 = __ldcs(p + 1);
+        v[g * 4 + 0] = v01.x;
+        v[g * 4 + 1] = v01.y;
+        v[g * 4 + 2] = v23.x;
+        v[g * 4 + 3] = v23.y;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          v[g * 4 + j] = (live && k0 + j < K) ? o.f64[base + k0 + j] : 0.0;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      bad |= !isfinite(v[j]);
+      mx = fmax(mx, fabs(v[j]));
+    }
+  } else if (live) {
     for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-      const double v = op_value(o, base + k * o.s_k);
-      bad |= !isfinite(v);
-      mx = fmax(mx, fabs(v));
+      const double x = op_value(o, base + k * o.s_k);
+      bad |= !isfinite(x);
+      mx = fmax(mx, fabs(x));
     }
   }
 #pragma unroll
@@ -290,7 +339,7 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   __syncthreads();
   mx = 0.0;
   bad = false;
-  for (int w = 0; w < 8; ++w) {
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
     mx = fmax(mx, s_max[w]);
     bad |= s_bad[w] != 0;
   }
@@ -300,104 +349,168 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   const int sh = zero ? 0 : shift;
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
   uint8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
-  // Four consecutive k per thread: two 16-byte loads (f64, aligned rows) and
-  // one 4-byte store per plane, both coalesced across the warp.
-  const bool vec = o.f64 && o.s_k == 1 && (reinterpret_cast<uintptr_t>(o.f64 + base) & 15) == 0;
+  if (in_regs) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int64_t k0 = g * group + threadIdx.x * 4;
+      if (k0 < Kp) {
+        Limbs x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(zero ? 0.0 : v[g * 4 + j], sh));
+        store_planes_n<4>(x, row_out + k0, plane_stride);
+      }
+    }
+    return;
+  }
   for (int64_t k0 = static_cast<int64_t>(threadIdx.x) * 4; k0 < Kp; k0 += 4 * blockDim.x) {
-    double v[4];
+    double w[4];
     if (!zero && vec && k0 + 4 <= K) {
       const double2* p = reinterpret_cast<const double2*>(o.f64 + base + k0);
       const double2 v01 = p[0], v23 = p[1];
-      v[0] = v01.x;
-      v[1] = v01.y;
-      v[2] = v23.x;
-      v[3] = v23.y;
+      w[0] = v01.x;
+      w[1] = v01.y;
+      w[2] = v23.x;
+      w[3] = v23.y;
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int64_t k = k0 + j;
-        v[j] = (zero || k >= K) ? 0.0 : op_value(o, base + k * o.s_k);
+        w[j] = (zero || k >= K) ? 0.0 : op_value(o, base + k * o.s_k);
       }
     }
     Limbs x[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(v[j], sh));
+    for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(w[j], sh));
     store_planes_n<4>(x, row_out + k0, plane_stride);
   }
 }
 
-// Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major),
-// pass 1: per-row maximum over a 256-deep slab of K per block, merged across
-// blocks with atomicMax on an encoded exponent (codes start at 0).
-__global__ void __launch_bounds__(256)
-colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
-              int* __restrict__ codes) {
-  __shared__ double s_max[8][32];
-  __shared__ int s_bad[8][32];
-  const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * 32 + lane, b = blockIdx.z;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 256;
-  const int64_t k1 = k0 + 256 < K ? k0 + 256 : K;
-  double mx = 0.0;
-  bool bad = false;
-  if (r < rows) {
-    for (int64_t k = k0 + ty; k < k1; k += 8) {
-      const double v = op_value(o, b * o.s_b + r * o.s_r + k * o.s_k);
-      bad |= !isfinite(v);
-      mx = fmax(mx, fabs(v));
-    }
-  }
-  s_max[ty][lane] = mx;
-  s_bad[ty][lane] = bad;
-  __syncthreads();
-  if (ty == 0 && r < rows) {
-    for (int w = 1; w < 8; ++w) {
-      mx = fmax(mx, s_max[w][lane]);
-      bad |= s_bad[w][lane] != 0;
-    }
-    const int code = bad ? kExpNonFinite : (mx == 0.0 ? 0 : ilogb(mx) + 1 + kExpBias);
-    if (code != 0) atomicMax(&codes[b * rows_pad + r], code);
+// Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major):
+// blocks of 64 rows x 256 K.  Pairs of adjacent rows load as one 16-byte
+// value when the layout allows it (paired_rows).
+constexpr int kColTileR = 64;
+
+__device__ __forceinline__ bool paired_rows(const DotOperand& o) {
+  return o.f64 && o.s_r == 1 && (reinterpret_cast<uintptr_t>(o.f64) & 15) == 0 &&
+         (o.s_k & 1) == 0 && (o.s_b & 1) == 0;
+}
+
+// Values of rows (row, row + 1) at k; zero outside the operand.
+__device__ __forceinline__ void load_row_pair(const DotOperand& o, bool paired, int64_t b,
+                                              int64_t row, int64_t k, int64_t rows, int64_t K,
+                                              double& x0, double& x1) {
+  x0 = x1 = 0.0;
+  if (k >= K) return;
+  const int64_t off = b * o.s_b + row * o.s_r + k * o.s_k;
+  if (paired && row + 2 <= rows) {
+    const double2 d = __ldcs(reinterpret_cast<const double2*>(o.f64 + off));
+    x0 = d.x;
+    x1 = d.y;
+  } else {
+    if (row < rows) x0 = op_value(o, off);
+    if (row + 1 < rows) x1 = op_value(o, off + o.s_r);
   }
 }
 
-// Pass 2: one block per (32 rows, 64 K) tile: values are quantised into a
-// shared-memory tile (loads coalesced along rows), then written transposed
-// (K-major), 8 residues per thread per modulus.
+// Pass 1: per-row maximum over a kColmaxSlab-deep slab of K per block, merged
+// across blocks with atomicMax on an encoded exponent (codes start at 0).
+constexpr int kColmaxSlab = 128;
+
+__global__ void __launch_bounds__(256, 6)
+colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
+              int* __restrict__ codes) {
+  __shared__ double s_max[8][kColTileR];
+  __shared__ int s_bad[8][kColTileR];
+  const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kColTileR, b = blockIdx.z;
+  const int64_t row = r0 + 2 * lane;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * kColmaxSlab;
+  double m0 = 0.0, m1 = 0.0;
+  bool bad = false, bad1 = false;
+  const int64_t k1 = k0 + kColmaxSlab < K ? k0 + kColmaxSlab : K;
+  if (paired_rows(o) && row + 2 <= rows) {
+    const double* p = o.f64 + b * o.s_b + row;
+#pragma unroll 4
+    for (int64_t k = k0 + ty; k < k1; k += 8) {
+      const double2 d = __ldcs(reinterpret_cast<const double2*>(p + k * o.s_k));
+      bad |= !isfinite(d.x);
+      bad1 |= !isfinite(d.y);
+      m0 = fmax(m0, fabs(d.x));
+      m1 = fmax(m1, fabs(d.y));
+    }
+  } else {
+    for (int64_t k = k0 + ty; k < k1; k += 8) {
+      double x0, x1;
+      load_row_pair(o, false, b, row, k, rows, K, x0, x1);
+      bad |= !isfinite(x0);
+      bad1 |= !isfinite(x1);
+      m0 = fmax(m0, fabs(x0));
+      m1 = fmax(m1, fabs(x1));
+    }
+  }
+  s_max[ty][2 * lane] = m0;
+  s_max[ty][2 * lane + 1] = m1;
+  s_bad[ty][2 * lane] = bad;
+  s_bad[ty][2 * lane + 1] = bad1;
+  __syncthreads();
+  if (threadIdx.x < kColTileR) {
+    const int64_t r = r0 + threadIdx.x;
+    double mx = 0.0;
+    bool nf = false;
+    for (int w = 0; w < 8; ++w) {
+      mx = fmax(mx, s_max[w][threadIdx.x]);
+      nf |= s_bad[w][threadIdx.x] != 0;
+    }
+    const int code = nf ? kExpNonFinite : (mx == 0.0 ? 0 : ilogb(mx) + 1 + kExpBias);
+    if (r < rows && code != 0) atomicMax(&codes[b * rows_pad + r], code);
+  }
+}
+
+// Pass 2: one block per (64 rows, 64 K) tile.  Values are loaded along rows
+// (coalesced), quantised into a shared-memory tile, and written transposed
+// (K-major): each thread turns 16 consecutive k of one row into one 16-byte
+// store per modulus.  Warps read the tile along rows (conflict-free).
 constexpr int kColTileK = 64;
+constexpr int kColTilePitch = kColTileR + 2;  // 16-byte aligned rows of the tile
 
 __global__ void __launch_bounds__(256)
 split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
                   int64_t batch, int P, const int* __restrict__ codes,
                   uint8_t* __restrict__ planes, int* __restrict__ shifts) {
-  __shared__ uint64_t tile[kColTileK][33];
-  __shared__ int s_shift[32];
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, b = blockIdx.z;
+  __shared__ __align__(16) uint64_t tile[kColTileK][kColTilePitch];
+  __shared__ int s_shift[kColTileR];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kColTileR, b = blockIdx.z;
   const int64_t kc = static_cast<int64_t>(blockIdx.y) * kColTileK;
-  if (threadIdx.x < 32) {
+  if (threadIdx.x < kColTileR) {
     const int64_t r = r0 + threadIdx.x;
     const int sh = r < rows ? shift_from_code(codes[b * rows_pad + r], P) : 0;
     s_shift[threadIdx.x] = sh;
     if (blockIdx.y == 0) shifts[b * rows_pad + r] = sh;
   }
   __syncthreads();
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < kColTileK * 32; idx += blockDim.x) {
-    const int kk = idx >> 5, rr = idx & 31;
-    const int64_t k = kc + kk, row = r0 + rr;
-    const int sh = s_shift[rr];
-    const bool use = row < rows && k < K && sh != kShiftNonFinite;
-    const double v = use ? op_value(o, b * o.s_b + row * o.s_r + k * o.s_k) : 0.0;
-    tile[kk][rr] = quantise(v, use ? sh : 0);
+  const bool paired = paired_rows(o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double x[8][2];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    load_row_pair(o, paired, b, r0 + 2 * lane, kc + warp + 8 * i, rows, K, x[i][0], x[i][1]);
+  const int sh0 = s_shift[2 * lane], sh1 = s_shift[2 * lane + 1];
+  const bool z0 = sh0 == kShiftNonFinite, z1 = sh1 == kShiftNonFinite;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint64_t t0 = quantise(z0 ? 0.0 : x[i][0], z0 ? 0 : sh0);
+    const uint64_t t1 = quantise(z1 ? 0.0 : x[i][1], z1 ? 0 : sh1);
+    *reinterpret_cast<ulonglong2*>(&tile[warp + 8 * i][2 * lane]) = make_ulonglong2(t0, t1);
   }
   __syncthreads();
-  const int my_row = threadIdx.x >> 3, my_grp = threadIdx.x & 7;
-  Limbs x[8];
+  const int my_row = lane + 32 * (warp & 1), my_grp = warp >> 1;
+  Limbs q[16];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = limbs_of(tile[my_grp * 8 + j][my_row]);
+  for (int j = 0; j < 16; ++j) q[j] = limbs_of(tile[my_grp * 16 + j][my_row]);
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  store_planes_n<8>(x, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
-                           my_grp * 8,
-                    plane_stride);
+  store_planes_n<16>(q, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
+                            my_grp * 16,
+                     plane_stride);
 }
 
 // ---------------------------------------------------------------------------
@@ -1001,8 +1114,8 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // Step 3: CRT reconstruction and scaling.
 
 struct CrtParams {
-  double w[kL][3];
-  double mlimb[3];
+  double w[kL][2];
+  double mlimb[2];
   double inv_m;
   int64_t batch, M, N, Mp, Np, K;
   const uint8_t* cres;
@@ -1024,12 +1137,19 @@ __device__ __forceinline__ void put_result(const DotResult& c, int64_t idx, doub
 }
 
 constexpr int kCrtThreads = 128;
-constexpr int kCrtCols = 8;  // consecutive outputs per thread
+constexpr int kCrtCols = 4;  // consecutive outputs per thread
 
-// blockIdx.y strides over the batch*M output rows, blockIdx.x * 1024 is the
-// first column of the block; each thread rebuilds 8 consecutive outputs from
-// one 8-byte load per residue plane.
-__global__ void __launch_bounds__(kCrtThreads)
+// Byte q of `word` as an f64: the bits of 2^52 + byte, minus 2^52 -- one
+// add on the FP64 pipe instead of a quarter-rate integer conversion.
+__device__ __forceinline__ double byte_to_f64(uint32_t word, int q) {
+  const uint32_t byte = __byte_perm(word, 0u, 0x4440u + static_cast<uint32_t>(q));
+  return __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(byte)), 0x1p52);
+}
+
+// blockIdx.y strides over the batch*M output rows, blockIdx.x * 512 is the
+// first column of the block; each thread rebuilds 4 consecutive outputs from
+// one 4-byte load per residue plane.
+__global__ void __launch_bounds__(kCrtThreads, 8)
 crt_kernel(CrtParams p) {
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
@@ -1040,22 +1160,18 @@ crt_kernel(CrtParams p) {
     const int64_t b = row / p.M, i = row - b * p.M;
     const int sa = p.sa[b * p.Mp + i];
     const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
-    double s0[kCrtCols], s1[kCrtCols], s2[kCrtCols];
+    double s_hi[kCrtCols], s_lo[kCrtCols];
 #pragma unroll
-    for (int q = 0; q < kCrtCols; ++q) s0[q] = s1[q] = s2[q] = 0.0;
+    for (int q = 0; q < kCrtCols; ++q) s_hi[q] = s_lo[q] = 0.0;
 #pragma unroll
     for (int l = 0; l < kL; ++l) {
-      const uint2 v = *reinterpret_cast<const uint2*>(p.cres + l * plane + at);
-      const double w0 = p.w[l][0], w1 = p.w[l][1], w2 = p.w[l][2];
+      const uint32_t word = __ldcs(reinterpret_cast<const unsigned int*>(p.cres + l * plane + at));
+      const double w_hi = p.w[l][0], w_lo = p.w[l][1];
 #pragma unroll
       for (int q = 0; q < kCrtCols; ++q) {
-        const uint32_t word = q < 4 ? v.x : v.y;
-        // (the integer -> f64 conversions run on the XU pipe, beside the
-        // FP64 FMAs)
-        const double r = static_cast<double>((word >> (8 * (q & 3))) & 0xFFu);
-        s0[q] = __fma_rn(r, w0, s0[q]);
-        s1[q] = __fma_rn(r, w1, s1[q]);
-        s2[q] = __fma_rn(r, w2, s2[q]);
+        const double r = byte_to_f64(word, q);
+        s_hi[q] = __fma_rn(r, w_hi, s_hi[q]);  // exact
+        s_lo[q] = __fma_rn(r, w_lo, s_lo[q]);
       }
     }
 #pragma unroll
@@ -1075,14 +1191,15 @@ crt_kernel(CrtParams p) {
                op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
         out = s;
       } else {
-        // C = S - round(S / Mprod) * Mprod, limb by limb (every term exact).
-        const double approx = __fma_rn(s2[q], 0x1p80, s1[q] * 0x1p40);
+        // C = S - round(S / Mprod) * Mprod: the quotient is exact (S / Mprod
+        // lies within 0.22 of an integer), the high limb difference is an
+        // exact integer below 2^53, and the low limb carries the only
+        // rounding (below 2^34 units of C_int).
+        const double approx = __fma_rn(s_hi[q], 0x1p70, s_lo[q]);
         const double qt = rint(approx * p.inv_m);
-        const double t0 = __fma_rn(-qt, p.mlimb[0], s0[q]);
-        const double t1 = __fma_rn(-qt, p.mlimb[1], s1[q]);
-        const double t2 = __fma_rn(-qt, p.mlimb[2], s2[q]);
-        const double hi = __fma_rn(t2, 0x1p40, t1);
-        out = scale2(scale2(__fma_rn(hi, 0x1p40, t0), -sa), -sb);
+        const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi[q]);
+        const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo[q]);
+        out = scale2(scale2(__fma_rn(t_hi, 0x1p70, t_lo), -sa), -sb);
       }
       put_result(p.c, row * p.N + j, out);
     }
@@ -1186,14 +1303,19 @@ int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_
   if (o.s_k == 1 || rows == 1) {
     ProfileScope prof("ozaki_split_rows", s);
     dim3 grid(static_cast<unsigned>(rows_pad), static_cast<unsigned>(batch));
-    split_kmajor_kernel<<<grid, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, planes, shifts);
+    split_kmajor_kernel<<<grid, split_rows_threads(K), 0, s>>>(o, rows, K, rows_pad, Kp, batch,
+                                                               P, planes, shifts);
   } else {
-    ProfileScope prof("ozaki_split_cols", s);
     DSB_CUDA_TRY(cudaMemsetAsync(codes, 0, sizeof(int) * batch * rows_pad, s));
-    dim3 g1(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>((K + 255) / 256),
+    dim3 g1(static_cast<unsigned>(rows_pad / kColTileR),
+            static_cast<unsigned>((K + kColmaxSlab - 1) / kColmaxSlab),
             static_cast<unsigned>(batch));
-    colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
-    dim3 g2(static_cast<unsigned>(rows_pad / 32), static_cast<unsigned>(Kp / kColTileK),
+    {
+      ProfileScope prof("ozaki_colmax", s);
+      colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
+    }
+    ProfileScope prof("ozaki_split_cols", s);
+    dim3 g2(static_cast<unsigned>(rows_pad / kColTileR), static_cast<unsigned>(Kp / kColTileK),
             static_cast<unsigned>(batch));
     split_cols_kernel<<<g2, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
   }

@@ -1,0 +1,19 @@
+"""Host-side pieces of bench.py: the sharded input draws of the large
+configuration must be exactly the slices of one sequential draw."""
+import numpy as np
+
+import bench
+
+
+def test_large_draw_is_a_slice_of_the_sequential_draw():
+    full = 1.0 + 1e-7 * np.random.default_rng(4).uniform(-1.0, 1.0, (40, 24))
+    for r0, r1 in ((0, 7), (7, 23), (23, 40)):
+        part = bench.large_draw(r0 * 24, (r1 - r0, 24))
+        assert np.array_equal(part, full[r0:r1])
+
+
+def test_shard_rows_tile_the_range():
+    for n, world in ((65536, 8), (4096, 3), (10, 4)):
+        parts = [bench.shard_rows(n, r, world) for r in range(world)]
+        assert parts[0][0] == 0 and parts[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))

@@ -2,10 +2,11 @@
 
 The GPU kernel (ds-experiment_b200/csrc/dot_ozaki.cu) quantises each operand
 row to a P-bit integer, multiplies residues modulo 14 coprime moduli exactly,
-and rebuilds the product by the Chinese remainder theorem in three 40-bit f64
-limbs.  This restates those steps in NumPy/Python integers at small sizes to
-check that the chosen P keeps the CRT exact and that the limb arithmetic
-reproduces the exact integer product.
+and rebuilds the product by the Chinese remainder theorem in two f64 limbs
+(the weights split at bit 70).  This restates those steps in NumPy/Python
+integers at small sizes: the byte-dot-product residues of the biased
+quantised integers, the unsigned residue GEMM, and the two-limb
+reconstruction, whose only rounding is far below the quantisation error.
 """
 import math
 
@@ -14,7 +15,7 @@ import numpy as np
 from oracle import exact
 
 MODULI = [256, 255, 253, 251, 247, 241, 239, 233, 229, 227, 223, 217, 211, 199]
-MASK40 = (1 << 40) - 1
+SPLIT = 70  # W = W_hi * 2^70 + W_lo
 
 
 def consts():
@@ -56,34 +57,62 @@ def quantise(X, P):
     return ints, shifts
 
 
-def sym_residue(x, m):
-    r = x % m
-    if r > (m - 1) // 2:
-        r -= m
-    return r
+def byte_residue(x_int, m):
+    """The split kernel's residue: t = x_int + 2^51 as seven bytes, dotted
+    with the weights 2^(8j) mod m (two 4-byte dot products), plus the
+    constant that cancels the bias, then s - m * umulhi(s, ceil(2^32 / m))."""
+    t = x_int + 2 ** 51
+    assert 0 <= t < 2 ** 52
+    if m == 256:
+        return t & 255
+    w = [pow(2, 8 * j, m) for j in range(7)]
+    unbias = (m - pow(2, 51, m)) % m
+    s = sum(((t >> (8 * j)) & 255) * w[j] for j in range(7)) + unbias
+    assert s < 2 ** 19
+    magic = (2 ** 32 - 1) // m + 1
+    return s - ((s * magic) >> 32) * m
+
+
+def test_byte_residues():
+    rng = np.random.default_rng(3)
+    edges = [0, 1, -1, 2 ** 50, -(2 ** 50), 2 ** 50 - 1, 12345678901234]
+    vals = edges + [int(v) for v in rng.integers(-(2 ** 50), 2 ** 50, 20000)]
+    for m in MODULI:
+        for x in vals:
+            assert byte_residue(x, m) == x % m
 
 
 def crt_limbs(residues):
-    """The kernel's f64 three-limb reconstruction, step by step."""
+    """The kernel's two-limb f64 reconstruction, step by step: s_hi exact,
+    s_lo rounded, q = rint(S / M) exact, t_hi exact, one final rounding."""
     M, W = consts()
-    wl = [(w & MASK40, (w >> 40) & MASK40, w >> 80) for w in W]
-    ml = (M & MASK40, (M >> 40) & MASK40, M >> 80)
-    s = [0.0, 0.0, 0.0]
-    for r, w in zip(residues, wl):
-        for j in range(3):
-            s[j] = float(r) * float(w[j]) + s[j]  # exact: all < 2^53
-    approx = s[2] * 2.0 ** 80 + s[1] * 2.0 ** 40
-    Md = ml[2] * 2.0 ** 80 + ml[1] * 2.0 ** 40 + ml[0]
-    q = float(np.rint(approx * (1.0 / Md)))
-    t = [s[j] - q * float(ml[j]) for j in range(3)]
-    hi = t[2] * 2.0 ** 40 + t[1]
-    return hi * 2.0 ** 40 + t[0], (s, q, t)
+    lo_mask = (1 << SPLIT) - 1
+    w_hi = [float(w >> SPLIT) for w in W]
+    w_lo = [float(w & lo_mask) for w in W]
+    m_hi, m_lo = float(M >> SPLIT), float(M & lo_mask)
+    s_hi = s_lo = 0.0
+    for r, wh, wl in zip(residues, w_hi, w_lo):
+        s_hi = float(r) * wh + s_hi  # exact: < 2^53
+        s_lo = float(r) * wl + s_lo  # rounded (numpy has no fma; error within the bound)
+    approx = s_hi * 2.0 ** SPLIT + s_lo
+    q = float(np.rint(approx * (1.0 / float(M))))
+    t_hi = s_hi - q * m_hi
+    t_lo = s_lo - q * m_lo
+    return t_hi * 2.0 ** SPLIT + t_lo, (s_hi, q, t_hi)
 
 
-def test_crt_limbs_exact():
+# Absolute error of the reconstruction in units of C_int: the rounded low
+# limb (weights rounded to 53 bits, 14 rounded accumulations, q * m_lo) stays
+# below 2^34; one unit of C_int is 2^-2P of max|a_row| * max|b_col|.
+CRT_ABS_ERR = 2.0 ** 34
+
+
+def test_crt_limbs_accuracy():
     rng = np.random.default_rng(0)
-    M, _ = consts()
-    for K in (1, 64, 4096, 8192, 65536):
+    M, W = consts()
+    assert max(w >> SPLIT for w in W) < 2 ** 41
+    assert 14 * 255 * max(w >> SPLIT for w in W) < 2 ** 53
+    for K in (1, 64, 4096, 8192, 32768):
         P = bits_for_k(K)
         bound = K * 2 ** (2 * P)
         assert 4 * bound <= M
@@ -91,10 +120,11 @@ def test_crt_limbs_exact():
             c = int(rng.integers(-2 ** 62, 2 ** 62)) * int(rng.integers(0, 2 ** 40)) % bound
             c = c if rng.random() < 0.5 else -c
             res = [c % m for m in MODULI]
-            got, (s, q, t) = crt_limbs(res)
-            for v in s + t:
+            got, (s_hi, q, t_hi) = crt_limbs(res)
+            for v in (s_hi, t_hi):
                 assert abs(v) < 2.0 ** 53 and v == int(v)
-            assert got == float(c) or abs(got - c) <= abs(c) * 2.0 ** -52
+            assert int(q) == (sum(r * w for r, w in zip(res, W)) - c) // M
+            assert abs(got - c) <= CRT_ABS_ERR + abs(c) * 2.0 ** -52
 
 
 def model_gemm(A, B):
@@ -107,14 +137,15 @@ def model_gemm(A, B):
     for i in range(M_rows):
         for j in range(N_cols):
             exact_int = sum(x * y for x, y in zip(ai[i], bi[j]))
-            # per-modulus GEMM on symmetric residues, as the tensor cores do
+            # per-modulus GEMM on unsigned residues (u8 x u8 -> s32), as the
+            # tensor cores do; the epilogue keeps the sum mod m
             res = []
             for m in MODULI:
-                acc = sum(sym_residue(x, m) * sym_residue(y, m) for x, y in zip(ai[i], bi[j]))
-                assert abs(acc) < 2 ** 31
+                acc = sum(byte_residue(x, m) * byte_residue(y, m) for x, y in zip(ai[i], bi[j]))
+                assert 0 <= acc < 2 ** 31
                 res.append(acc % m)
             got, _ = crt_limbs(res)
-            assert got == float(exact_int) or abs(got - exact_int) <= abs(exact_int) * 2.0 ** -52
+            assert abs(got - exact_int) <= CRT_ABS_ERR + abs(exact_int) * 2.0 ** -52
             out[i, j] = math.ldexp(got, -(sa[i] + sb[j]))
     return out
 
