@@ -286,10 +286,11 @@ __host__ __device__ constexpr int split_rows_threads(int64_t K) {
 
 __global__ void __launch_bounds__(kSplitRowsMaxThreads)
 split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
-                    int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts) {
+                    int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts,
+                    int64_t row0) {
   __shared__ double s_max[kSplitRowsMaxThreads / 32];
   __shared__ int s_bad[kSplitRowsMaxThreads / 32];
-  const int64_t r = blockIdx.x, b = blockIdx.y;
+  const int64_t r = row0 + blockIdx.x, b = blockIdx.y;
   const bool live = r < rows;
   const int64_t base = b * o.s_b + r * o.s_r;
   const bool vec = o.f64 && o.s_k == 1 && (reinterpret_cast<uintptr_t>(o.f64 + base) & 15) == 0;
@@ -518,6 +519,7 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
 
 struct GemmParams {
   int batch, tiles_m, tiles_n, kblocks;
+  int tm0;  // first tile row of this launch (a band of tiles_m tile rows)
   int64_t Mp, Np;
   int64_t units;
   uint8_t* cres;
@@ -646,16 +648,27 @@ __device__ __forceinline__ Unit unit_of(int64_t u, const GemmParams& p) {
   const int64_t per_b = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   x.b = static_cast<int>(rem / per_b);
   rem -= x.b * per_b;
-  x.tm = static_cast<int>(rem / p.tiles_n);
-  x.tn = static_cast<int>(rem - static_cast<int64_t>(x.tm) * p.tiles_n);
+  const int tm = static_cast<int>(rem / p.tiles_n);
+  x.tn = static_cast<int>(rem - static_cast<int64_t>(tm) * p.tiles_n);
+  x.tm = p.tm0 + tm;
   return x;
 }
 
-__device__ __forceinline__ uint32_t mod_u8(int v, int m, double inv_m) {
-  int r = v - m * static_cast<int>(floor(static_cast<double>(v) * inv_m));
-  if (r < 0) r += m;
-  if (r >= m) r -= m;
-  return static_cast<uint32_t>(r);
+// v mod m for 0 <= v < 2^31 (a u8 x u8 -> s32 accumulator, K <= 32768):
+// floor(v / m) = umulhi(v, ceil(2^39 / m)) >> 7 exactly, because
+// v * (ceil(2^39 / m) * m - 2^39) < 2^31 * 2^8 = 2^39.  Integer pipes only.
+__host__ __device__ constexpr uint32_t epilogue_magic(uint32_t m) {
+  return static_cast<uint32_t>(((1ull << 39) + m - 1) / m);
+}
+
+__device__ __forceinline__ uint32_t mod_u8(uint32_t v, uint32_t m, uint32_t magic) {
+  return v - (__umulhi(v, magic) >> 7) * m;
+}
+
+// Four accumulators -> their residues as the bytes of one word.
+__device__ __forceinline__ uint32_t mod_pack4(const uint32_t* v, uint32_t m, uint32_t magic) {
+  return __byte_perm(__byte_perm(mod_u8(v[0], m, magic), mod_u8(v[1], m, magic), 0x0040),
+                     __byte_perm(mod_u8(v[2], m, magic), mod_u8(v[3], m, magic), 0x0040), 0x5410);
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -788,8 +801,8 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, 4)) break;
       tc_fence_after();
       const Unit w = unit_of(u, p);
-      const int m = mod_of(w.l);
-      const double inv_m = 1.0 / static_cast<double>(m);
+      const uint32_t m = static_cast<uint32_t>(mod_of(w.l));
+      const uint32_t magic = epilogue_magic(m);
       const int64_t row = (static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
                           static_cast<int64_t>(w.tm) * kTileM + row_in_tile;
       uint8_t* out = p.cres + row * p.Np + static_cast<int64_t>(w.tn) * kTileN;
@@ -801,13 +814,7 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tmem_ld32(tbase + c0, v);
         uint32_t packed[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            word |= mod_u8(static_cast<int>(v[q * 4 + j]), m, inv_m) << (8 * j);
-          packed[q] = word;
-        }
+        for (int q = 0; q < 8; ++q) packed[q] = mod_pack4(v + q * 4, m, magic);
         uint4* dst = reinterpret_cast<uint4*>(out + c0);
         dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
@@ -1068,8 +1075,8 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, 14)) break;
       tc_fence_after();
       const Unit w = unit_of(u, p);
-      const int m = mod_of(w.l);
-      const double inv_m = 1.0 / static_cast<double>(m);
+      const uint32_t m = static_cast<uint32_t>(mod_of(w.l));
+      const uint32_t magic = epilogue_magic(m);
       const int64_t row = (static_cast<int64_t>(w.l) * p.batch + w.b) * p.Mp +
                           static_cast<int64_t>(w.tm) * 256 + rank * 128 + row_in_tile;
       uint8_t* out = p.cres + row * p.Np + static_cast<int64_t>(w.tn) * 256;
@@ -1081,13 +1088,7 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tmem_ld32(tbase + c0, v);
         uint32_t packed[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            word |= mod_u8(static_cast<int>(v[q * 4 + j]), m, inv_m) << (8 * j);
-          packed[q] = word;
-        }
+        for (int q = 0; q < 8; ++q) packed[q] = mod_pack4(v + q * 4, m, magic);
         uint4* dst = reinterpret_cast<uint4*>(out + c0);
         dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
@@ -1118,6 +1119,7 @@ struct CrtParams {
   double mlimb[2];
   double inv_m;
   int64_t batch, M, N, Mp, Np, K;
+  int64_t row_begin, row_end;  // rows of the flattened [batch * M] output this launch covers
   const uint8_t* cres;
   const int* sa;  // [batch][Mp]
   const int* sb;  // [batch][Np]
@@ -1155,8 +1157,7 @@ crt_kernel(CrtParams p) {
   const bool failed = *p.err != 0;
   const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCrtCols;
   if (j0 >= p.N) return;
-  const int64_t rows_total = p.batch * p.M;
-  for (int64_t row = blockIdx.y; row < rows_total; row += gridDim.y) {
+  for (int64_t row = p.row_begin + blockIdx.y; row < p.row_end; row += gridDim.y) {
     const int64_t b = row / p.M, i = row - b * p.M;
     const int sa = p.sa[b * p.Mp + i];
     const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
@@ -1298,13 +1299,20 @@ const GemmSetup& gemm_setup() {
   return by_device[dev];
 }
 
+// Split of one operand.  Rows contiguous in K take split_kmajor_kernel over
+// rows [row0, row1) of the padded row range; other layouts take the column
+// max and the tiled column split over all rows.
+bool split_by_rows(const DotOperand& o, int64_t rows) { return o.s_k == 1 || rows == 1; }
+
 int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
-                 int64_t Kp, int P, uint8_t* planes, int* shifts, int* codes, cudaStream_t s) {
-  if (o.s_k == 1 || rows == 1) {
+                 int64_t Kp, int P, uint8_t* planes, int* shifts, int* codes, cudaStream_t s,
+                 int64_t row0 = 0, int64_t row1 = -1) {
+  if (split_by_rows(o, rows)) {
+    if (row1 < 0) row1 = rows_pad;
     ProfileScope prof("ozaki_split_rows", s);
-    dim3 grid(static_cast<unsigned>(rows_pad), static_cast<unsigned>(batch));
+    dim3 grid(static_cast<unsigned>(row1 - row0), static_cast<unsigned>(batch));
     split_kmajor_kernel<<<grid, split_rows_threads(K), 0, s>>>(o, rows, K, rows_pad, Kp, batch,
-                                                               P, planes, shifts);
+                                                               P, planes, shifts, row0);
   } else {
     DSB_CUDA_TRY(cudaMemsetAsync(codes, 0, sizeof(int) * batch * rows_pad, s));
     dim3 g1(static_cast<unsigned>(rows_pad / kColTileR),
@@ -1371,53 +1379,20 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   int* err = reinterpret_cast<int*>(ws + g.off_err);
   const int P = bits_for_k(p.K);
 
-  DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
-  {
-    ProfileScope prof("ozaki_split", s);
-    if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
-      return st;
-    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, cb, s))
-      return st;
-  }
-
   CUtensorMap ta, tb;
   if (int st = make_tmap(&ta, planes_a, g.Kp, kL * p.batch * g.Mp, kTileM)) return st;
   // The pair kernel loads half of each 256-row B tile per CTA.
   if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np, pair ? kTileN / 2 : kTileN))
     return st;
+  const int tile_rows = pair ? 2 * kTileM : kTileM;
   GemmParams gp{};
   gp.batch = static_cast<int>(p.batch);
-  gp.tiles_m = static_cast<int>(g.Mp / (pair ? 2 * kTileM : kTileM));
   gp.tiles_n = static_cast<int>(g.Np / kTileN);
   gp.kblocks = static_cast<int>(g.Kp / kTileK);
   gp.Mp = g.Mp;
   gp.Np = g.Np;
-  gp.units = static_cast<int64_t>(kL) * p.batch * gp.tiles_m * gp.tiles_n;
   gp.cres = cres;
   gp.err = err;
-  {
-    ProfileScope prof("ozaki_gemm", s);
-    if (pair) {
-      const int64_t clusters = gp.units < setup.pair_clusters ? gp.units : setup.pair_clusters;
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
-      cfg.blockDim = dim3(kGemmThreads);
-      cfg.dynamicSmemBytes = gemm2_smem_bytes();
-      cfg.stream = s;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel, ta, tb, gp));
-    } else {
-      const int grid = static_cast<int>(gp.units < sm_count() ? gp.units : sm_count());
-      ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), s>>>(ta, tb, gp);
-    }
-    if (int st = launch_status()) return st;
-  }
 
   const CrtConsts& cc = crt_consts();
   CrtParams cp{};
@@ -1437,12 +1412,64 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   cp.a = p.a;
   cp.b = p.b;
   cp.c = p.c;
-  ProfileScope prof("ozaki_crt", s);
-  const int64_t rows_total = p.batch * p.M;
-  dim3 cg(static_cast<unsigned>((p.N + kCrtThreads * kCrtCols - 1) / (kCrtThreads * kCrtCols)),
-          static_cast<unsigned>(rows_total < 65535 ? rows_total : 65535));
-  crt_kernel<<<cg, kCrtThreads, 0, s>>>(cp);
-  return launch_status();
+
+  // GEMM over tile rows [tm0, tm0 + tiles) on stream `st`.
+  auto launch_gemm = [&](int tm0, int tiles, cudaStream_t st) -> int {
+    GemmParams q = gp;
+    q.tm0 = tm0;
+    q.tiles_m = tiles;
+    q.units = static_cast<int64_t>(kL) * p.batch * tiles * q.tiles_n;
+    ProfileScope prof("ozaki_gemm", st);
+    if (pair) {
+      const int64_t clusters = q.units < setup.pair_clusters ? q.units : setup.pair_clusters;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = gemm2_smem_bytes();
+      cfg.stream = st;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel, ta, tb, q));
+    } else {
+      const int grid = static_cast<int>(q.units < sm_count() ? q.units : sm_count());
+      ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), st>>>(ta, tb, q);
+    }
+    return launch_status();
+  };
+  // CRT of output rows [r0, r1) of the flattened [batch * M] result.
+  auto launch_crt = [&](int64_t r0, int64_t r1, cudaStream_t st) -> int {
+    if (r1 <= r0) return ok();
+    CrtParams q = cp;
+    q.row_begin = r0;
+    q.row_end = r1;
+    ProfileScope prof("ozaki_crt", st);
+    const int64_t n = r1 - r0;
+    dim3 cg(static_cast<unsigned>((p.N + kCrtThreads * kCrtCols - 1) / (kCrtThreads * kCrtCols)),
+            static_cast<unsigned>(n < 65535 ? n : 65535));
+    crt_kernel<<<cg, kCrtThreads, 0, st>>>(q);
+    return launch_status();
+  };
+
+  // One stream, one launch per step: nothing else runs beside the GEMM.  An
+  // overlapped schedule (bands of A's rows, the GEMM of band i on a second
+  // stream beside the split of band i + 1 and the CRT of band i - 1) left
+  // CTA pairs of the GEMM blocked in tcgen05.alloc on some SMs; it is not
+  // used.
+  DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+  {
+    ProfileScope prof("ozaki_split", s);
+    if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
+      return st;
+    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, cb, s))
+      return st;
+  }
+  if (int st = launch_gemm(0, static_cast<int>(g.Mp / tile_rows), s)) return st;
+  return launch_crt(0, p.batch * p.M, s);
 }
 
 }  // namespace dsb

@@ -163,3 +163,4 @@ def test_precision_highest_256(ops):
     f64 = AA @ B.astype(np.float64)
     f32 = (A * A) @ B
     assert np.mean(np.abs(got - f64)) <= np.mean(np.abs(f32 - f64))
+

@@ -159,3 +159,18 @@ def test_model_gemm_accuracy():
     truth = exact.exact_gemm_entries(A, B, rows.ravel(), cols.ravel()).reshape(4, 3)
     mag = np.abs(A) @ np.abs(B)
     assert np.max(np.abs(got - truth) / mag) < 2.0 ** -46
+
+
+def test_epilogue_modulo():
+    """The GEMM epilogue's v mod m = v - m * (umulhi(v, ceil(2^39/m)) >> 7),
+    exact for every s32 accumulator value 0 <= v < 2^31."""
+    rng = np.random.default_rng(9)
+    vals = [0, 1, 2 ** 31 - 1, 2 ** 30, 255 * 255 * 32768] + \
+        [int(v) for v in rng.integers(0, 2 ** 31, 50000)]
+    for m in MODULI:
+        magic = (2 ** 39 + m - 1) // m
+        assert magic < 2 ** 32
+        assert (2 ** 31) * (magic * m - 2 ** 39) < 2 ** 39
+        for v in vals + [k * m - 1 for k in range(1, 2 ** 31 // m, 2 ** 31 // m // 1000)]:
+            q = ((v * magic) >> 32) >> 7
+            assert v - q * m == v % m
