@@ -1148,17 +1148,38 @@ __device__ __forceinline__ double byte_to_f64(uint32_t word, int q) {
   return __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(byte)), 0x1p52);
 }
 
-// blockIdx.y strides over the batch*M output rows, blockIdx.x * 512 is the
-// first column of the block; each thread rebuilds 4 consecutive outputs from
-// one 4-byte load per residue plane.
+// 2^e as an f64 for a normal exponent.
+__device__ __forceinline__ double pow2_normal(int e) {
+  return __longlong_as_double(static_cast<long long>(1023 + e) << 52);
+}
+
+// blockIdx.x * 512 is the first column of the block; blockIdx.y strides over
+// the batch*M output rows, so each thread rebuilds 4 consecutive outputs of
+// several rows (one 4-byte load per residue plane and row) with its
+// columns' scale exponents loaded once per batch entry.
 __global__ void __launch_bounds__(kCrtThreads, 8)
 crt_kernel(CrtParams p) {
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
   const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCrtCols;
   if (j0 >= p.N) return;
-  for (int64_t row = p.row_begin + blockIdx.y; row < p.row_end; row += gridDim.y) {
-    const int64_t b = row / p.M, i = row - b * p.M;
+  int64_t cur_b = -1;
+  int sbv[kCrtCols];
+  // (b, i) of the flattened row, advanced without a 64-bit division per row
+  int64_t b = (p.row_begin + blockIdx.y) / p.M;
+  int64_t i = (p.row_begin + blockIdx.y) - b * p.M;
+  for (int64_t row = p.row_begin + blockIdx.y; row < p.row_end;
+       row += gridDim.y, i += gridDim.y) {
+    while (i >= p.M) {
+      i -= p.M;
+      ++b;
+    }
+    if (b != cur_b) {
+      cur_b = b;
+#pragma unroll
+      for (int q = 0; q < kCrtCols; ++q)
+        sbv[q] = j0 + q < p.N ? p.sb[b * p.Np + j0 + q] : 0;
+    }
     const int sa = p.sa[b * p.Mp + i];
     const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
     double s_hi[kCrtCols], s_lo[kCrtCols];
@@ -1179,7 +1200,7 @@ crt_kernel(CrtParams p) {
     for (int q = 0; q < kCrtCols; ++q) {
       const int64_t j = j0 + q;
       if (j >= p.N) break;
-      const int sb = p.sb[b * p.Np + j];
+      const int sb = sbv[q];
       double out;
       if (failed) {
         out = __longlong_as_double(0x7ff8000000000000LL);
@@ -1200,7 +1221,10 @@ crt_kernel(CrtParams p) {
         const double qt = rint(approx * p.inv_m);
         const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi[q]);
         const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo[q]);
-        out = scale2(scale2(__fma_rn(t_hi, 0x1p70, t_lo), -sa), -sb);
+        const double c = __fma_rn(t_hi, 0x1p70, t_lo);
+        // scale by 2^-(sa + sb): one exact multiply when 2^-(sa+sb) is normal
+        const int e = -(sa + sb);
+        out = (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sb);
       }
       put_result(p.c, row * p.N + j, out);
     }
@@ -1448,9 +1472,14 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
     q.row_begin = r0;
     q.row_end = r1;
     ProfileScope prof("ozaki_crt", st);
+    // about 16 blocks of 128 threads per SM in one wave, each thread taking
+    // several rows
     const int64_t n = r1 - r0;
-    dim3 cg(static_cast<unsigned>((p.N + kCrtThreads * kCrtCols - 1) / (kCrtThreads * kCrtCols)),
-            static_cast<unsigned>(n < 65535 ? n : 65535));
+    const int64_t gx = (p.N + kCrtThreads * kCrtCols - 1) / (kCrtThreads * kCrtCols);
+    int64_t gy = (static_cast<int64_t>(sm_count()) * 16 + gx - 1) / gx;
+    if (gy > n) gy = n;
+    if (gy > 65535) gy = 65535;
+    dim3 cg(static_cast<unsigned>(gx), static_cast<unsigned>(gy < 1 ? 1 : gy));
     crt_kernel<<<cg, kCrtThreads, 0, st>>>(q);
     return launch_status();
   };
