@@ -810,7 +810,8 @@ def run_large(args):
         ach = local_bytes / (per * 1e-3) / 1e9
         line["roofline"] = {"bound": "hbm", "kernel": fam, "achieved": round(ach, 1),
                             "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+                            "frac": round(ach / peaks["hbm_gbs"], 4),
+                            "traffic": ncu_traffic(fam, "batched_dot") if world == 1 else None,
                             "kernel_ms_per_step": round(per, 4),
                             "peak_source": f"{peak_src} hbm_gbs"}
         line["config"] = {"workload": "ds_dot_general_f64 batched dot, batch 4096 x length "
