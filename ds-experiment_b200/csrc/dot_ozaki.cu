@@ -181,13 +181,18 @@ __device__ __forceinline__ uint64_t quantise(double v, int shift) {
   return static_cast<uint64_t>(__double_as_longlong(y)) & ((1ull << 52) - 1);
 }
 
-// t = hi * 2^32 + lo (hi < 2^20): the seven bytes of t in two words.
+// t = hi * 2^32 + lo (hi < 2^20): the seven bytes of t in two words, and
+// the unbiased integer t - 2^51 as an f64 (exact: |t - 2^51| <= 2^50).
 struct Limbs {
   uint32_t lo, hi;
+  double xd;
 };
 
 __device__ __forceinline__ Limbs limbs_of(uint64_t t) {
-  return Limbs{static_cast<uint32_t>(t), static_cast<uint32_t>(t >> 32)};
+  // t is the mantissa of 1.5 * 2^52 + x_int, a double in [2^52, 2^53)
+  const double y = __longlong_as_double(static_cast<long long>(0x4330000000000000ull | t));
+  return Limbs{static_cast<uint32_t>(t), static_cast<uint32_t>(t >> 32),
+               __dsub_rn(y, 6755399441055744.0)};
 }
 
 // 2^e mod m, for the byte weights below.
@@ -210,18 +215,65 @@ __host__ __device__ constexpr uint32_t byte_weights(int j0, int count, uint32_t 
 // s = t - 2^51 (mod m); then s mod m = s - m * umulhi(s, ceil(2^32 / m)),
 // exact because s * (ceil(2^32 / m) * m - 2^32) < 2^19 * 2^8 < 2^32.
 // m = 256 is the low byte of t (2^51 = 0 mod 256).
-template <int l>
+// Per modulus: {byte weights of the low word, of the high word, the bias
+// correction, ceil(2^32 / m)}.  In the constant bank, so the instructions
+// read them as operands instead of materialising 52 immediates per element.
+struct SplitConsts {
+  uint32_t w_lo, w_hi, unbias, magic;
+};
+
+__host__ __device__ constexpr SplitConsts split_consts(uint32_t m) {
+  return SplitConsts{byte_weights(0, 4, m), byte_weights(4, 3, m), (m - pow2_mod(51, m)) % m,
+                     m == 256u ? 0u : 0xFFFFFFFFu / m + 1u};
+}
+
+__constant__ SplitConsts c_split[kL] = {
+    split_consts(mod_of(0)),  split_consts(mod_of(1)),  split_consts(mod_of(2)),
+    split_consts(mod_of(3)),  split_consts(mod_of(4)),  split_consts(mod_of(5)),
+    split_consts(mod_of(6)),  split_consts(mod_of(7)),  split_consts(mod_of(8)),
+    split_consts(mod_of(9)),  split_consts(mod_of(10)), split_consts(mod_of(11)),
+    split_consts(mod_of(12)), split_consts(mod_of(13))};
+
+// The same residue on the FP64 pipe, for half of the moduli, so that the
+// integer and FP64 pipes share the work.  q = rint(x / m) from one FMA with
+// 1.5 * 2^52 (x / m is known to 2^-10, so q is within one of the nearest
+// integer); r = x - q m is exact, |r| < m; adding 2^52 + m exactly leaves
+// m + r in (0, 2m) as the low word; one unsigned min folds it into [0, m).
+struct SplitF64 {
+  double inv, m, two52_plus_m;
+};
+
+__host__ __device__ constexpr SplitF64 split_f64(uint32_t m) {
+  return SplitF64{1.0 / static_cast<double>(m), static_cast<double>(m),
+                  4503599627370496.0 + static_cast<double>(m)};
+}
+
+__constant__ SplitF64 c_split_f64[kL] = {
+    split_f64(mod_of(0)),  split_f64(mod_of(1)),  split_f64(mod_of(2)),
+    split_f64(mod_of(3)),  split_f64(mod_of(4)),  split_f64(mod_of(5)),
+    split_f64(mod_of(6)),  split_f64(mod_of(7)),  split_f64(mod_of(8)),
+    split_f64(mod_of(9)),  split_f64(mod_of(10)), split_f64(mod_of(11)),
+    split_f64(mod_of(12)), split_f64(mod_of(13))};
+
+// With kMixed, moduli 1..7 take the FP64 path and 8..13 the integer one;
+// otherwise all take the integer path.  0 (256) is a mask.
+template <bool kMixed>
+constexpr bool residue_on_fp64(int l) { return kMixed && l >= 1 && l <= 7; }
+
+template <int l, bool kMixed>
 __device__ __forceinline__ uint32_t residue(const Limbs& x) {
   constexpr uint32_t m = mod_of(l);
   if constexpr (m == 256u) {
     return x.lo & 0xFFu;
+  } else if constexpr (residue_on_fp64<kMixed>(l)) {
+    const SplitF64& c = c_split_f64[l];
+    const double q = __dsub_rn(__fma_rn(x.xd, c.inv, 6755399441055744.0), 6755399441055744.0);
+    const double r = __fma_rn(-q, c.m, x.xd);
+    const uint32_t v = static_cast<uint32_t>(__double2loint(__dadd_rn(r, c.two52_plus_m)));
+    return min(v, v - m);
   } else {
-    constexpr uint32_t w_lo = byte_weights(0, 4, m);
-    constexpr uint32_t w_hi = byte_weights(4, 3, m);
-    constexpr uint32_t unbias = (m - pow2_mod(51, m)) % m;
-    constexpr uint32_t magic = 0xFFFFFFFFu / m + 1u;  // ceil(2^32 / m), m not a power of 2
-    const uint32_t s = __dp4a(x.lo, w_lo, __dp4a(x.hi, w_hi, unbias));
-    return s - __umulhi(s, magic) * m;
+    const uint32_t s = __dp4a(x.lo, c_split[l].w_lo, __dp4a(x.hi, c_split[l].w_hi, c_split[l].unbias));
+    return s - __umulhi(s, c_split[l].magic) * m;
   }
 }
 
@@ -232,15 +284,15 @@ __device__ __forceinline__ uint32_t pack4(uint32_t r0, uint32_t r1, uint32_t r2,
 
 // Residues of N = 4, 8 or 16 consecutive values -> one 4-, 8- or 16-byte
 // store per modulus plane.
-template <int N, int l = 0>
+template <int N, bool kMixed, int l = 0>
 __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* base,
                                                size_t plane_stride) {
   if constexpr (l < kL) {
     uint32_t w[N / 4];
 #pragma unroll
     for (int q = 0; q < N / 4; ++q)
-      w[q] = pack4(residue<l>(x[q * 4]), residue<l>(x[q * 4 + 1]), residue<l>(x[q * 4 + 2]),
-                   residue<l>(x[q * 4 + 3]));
+      w[q] = pack4(residue<l, kMixed>(x[q * 4]), residue<l, kMixed>(x[q * 4 + 1]),
+                   residue<l, kMixed>(x[q * 4 + 2]), residue<l, kMixed>(x[q * 4 + 3]));
     uint8_t* dst = base + l * plane_stride;
     if constexpr (N == 4) {
       *reinterpret_cast<uint32_t*>(dst) = w[0];
@@ -249,7 +301,7 @@ __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* bas
     } else {
       *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    store_planes_n<N, l + 1>(x, base, plane_stride);
+    store_planes_n<N, kMixed, l + 1>(x, base, plane_stride);
   }
 }
 
@@ -284,7 +336,7 @@ __host__ __device__ constexpr int split_rows_threads(int64_t K) {
   return K > 4096 && K <= 16 * kSplitRowsMaxThreads ? kSplitRowsMaxThreads : 256;
 }
 
-__global__ void __launch_bounds__(kSplitRowsMaxThreads)
+__global__ void __launch_bounds__(kSplitRowsMaxThreads, 2)
 split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
                     int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts,
                     int64_t row0) {
@@ -358,7 +410,7 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
         Limbs x[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(zero ? 0.0 : v[g * 4 + j], sh));
-        store_planes_n<4>(x, row_out + k0, plane_stride);
+        store_planes_n<4, true>(x, row_out + k0, plane_stride);
       }
     }
     return;
@@ -382,7 +434,7 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
     Limbs x[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(w[j], sh));
-    store_planes_n<4>(x, row_out + k0, plane_stride);
+    store_planes_n<4, true>(x, row_out + k0, plane_stride);
   }
 }
 
@@ -509,9 +561,9 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
 #pragma unroll
   for (int j = 0; j < 16; ++j) q[j] = limbs_of(tile[my_grp * 16 + j][my_row]);
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  store_planes_n<16>(q, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp + kc +
-                            my_grp * 16,
-                     plane_stride);
+  store_planes_n<16, false>(q, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp +
+                                   kc + my_grp * 16,
+                            plane_stride);
 }
 
 // ---------------------------------------------------------------------------
