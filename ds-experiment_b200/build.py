@@ -29,7 +29,7 @@ LIB = os.path.join(HERE, "ds_b200", "libds_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "--fmad=false", "-Xcompiler", "-fPIC",
-    "-Xcompiler", "-fvisibility=hidden", "-I", INCLUDE, "-I", CSRC,
+    "-Xcompiler", "-fvisibility=hidden", "-I", INCLUDE, "-I", CSRC, "-I", BUILD,
     "-Xptxas", "-warn-spills", "--expt-relaxed-constexpr",
 ]
 
@@ -61,8 +61,22 @@ def _compile(src, obj, extra):
     return r.stderr
 
 
+def _gen_arith_source():
+    """ds_arith.cuh as a C++ raw string literal (the DS primitives that
+    fuse.cu hands to NVRTC), without its include guard and CUDA header."""
+    src = open(os.path.join(CSRC, "ds_arith.cuh")).read()
+    body = "\n".join(l for l in src.splitlines()
+                     if not l.startswith("#pragma once") and not l.startswith("#include"))
+    text = 'R"DSARITH(' + body + '\n)DSARITH"\n'
+    out = os.path.join(BUILD, "ds_arith_src.inc")
+    if not os.path.exists(out) or open(out).read() != text:
+        with open(out, "w") as f:
+            f.write(text)
+
+
 def build(force: bool = False, jobs: int = 0, verbose: bool = False, extra=()) -> str:
     os.makedirs(BUILD, exist_ok=True)
+    _gen_arith_source()
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     deps = _deps()
     objs = []

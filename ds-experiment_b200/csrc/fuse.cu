@@ -1,0 +1,443 @@
+// Fused elementwise DS programs: the DS pass's lowering of an elementwise
+// DAG (DsTransformPass.cpp:244-321 -- constants and f64 arguments split by
+// emitFromFloat, broadcast_in_dim applied to hi and lo alike, add / subtract
+// / multiply as DS operations, the result recombined at the return) emitted
+// as ONE kernel instead of one custom call, or one StableHLO fusion, per op.
+//
+// The program is a list of SSA operations (inputs, constants, add, sub, mul,
+// negate).  The host generates CUDA C++ for it -- the DS primitives of
+// ds_arith.cuh, the same source the library's own kernels are built from,
+// so the arithmetic is the same operation for operation -- with the
+// broadcast index arithmetic of every input folded to constants, compiles it
+// once with NVRTC for sm_100a (no FMA contraction) and caches the function
+// per device.  NVRTC and the driver's module calls are looked up at run time
+// (dlopen / cudaGetDriverEntryPoint), so the library has no link-time
+// dependency on either.
+#include <cuda.h>
+#include <dlfcn.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "profile.h"
+
+namespace dsb {
+namespace {
+
+// The DS primitives, as source text (generated from ds_arith.cuh at build
+// time).
+const char kDsArithSource[] =
+#include "ds_arith_src.inc"
+    ;
+
+constexpr int kMaxFusedOps = 256;
+constexpr int kMaxFusedInputs = 16;
+constexpr int kMaxRank = 8;
+
+// ---- NVRTC, loaded on first use -------------------------------------------
+
+typedef int nvrtcResult_t;
+typedef struct _nvrtcProgram* nvrtcProgram_t;
+struct Nvrtc {
+  void* handle = nullptr;
+  nvrtcResult_t (*create)(nvrtcProgram_t*, const char*, const char*, int, const char* const*,
+                          const char* const*) = nullptr;
+  nvrtcResult_t (*compile)(nvrtcProgram_t, int, const char* const*) = nullptr;
+  nvrtcResult_t (*log_size)(nvrtcProgram_t, size_t*) = nullptr;
+  nvrtcResult_t (*log)(nvrtcProgram_t, char*) = nullptr;
+  nvrtcResult_t (*cubin_size)(nvrtcProgram_t, size_t*) = nullptr;
+  nvrtcResult_t (*cubin)(nvrtcProgram_t, char*) = nullptr;
+  nvrtcResult_t (*destroy)(nvrtcProgram_t*) = nullptr;
+  std::string error;
+};
+
+const Nvrtc& nvrtc() {
+  static Nvrtc n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* names[] = {"libnvrtc.so.12", "libnvrtc.so"};
+    for (const char* nm : names) {
+      n.handle = dlopen(nm, RTLD_NOW | RTLD_LOCAL);
+      if (n.handle) break;
+    }
+    if (!n.handle) {
+      n.error = "NVRTC (libnvrtc.so.12) could not be loaded";
+      return;
+    }
+    auto sym = [&](const char* s) { return dlsym(n.handle, s); };
+    n.create = reinterpret_cast<decltype(n.create)>(sym("nvrtcCreateProgram"));
+    n.compile = reinterpret_cast<decltype(n.compile)>(sym("nvrtcCompileProgram"));
+    n.log_size = reinterpret_cast<decltype(n.log_size)>(sym("nvrtcGetProgramLogSize"));
+    n.log = reinterpret_cast<decltype(n.log)>(sym("nvrtcGetProgramLog"));
+    n.cubin_size = reinterpret_cast<decltype(n.cubin_size)>(sym("nvrtcGetCUBINSize"));
+    n.cubin = reinterpret_cast<decltype(n.cubin)>(sym("nvrtcGetCUBIN"));
+    n.destroy = reinterpret_cast<decltype(n.destroy)>(sym("nvrtcDestroyProgram"));
+    if (!n.create || !n.compile || !n.log_size || !n.log || !n.cubin_size || !n.cubin ||
+        !n.destroy)
+      n.error = "NVRTC is missing an entry point";
+  });
+  return n;
+}
+
+// ---- driver module calls ----------------------------------------------------
+
+struct Driver {
+  CUresult (*load)(CUmodule*, const void*) = nullptr;
+  CUresult (*get)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                     unsigned, CUstream, void**, void**) = nullptr;
+  bool ok = false;
+};
+
+const Driver& driver() {
+  static Driver d;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    auto get = [](const char* name) -> void* {
+      void* f = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess)
+        return nullptr;
+      return f;
+    };
+    d.load = reinterpret_cast<decltype(d.load)>(get("cuModuleLoadData"));
+    d.get = reinterpret_cast<decltype(d.get)>(get("cuModuleGetFunction"));
+    d.launch = reinterpret_cast<decltype(d.launch)>(get("cuLaunchKernel"));
+    d.ok = d.load && d.get && d.launch;
+  });
+  return d;
+}
+
+// ---- program description and code generation -------------------------------
+
+struct InputView {
+  int type;                 // DS_FUSED_F64, DS_FUSED_F32, DS_FUSED_PACKED
+  int64_t stride[kMaxRank];  // element stride per output dimension (0: broadcast)
+  bool full;                 // the input is the output's own layout
+};
+
+struct Desc {
+  std::vector<ds_fused_op> ops;
+  std::vector<InputView> in;
+  int out_type = DS_FUSED_F64;
+  int rank = 0;
+  int64_t dims[kMaxRank] = {};
+  int64_t n = 1;
+};
+
+const char* ctype(int type) {
+  return type == DS_FUSED_F64 ? "double" : (type == DS_FUSED_F32 ? "float" : "float2");
+}
+
+std::string hex32(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  char b[16];
+  std::snprintf(b, sizeof b, "0x%08xu", u);
+  return b;
+}
+
+// Index of input k for output element i: sum over the output dimensions of
+// ((i / out_stride_d) % dim_d) * in_stride_d, all constants.
+std::string index_expr(const Desc& d, const InputView& v) {
+  if (v.full) return "i";
+  std::string e;
+  int64_t out_stride = 1;
+  std::vector<std::string> terms;
+  for (int k = d.rank - 1; k >= 0; --k) {
+    if (v.stride[k] != 0 && d.dims[k] > 1) {
+      std::string t = "(i / " + std::to_string(out_stride) + "LL)";
+      if (k > 0) t = "(" + t + " % " + std::to_string(d.dims[k]) + "LL)";
+      if (v.stride[k] != 1) t += " * " + std::to_string(v.stride[k]) + "LL";
+      terms.push_back(t);
+    }
+    out_stride *= d.dims[k];
+  }
+  if (terms.empty()) return "0";
+  for (size_t t = 0; t < terms.size(); ++t) e += (t ? " + " : "") + terms[t];
+  return e;
+}
+
+std::string generate(const Desc& d) {
+  std::string s;
+  s += kDsArithSource;
+  s += "\nusing namespace dsb;\n";
+  s += "extern \"C\" __global__ void __launch_bounds__(256) ds_fused_kernel(";
+  for (size_t k = 0; k < d.in.size(); ++k)
+    s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
+         ", ";
+  s += std::string(ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
+  s += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
+  s += "  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {\n";
+  for (size_t j = 0; j < d.ops.size(); ++j) {
+    const ds_fused_op& o = d.ops[j];
+    const std::string v = "v" + std::to_string(j);
+    switch (o.code) {
+      case DS_FUSED_INPUT: {
+        const InputView& in = d.in[o.a];
+        const std::string ld = "__ldg(in" + std::to_string(o.a) + " + (" + index_expr(d, in) + "))";
+        if (in.type == DS_FUSED_F64)
+          s += "    const ds2 " + v + " = from_f64(" + ld + ");\n";
+        else if (in.type == DS_FUSED_F32)
+          s += "    const ds2 " + v + " = ds2{" + ld + ", 0.0f};\n";
+        else
+          s += "    const float2 p" + std::to_string(j) + " = " + ld + ";\n    const ds2 " + v +
+               " = ds2{p" + std::to_string(j) + ".x, p" + std::to_string(j) + ".y};\n";
+        break;
+      }
+      case DS_FUSED_CONST: {
+        // emitFromFloat of the constant, on the host: hi = (float)c,
+        // lo = (float)(c - (double)hi), exact bit patterns in the source.
+        const float hi = static_cast<float>(o.value);
+        const float lo = static_cast<float>(o.value - static_cast<double>(hi));
+        s += "    const ds2 " + v + " = ds2{__uint_as_float(" + hex32(hi) + "), __uint_as_float(" +
+             hex32(lo) + ")};\n";
+        break;
+      }
+      case DS_FUSED_ADD:
+        s += "    const ds2 " + v + " = add(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
+             ");\n";
+        break;
+      case DS_FUSED_SUB:
+        s += "    const ds2 " + v + " = sub(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
+             ");\n";
+        break;
+      case DS_FUSED_MUL:
+        s += "    const ds2 " + v + " = mul(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
+             ");\n";
+        break;
+      default:  // DS_FUSED_NEG: exact
+        s += "    const ds2 " + v + " = ds2{-v" + std::to_string(o.a) + ".hi, -v" +
+             std::to_string(o.a) + ".lo};\n";
+        break;
+    }
+  }
+  const std::string r = "v" + std::to_string(d.ops.size() - 1);
+  if (d.out_type == DS_FUSED_F64)
+    s += "    out[i] = to_f64(" + r + ");\n";
+  else if (d.out_type == DS_FUSED_F32)
+    s += "    out[i] = __fadd_rn(" + r + ".hi, " + r + ".lo);\n";
+  else
+    s += "    out[i] = make_float2(" + r + ".hi, " + r + ".lo);\n";
+  s += "  }\n}\n";
+  return s;
+}
+
+int invalid(const std::string& m) { return set_error(DS_INVALID_ARGUMENT, m); }
+
+int64_t prod(const int64_t* d, int64_t r) {
+  int64_t n = 1;
+  for (int64_t i = 0; i < r; ++i) n *= d[i];
+  return n;
+}
+
+// Validate the program and the buffers and fill `d` (numpy broadcasting of
+// every input's logical shape to the output's).
+int describe(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+             const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+             const ds_buffer* out, Desc& d) {
+  if (ops == nullptr || n_ops < 1 || n_ops > kMaxFusedOps)
+    return invalid("ds_fused: 1 to 256 operations expected");
+  if (n_inputs < 0 || n_inputs > kMaxFusedInputs || (n_inputs > 0 && (!inputs || !input_types)))
+    return invalid("ds_fused: 0 to 16 inputs expected");
+  if (out_type < DS_FUSED_F64 || out_type > DS_FUSED_PACKED)
+    return invalid("ds_fused: unknown output type");
+  if (out == nullptr || out->rank < 0 || out->rank > kMaxRank + 1 || (out->rank && !out->dims))
+    return invalid("ds_fused: invalid output buffer");
+  // logical output shape
+  int64_t orank = out->rank;
+  if (out_type == DS_FUSED_PACKED) {
+    if (orank == 0 || out->dims[orank - 1] != 2)
+      return invalid("ds_fused: a packed output needs last dim == 2");
+    --orank;
+  }
+  if (orank > kMaxRank) return invalid("ds_fused: at most 8 dimensions");
+  d.rank = static_cast<int>(orank);
+  for (int k = 0; k < d.rank; ++k) {
+    if (out->dims[k] < 0) return invalid("ds_fused: negative dimension");
+    d.dims[k] = out->dims[k];
+  }
+  d.n = prod(d.dims, d.rank);
+  if (d.n > 0 && out->data == nullptr) return invalid("ds_fused: null output pointer");
+  d.out_type = out_type;
+  d.in.resize(n_inputs);
+  for (int32_t k = 0; k < n_inputs; ++k) {
+    const ds_buffer* b = inputs[k];
+    const int t = input_types[k];
+    if (t < DS_FUSED_F64 || t > DS_FUSED_PACKED) return invalid("ds_fused: unknown input type");
+    if (b == nullptr || b->rank < 0 || b->rank > kMaxRank + 1 || (b->rank && !b->dims))
+      return invalid("ds_fused: invalid input buffer");
+    int64_t r = b->rank;
+    if (t == DS_FUSED_PACKED) {
+      if (r == 0 || b->dims[r - 1] != 2) return invalid("ds_fused: a packed input needs last dim == 2");
+      --r;
+    }
+    if (r > d.rank) return invalid("ds_fused: an input has more dimensions than the output");
+    InputView& v = d.in[k];
+    v.type = t;
+    int64_t st = 1;
+    bool full = r == d.rank;
+    for (int q = d.rank - 1; q >= 0; --q) {
+      const int64_t src = q - (d.rank - r);  // right-aligned
+      const int64_t dim = src >= 0 ? b->dims[src] : 1;
+      if (dim != d.dims[q] && dim != 1)
+        return invalid("ds_fused: input " + std::to_string(k) + " does not broadcast to the output");
+      v.stride[q] = (dim == 1 && d.dims[q] != 1) ? 0 : st;
+      if (dim != d.dims[q]) full = false;
+      st *= dim;
+    }
+    v.full = full;
+    if (prod(b->dims, r) > 0 && b->data == nullptr) return invalid("ds_fused: null input pointer");
+  }
+  d.ops.assign(ops, ops + n_ops);
+  for (int32_t j = 0; j < n_ops; ++j) {
+    const ds_fused_op& o = ops[j];
+    switch (o.code) {
+      case DS_FUSED_INPUT:
+        if (o.a < 0 || o.a >= n_inputs) return invalid("ds_fused: input index out of range");
+        break;
+      case DS_FUSED_CONST:
+        break;
+      case DS_FUSED_ADD:
+      case DS_FUSED_SUB:
+      case DS_FUSED_MUL:
+        if (o.a < 0 || o.a >= j || o.b < 0 || o.b >= j)
+          return invalid("ds_fused: operands must be earlier operations");
+        break;
+      case DS_FUSED_NEG:
+        if (o.a < 0 || o.a >= j) return invalid("ds_fused: operands must be earlier operations");
+        break;
+      default:
+        return invalid("ds_fused: unknown operation code");
+    }
+  }
+  return DS_OK;
+}
+
+// Compiled functions per (device, source).
+std::mutex g_mu;
+std::map<std::pair<int, std::string>, CUfunction> g_funcs;
+
+int compile(const std::string& src, CUfunction* fn) {
+  int dev = 0;
+  DSB_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_funcs.find({dev, src});
+  if (it != g_funcs.end()) {
+    *fn = it->second;
+    return DS_OK;
+  }
+  const Nvrtc& nv = nvrtc();
+  if (!nv.error.empty()) return set_error(DS_INTERNAL, "ds_fused: " + nv.error);
+  const Driver& drv = driver();
+  if (!drv.ok) return set_error(DS_INTERNAL, "ds_fused: driver module calls unavailable");
+  nvrtcProgram_t prog = nullptr;
+  if (nv.create(&prog, src.c_str(), "ds_fused.cu", 0, nullptr, nullptr) != 0)
+    return set_error(DS_INTERNAL, "ds_fused: nvrtcCreateProgram failed");
+  const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-std=c++17", "-default-device"};
+  const int rc = nv.compile(prog, 4, opts);
+  if (rc != 0) {
+    size_t n = 0;
+    nv.log_size(prog, &n);
+    std::string log(n, '\0');
+    if (n) nv.log(prog, &log[0]);
+    nv.destroy(&prog);
+    return set_error(DS_INTERNAL, "ds_fused: NVRTC compilation failed: " + log);
+  }
+  size_t n = 0;
+  nv.cubin_size(prog, &n);
+  std::vector<char> cubin(n);
+  nv.cubin(prog, cubin.data());
+  nv.destroy(&prog);
+  CUmodule mod = nullptr;
+  if (drv.load(&mod, cubin.data()) != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused: cuModuleLoadData failed");
+  CUfunction f = nullptr;
+  if (drv.get(&f, mod, "ds_fused_kernel") != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused: cuModuleGetFunction failed");
+  g_funcs[{dev, src}] = f;
+  *fn = f;
+  return DS_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+extern "C" {
+
+int ds_fused_source(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                    const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+                    const ds_buffer* out, char* buf, size_t cap, size_t* len) {
+  Desc d;
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, out_type, out, d)) return st;
+  const std::string src = generate(d);
+  if (len) *len = src.size() + 1;
+  if (buf && cap) {
+    const size_t k = src.size() < cap - 1 ? src.size() : cap - 1;
+    std::memcpy(buf, src.data(), k);
+    buf[k] = '\0';
+  }
+  return ok();
+}
+
+int ds_fused_compile_check(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                           const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+                           const ds_buffer* out) {
+  Desc d;
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, out_type, out, d)) return st;
+  const Nvrtc& nv = nvrtc();
+  if (!nv.error.empty()) return set_error(DS_INTERNAL, "ds_fused: " + nv.error);
+  const std::string src = generate(d);
+  nvrtcProgram_t prog = nullptr;
+  if (nv.create(&prog, src.c_str(), "ds_fused.cu", 0, nullptr, nullptr) != 0)
+    return set_error(DS_INTERNAL, "ds_fused: nvrtcCreateProgram failed");
+  const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-std=c++17", "-default-device"};
+  const int rc = nv.compile(prog, 4, opts);
+  std::string log;
+  if (rc != 0) {
+    size_t n = 0;
+    nv.log_size(prog, &n);
+    log.assign(n, '\0');
+    if (n) nv.log(prog, &log[0]);
+  }
+  nv.destroy(&prog);
+  if (rc != 0) return set_error(DS_INTERNAL, "ds_fused: NVRTC compilation failed: " + log);
+  return ok();
+}
+
+int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                 const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+                 const ds_buffer* out, void* stream) {
+  Desc d;
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, out_type, out, d)) return st;
+  if (d.n == 0) return ok();
+  CUfunction fn = nullptr;
+  if (int st = compile(generate(d), &fn)) return st;
+  std::vector<void*> ptrs(n_inputs + 1);
+  std::vector<void*> args(n_inputs + 2);
+  for (int32_t k = 0; k < n_inputs; ++k) {
+    ptrs[k] = inputs[k]->data;
+    args[k] = &ptrs[k];
+  }
+  ptrs[n_inputs] = out->data;
+  args[n_inputs] = &ptrs[n_inputs];
+  long long n = d.n;
+  args[n_inputs + 1] = &n;
+  const unsigned grid = grid_for(d.n, 256, 8);
+  ProfileScope prof("fused", static_cast<cudaStream_t>(stream));
+  if (driver().launch(fn, grid, 1, 1, 256, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
+                      nullptr) != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused: cuLaunchKernel failed");
+  return ok();
+}
+
+}  // extern "C"

@@ -48,6 +48,14 @@ class DsDotDims(ctypes.Structure):
                 ("rhs_contracting", ctypes.c_int64)]
 
 
+class DsFusedOp(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_int32), ("a", ctypes.c_int32), ("b", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("value", ctypes.c_double)]
+
+
+DS_FUSED_INPUT, DS_FUSED_CONST, DS_FUSED_ADD, DS_FUSED_SUB, DS_FUSED_MUL, DS_FUSED_NEG = range(6)
+DS_FUSED_F64, DS_FUSED_F32, DS_FUSED_PACKED = 0, 1, 2
+
 _BUF = ctypes.POINTER(DsBuffer)
 _VP = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -55,6 +63,7 @@ _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
 _I64P = ctypes.POINTER(ctypes.c_int64)
 _DIMS = ctypes.POINTER(DsDotDims)
+_OPS = ctypes.POINTER(DsFusedOp)
 
 # name -> (argtypes, restype)
 SIGNATURES = {
@@ -98,6 +107,12 @@ SIGNATURES = {
     "ds_dot_general": ([_BUF, _BUF, _BUF, _BUF, _DIMS, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                        ctypes.c_int),
     "ds_dot_general_f64": ([_BUF, _BUF, _DIMS, _I32, _BUF, _VP, _SZ, _VP], ctypes.c_int),
+    "ds_fused_run": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF), _I32, _I32, _BUF,
+                      _VP], ctypes.c_int),
+    "ds_fused_source": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF), _I32, _I32, _BUF,
+                         ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ)], ctypes.c_int),
+    "ds_fused_compile_check": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF), _I32, _I32,
+                                _BUF], ctypes.c_int),
     "ds_dot_tensor_plan": ([_I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_dot_tensor_kernel_info": ([ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_profile_enable": ([ctypes.c_int], None),

@@ -1,0 +1,279 @@
+"""Fused elementwise DS programs: one kernel per elementwise DAG.
+
+The reference's DS pass turns every f64 add, subtract and multiply of a
+function into a chain of f32 StableHLO operations (DsTransformPass.cpp:
+282-321), with constants and arguments split by emitFromFloat (:169-187,
+:244-257) and broadcast_in_dim applied to hi and lo alike (:259-279); XLA
+then fuses what it can, and the reference documents the cliff where it does
+not (README.md:53-68).  Here the same lowering is one generated kernel:
+
+    from ds_b200 import fuse
+
+    @fuse.jit
+    def f(x, y, z):
+        return (x + y) * z - 0.1 * x
+
+    out = f(x, y, z)      # torch CUDA tensors; f64 result computed in DS
+
+`fn` is traced once per argument signature (which arguments are tensors,
+their element types and shapes; scalar arguments are baked in as constants)
+into a list of operations, which the library turns into CUDA source, compiles
+with NVRTC for sm_100a and caches (ds_fused_run in ds_b200.h).  Inputs
+broadcast with numpy's rules.  f64 tensors are split on load, f32 tensors
+enter as (v, 0), `Packed(t)` marks a packed DS tensor [..., 2].  The result
+is f64 if any input is f64, else f32, unless `out_dtype` says otherwise
+("f64", "f32" or "packed").
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+
+
+class Packed:
+    """A packed DS tensor [..., 2] (hi, lo) used as a fused-program input."""
+
+    def __init__(self, t: torch.Tensor):
+        if t.dtype != torch.float32 or t.dim() == 0 or t.shape[-1] != 2:
+            raise ValueError("Packed expects a float32 tensor with last dim == 2")
+        self.t = t
+
+
+class _Program:
+    def __init__(self):
+        self.ops: List[Tuple[int, int, int, float]] = []
+
+    def add(self, code, a=0, b=0, value=0.0) -> "Node":
+        self.ops.append((code, int(a), int(b), float(value)))
+        return Node(self, len(self.ops) - 1)
+
+    def const(self, v: float) -> "Node":
+        return self.add(_lib.DS_FUSED_CONST, value=v)
+
+
+class Node:
+    """A traced DS value: arithmetic on Nodes (and Python numbers) records
+    operations of the program."""
+
+    def __init__(self, prog: _Program, idx: int):
+        self.prog, self.idx = prog, idx
+
+    def _lift(self, other) -> "Node":
+        if isinstance(other, Node):
+            if other.prog is not self.prog:
+                raise ValueError("values of different traces mixed")
+            return other
+        if isinstance(other, (int, float)):
+            return self.prog.const(float(other))
+        return NotImplemented
+
+    def _bin(self, code, other, swap=False):
+        o = self._lift(other)
+        if o is NotImplemented:
+            return NotImplemented
+        a, b = (o, self) if swap else (self, o)
+        return self.prog.add(code, a.idx, b.idx)
+
+    def __add__(self, o):
+        return self._bin(_lib.DS_FUSED_ADD, o)
+
+    def __radd__(self, o):
+        return self._bin(_lib.DS_FUSED_ADD, o, swap=True)
+
+    def __sub__(self, o):
+        return self._bin(_lib.DS_FUSED_SUB, o)
+
+    def __rsub__(self, o):
+        return self._bin(_lib.DS_FUSED_SUB, o, swap=True)
+
+    def __mul__(self, o):
+        return self._bin(_lib.DS_FUSED_MUL, o)
+
+    def __rmul__(self, o):
+        return self._bin(_lib.DS_FUSED_MUL, o, swap=True)
+
+    def __neg__(self):
+        return self.prog.add(_lib.DS_FUSED_NEG, self.idx)
+
+    def __pos__(self):
+        return self
+
+
+_TYPES = {torch.float64: _lib.DS_FUSED_F64, torch.float32: _lib.DS_FUSED_F32}
+_OUT = {"f64": _lib.DS_FUSED_F64, "f32": _lib.DS_FUSED_F32, "packed": _lib.DS_FUSED_PACKED}
+
+
+def _broadcast(shapes):
+    try:
+        return tuple(torch.broadcast_shapes(*shapes))
+    except RuntimeError as e:
+        raise ValueError(f"fused inputs do not broadcast: {e}") from None
+
+
+def _kind(a):
+    if isinstance(a, Packed):
+        return ("packed", tuple(a.t.shape))
+    if isinstance(a, torch.Tensor):
+        if a.dtype not in _TYPES:
+            raise TypeError(f"fused inputs are float64 or float32 tensors, got {a.dtype}")
+        return (str(a.dtype), tuple(a.shape))
+    if isinstance(a, (int, float)):
+        return ("scalar", float(a))
+    raise TypeError(f"unsupported fused argument {type(a).__name__}")
+
+
+class _Compiled:
+    def __init__(self, ops, n_inputs):
+        self.n_ops = len(ops)
+        self.ops = (_lib.DsFusedOp * self.n_ops)(
+            *[_lib.DsFusedOp(c, a, b, 0, v) for c, a, b, v in ops])
+        self.n_inputs = n_inputs
+
+
+def trace(fn: Callable, args: Sequence) -> Tuple[list, List[int]]:
+    """Record fn's operations for these arguments: (ops, positions of the
+    tensor arguments in input order)."""
+    prog = _Program()
+    traced, tensors = [], []
+    for pos, a in enumerate(args):
+        if isinstance(a, (int, float)) and not isinstance(a, bool):
+            traced.append(float(a))
+        else:
+            traced.append(prog.add(_lib.DS_FUSED_INPUT, len(tensors)))
+            tensors.append(pos)
+    result = fn(*traced)
+    if not isinstance(result, Node):
+        if isinstance(result, (int, float)):
+            result = prog.const(float(result))
+        else:
+            raise TypeError("a fused function must return an expression of its arguments")
+    if result.idx != len(prog.ops) - 1:
+        # make the result the last operation (a copy: 0 + r would round)
+        prog.add(_lib.DS_FUSED_NEG, prog.add(_lib.DS_FUSED_NEG, result.idx).idx)
+    return prog.ops, tensors
+
+
+def _buffers(tensors):
+    bufs, keep = [], []
+    for t in tensors:
+        b, d = _lib.make_buffer(t.data_ptr(), tuple(t.shape))
+        bufs.append(b)
+        keep.append((b, d))
+    return bufs, keep
+
+
+class jit:
+    """Decorator: run `fn` as one fused DS kernel (see the module docstring)."""
+
+    def __init__(self, fn: Callable, out_dtype: Optional[str] = None):
+        self.fn = fn
+        self.out_dtype = out_dtype
+        self._cache: Dict[tuple, Tuple[_Compiled, List[int]]] = {}
+        self.__doc__ = fn.__doc__
+
+    def _prepare(self, args):
+        key = tuple(_kind(a) for a in args)
+        hit = self._cache.get(key)
+        if hit is None:
+            ops, positions = trace(self.fn, args)
+            hit = (_Compiled(ops, len(positions)), positions)
+            self._cache[key] = hit
+        return hit
+
+    def _io(self, args, positions, out=None):
+        tensors, types, logical = [], [], []
+        device = None
+        for pos in positions:
+            a = args[pos]
+            if isinstance(a, Packed):
+                t, ty, shape = a.t, _lib.DS_FUSED_PACKED, tuple(a.t.shape[:-1])
+            else:
+                t, ty, shape = a, _TYPES[a.dtype], tuple(a.shape)
+            if not t.is_cuda:
+                raise ValueError("fused inputs must be CUDA tensors (there is no CPU path)")
+            if not t.is_contiguous():
+                raise ValueError("fused inputs must be contiguous")
+            device = device or t.device
+            if t.device != device:
+                raise ValueError("fused inputs must be on one device")
+            tensors.append(t)
+            types.append(ty)
+            logical.append(shape)
+        if device is None:
+            raise ValueError("a fused call needs at least one tensor argument")
+        shape = _broadcast(logical)
+        out_type = _OUT[self.out_dtype] if self.out_dtype else (
+            _lib.DS_FUSED_F64 if _lib.DS_FUSED_F64 in types else _lib.DS_FUSED_F32)
+        if out is None:
+            if out_type == _lib.DS_FUSED_PACKED:
+                out = torch.empty(shape + (2,), dtype=torch.float32, device=device)
+            else:
+                out = torch.empty(shape, dtype=torch.float64 if out_type == _lib.DS_FUSED_F64
+                                  else torch.float32, device=device)
+        return tensors, types, out_type, out
+
+    def __call__(self, *args, out: Optional[torch.Tensor] = None):
+        comp, positions = self._prepare(args)
+        tensors, types, out_type, out = self._io(args, positions, out)
+        bufs, keep = _buffers(tensors)
+        ob, od = _lib.make_buffer(out.data_ptr(), tuple(out.shape))
+        arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
+            *[ctypes.pointer(b) for b in bufs])
+        ty = (ctypes.c_int32 * max(len(types), 1))(*types)
+        dev = out.device
+        if dev.index is not None and dev.index != torch.cuda.current_device():
+            with torch.cuda.device(dev):
+                st = self._run(comp, ty, arr, len(bufs), out_type, ob)
+        else:
+            st = self._run(comp, ty, arr, len(bufs), out_type, ob)
+        _lib.check(st, "ds_fused_run")
+        return out
+
+    @staticmethod
+    def _run(comp, ty, arr, n, out_type, ob):
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        return _lib.lib().ds_fused_run(comp.ops, comp.n_ops, ty, arr, n, out_type,
+                                       ctypes.byref(ob), stream)
+
+    def source(self, *args) -> str:
+        """The CUDA source generated for these arguments (needs no GPU:
+        the tensors may live on any device)."""
+        comp, positions = self._prepare(args)
+        types, bufs, keep = [], [], []
+        logical = []
+        for pos in positions:
+            a = args[pos]
+            t = a.t if isinstance(a, Packed) else a
+            types.append(_lib.DS_FUSED_PACKED if isinstance(a, Packed) else _TYPES[a.dtype])
+            logical.append(tuple(t.shape[:-1]) if isinstance(a, Packed) else tuple(t.shape))
+            b, d = _lib.make_buffer(1, tuple(t.shape))  # pointer unused
+            bufs.append(b)
+            keep.append(d)
+        shape = _broadcast(logical)
+        out_type = _OUT[self.out_dtype] if self.out_dtype else (
+            _lib.DS_FUSED_F64 if _lib.DS_FUSED_F64 in types else _lib.DS_FUSED_F32)
+        oshape = shape + ((2,) if out_type == _lib.DS_FUSED_PACKED else ())
+        ob, od = _lib.make_buffer(1, oshape)
+        arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
+            *[ctypes.pointer(b) for b in bufs])
+        ty = (ctypes.c_int32 * max(len(types), 1))(*types)
+        n = ctypes.c_size_t()
+        L = _lib.lib()
+        _lib.check(L.ds_fused_source(comp.ops, comp.n_ops, ty, arr, len(bufs), out_type,
+                                     ctypes.byref(ob), None, 0, ctypes.byref(n)), "source")
+        buf = ctypes.create_string_buffer(n.value)
+        _lib.check(L.ds_fused_source(comp.ops, comp.n_ops, ty, arr, len(bufs), out_type,
+                                     ctypes.byref(ob), buf, n.value, ctypes.byref(n)), "source")
+        self._last_check = lambda: _lib.check(L.ds_fused_compile_check(
+            comp.ops, comp.n_ops, ty, arr, len(bufs), out_type, ctypes.byref(ob)), "compile")
+        return buf.value.decode()
+
+    def compile_check(self, *args) -> None:
+        """Generate and compile (NVRTC) for these arguments without running:
+        raises on a compilation error.  Needs no GPU."""
+        self.source(*args)
+        self._last_check()

@@ -292,6 +292,47 @@ DS_API int ds_dot_general_f64(const ds_buffer* lhs, const ds_buffer* rhs,
                        const ds_buffer* out, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* ---- fused elementwise programs ----------------------------------------- */
+
+/* The DS pass's lowering of an elementwise DAG (DsTransformPass.cpp:244-321:
+   constants and f64 arguments split by emitFromFloat, broadcast_in_dim on hi
+   and lo alike, add / subtract / multiply as DS operations, the result
+   recombined at the return) run as ONE kernel per DAG.  `ops` lists the DAG
+   in SSA order; operation j refers to earlier operations by index and the
+   last one is the result:
+     DS_FUSED_INPUT  a = input index (f64 inputs are split, f32 inputs become
+                     (v, 0), packed inputs [..., 2] are DS pairs)
+     DS_FUSED_CONST  value (split like an f64 argument)
+     DS_FUSED_ADD / SUB / MUL  a, b
+     DS_FUSED_NEG    a (exact: (-hi, -lo))
+   Inputs broadcast to the output's logical shape with numpy's rules (packed
+   tensors without their trailing 2).  The output is f64 (hi + lo in f64),
+   f32 (hi + lo in f32, as ds_to_f32) or packed DS [..., 2].  The kernel is
+   generated and compiled (NVRTC, sm_100a, no FMA contraction) on the first
+   call for each program, types and shapes, then cached per device. */
+enum { DS_FUSED_INPUT = 0, DS_FUSED_CONST = 1, DS_FUSED_ADD = 2, DS_FUSED_SUB = 3,
+       DS_FUSED_MUL = 4, DS_FUSED_NEG = 5 };
+enum { DS_FUSED_F64 = 0, DS_FUSED_F32 = 1, DS_FUSED_PACKED = 2 };
+typedef struct ds_fused_op {
+  int32_t code;
+  int32_t a;
+  int32_t b;
+  int32_t reserved;
+  double value;
+} ds_fused_op;
+
+DS_API int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                        const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+                        const ds_buffer* out, void* stream);
+/* The generated CUDA source (for inspection); *len = its size + 1. */
+DS_API int ds_fused_source(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                           const ds_buffer* const* inputs, int32_t n_inputs, int32_t out_type,
+                           const ds_buffer* out, char* buf, size_t cap, size_t* len);
+/* Generate and compile without loading (no GPU needed). */
+DS_API int ds_fused_compile_check(const ds_fused_op* ops, int32_t n_ops,
+                                  const int32_t* input_types, const ds_buffer* const* inputs,
+                                  int32_t n_inputs, int32_t out_type, const ds_buffer* out);
+
 /* ---- diagnostics (no reference counterpart) ------------------------------ */
 
 /* Per-kernel GPU time.  While enabled, each op brackets its main kernel with
