@@ -512,6 +512,16 @@ def run_stream(args):
         if wl == "reduce" and world > 1:
             exchange.check()
             exchange.close()
+        if wl == "fused_add_mul":
+            # the same chain as a generated kernel (ds_b200.fuse): one kernel
+            # per elementwise DAG, as the retargeted pass would emit it
+            from ds_b200 import fuse
+            chain = fuse.jit(lambda a_, b_, c_: (a_ + b_) * c_)
+            fms, fout = timed(lambda: chain(a, b, c), args.steps)
+            line["fused_program"] = {
+                "GB/s": round(world * bpe * n / (fms * 1e-3) / 1e9, 1), "ms_per_step": round(fms, 4),
+                "bit_exact_vs_hand_written": bool(torch.equal(fout.view(torch.int64),
+                                                              out.view(torch.int64)))}
         k_ms, k_n = _lib.profile_read(fam)
         # device time of the family per step: at N > 1 the reduce family
         # also holds the tiny combine of the gathered pairs

@@ -130,6 +130,7 @@ struct Desc {
   int rank = 0;
   int64_t dims[kMaxRank] = {};
   int64_t n = 1;
+  bool pairs = false;  // all inputs full and 16-byte aligned, output too
 };
 
 const char* ctype(int type) {
@@ -165,33 +166,19 @@ std::string index_expr(const Desc& d, const InputView& v) {
   return e;
 }
 
-std::string generate(const Desc& d) {
+// The operations of the program for one element; `load(k)` gives the DS
+// value of input k, every name gets `sfx`.
+template <typename Load>
+std::string program_body(const Desc& d, const std::string& sfx, Load load) {
   std::string s;
-  s += kDsArithSource;
-  s += "\nusing namespace dsb;\n";
-  s += "extern \"C\" __global__ void __launch_bounds__(256) ds_fused_kernel(";
-  for (size_t k = 0; k < d.in.size(); ++k)
-    s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
-         ", ";
-  s += std::string(ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
-  s += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
-  s += "  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {\n";
   for (size_t j = 0; j < d.ops.size(); ++j) {
     const ds_fused_op& o = d.ops[j];
-    const std::string v = "v" + std::to_string(j);
+    const std::string v = "v" + std::to_string(j) + sfx;
+    auto ref = [&](int k) { return "v" + std::to_string(k) + sfx; };
     switch (o.code) {
-      case DS_FUSED_INPUT: {
-        const InputView& in = d.in[o.a];
-        const std::string ld = "__ldg(in" + std::to_string(o.a) + " + (" + index_expr(d, in) + "))";
-        if (in.type == DS_FUSED_F64)
-          s += "    const ds2 " + v + " = from_f64(" + ld + ");\n";
-        else if (in.type == DS_FUSED_F32)
-          s += "    const ds2 " + v + " = ds2{" + ld + ", 0.0f};\n";
-        else
-          s += "    const float2 p" + std::to_string(j) + " = " + ld + ";\n    const ds2 " + v +
-               " = ds2{p" + std::to_string(j) + ".x, p" + std::to_string(j) + ".y};\n";
+      case DS_FUSED_INPUT:
+        s += "    const ds2 " + v + " = " + load(o.a) + ";\n";
         break;
-      }
       case DS_FUSED_CONST: {
         // emitFromFloat of the constant, on the host: hi = (float)c,
         // lo = (float)(c - (double)hi), exact bit patterns in the source.
@@ -202,31 +189,96 @@ std::string generate(const Desc& d) {
         break;
       }
       case DS_FUSED_ADD:
-        s += "    const ds2 " + v + " = add(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
-             ");\n";
+        s += "    const ds2 " + v + " = add(" + ref(o.a) + ", " + ref(o.b) + ");\n";
         break;
       case DS_FUSED_SUB:
-        s += "    const ds2 " + v + " = sub(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
-             ");\n";
+        s += "    const ds2 " + v + " = sub(" + ref(o.a) + ", " + ref(o.b) + ");\n";
         break;
       case DS_FUSED_MUL:
-        s += "    const ds2 " + v + " = mul(v" + std::to_string(o.a) + ", v" + std::to_string(o.b) +
-             ");\n";
+        s += "    const ds2 " + v + " = mul(" + ref(o.a) + ", " + ref(o.b) + ");\n";
         break;
       default:  // DS_FUSED_NEG: exact
-        s += "    const ds2 " + v + " = ds2{-v" + std::to_string(o.a) + ".hi, -v" +
-             std::to_string(o.a) + ".lo};\n";
+        s += "    const ds2 " + v + " = ds2{-" + ref(o.a) + ".hi, -" + ref(o.a) + ".lo};\n";
         break;
     }
   }
-  const std::string r = "v" + std::to_string(d.ops.size() - 1);
-  if (d.out_type == DS_FUSED_F64)
-    s += "    out[i] = to_f64(" + r + ");\n";
-  else if (d.out_type == DS_FUSED_F32)
-    s += "    out[i] = __fadd_rn(" + r + ".hi, " + r + ".lo);\n";
-  else
-    s += "    out[i] = make_float2(" + r + ".hi, " + r + ".lo);\n";
-  s += "  }\n}\n";
+  return s;
+}
+
+std::string from_value(int type, const std::string& x) {
+  if (type == DS_FUSED_F64) return "from_f64(" + x + ")";
+  if (type == DS_FUSED_F32) return "ds2{" + x + ", 0.0f}";
+  return "ds2{(" + x + ").x, (" + x + ").y}";
+}
+
+std::string to_value(int type, const std::string& r) {
+  if (type == DS_FUSED_F64) return "to_f64(" + r + ")";
+  if (type == DS_FUSED_F32) return "__fadd_rn(" + r + ".hi, " + r + ".lo)";
+  return "make_float2(" + r + ".hi, " + r + ".lo)";
+}
+
+// Vector types of two consecutive elements.
+const char* pair_type(int type) {
+  return type == DS_FUSED_F64 ? "double2" : (type == DS_FUSED_F32 ? "float2" : "float4");
+}
+
+std::string generate(const Desc& d) {
+  std::string s;
+  s += kDsArithSource;
+  s += "\nusing namespace dsb;\n";
+  s += "extern \"C\" __global__ void __launch_bounds__(256) ds_fused_kernel(";
+  for (size_t k = 0; k < d.in.size(); ++k)
+    s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
+         ", ";
+  s += std::string(ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
+  s += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
+  s += "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
+  const std::string last = std::to_string(d.ops.size() - 1);
+  // element i, one at a time
+  auto scalar_loop = [&](const std::string& first) {
+    std::string t = "  for (long long i = " + first + "; i < n; i += stride) {\n";
+    t += program_body(d, "", [&](int k) {
+      const InputView& in = d.in[k];
+      return from_value(in.type, "__ldg(in" + std::to_string(k) + " + (" + index_expr(d, in) + "))");
+    });
+    t += "    out[i] = " + to_value(d.out_type, "v" + last) + ";\n  }\n";
+    return t;
+  };
+  if (d.pairs) {
+    // every input is laid out like the output and 16-byte aligned: two
+    // elements per thread per step, one vector load per input
+    s += "  const long long npairs = n >> 1;\n";
+    s += "  for (long long p = tid; p < npairs; p += stride) {\n";
+    for (size_t k = 0; k < d.in.size(); ++k)
+      s += std::string("    const ") + pair_type(d.in[k].type) + " x" + std::to_string(k) +
+           " = __ldcs(reinterpret_cast<const " + pair_type(d.in[k].type) + "*>(in" +
+           std::to_string(k) + ") + p);\n";
+    for (int e = 0; e < 2; ++e) {
+      const std::string sfx = e == 0 ? "_0" : "_1";
+      s += program_body(d, sfx, [&](int k) {
+        const int t = d.in[k].type;
+        const std::string x = "x" + std::to_string(k);
+        if (t == DS_FUSED_PACKED)
+          return std::string("ds2{") + x + (e == 0 ? ".x, " : ".z, ") + x + (e == 0 ? ".y}" : ".w}");
+        return from_value(t, x + (e == 0 ? ".x" : ".y"));
+      });
+    }
+    const std::string r0 = "v" + last + "_0", r1 = "v" + last + "_1";
+    if (d.out_type == DS_FUSED_F64)
+      s += "    __stcs(reinterpret_cast<double2*>(out) + p, make_double2(to_f64(" + r0 +
+           "), to_f64(" + r1 + ")));\n";
+    else if (d.out_type == DS_FUSED_F32)
+      s += "    __stcs(reinterpret_cast<float2*>(out) + p, make_float2(" + to_value(DS_FUSED_F32, r0) +
+           ", " + to_value(DS_FUSED_F32, r1) + "));\n";
+    else
+      s += "    __stcs(reinterpret_cast<float4*>(out) + p, make_float4(" + r0 + ".hi, " + r0 +
+           ".lo, " + r1 + ".hi, " + r1 + ".lo));\n";
+    s += "  }\n";
+    s += scalar_loop("2 * npairs + tid");  // the odd last element
+  } else {
+    s += scalar_loop("tid");
+  }
+  s += "}\n";
   return s;
 }
 
@@ -296,6 +348,9 @@ int describe(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
     v.full = full;
     if (prod(b->dims, r) > 0 && b->data == nullptr) return invalid("ds_fused: null input pointer");
   }
+  d.pairs = aligned(out->data, 16);
+  for (int32_t k = 0; k < n_inputs; ++k)
+    d.pairs = d.pairs && d.in[k].full && aligned(inputs[k]->data, 16);
   d.ops.assign(ops, ops + n_ops);
   for (int32_t j = 0; j < n_ops; ++j) {
     const ds_fused_op& o = ops[j];
@@ -432,7 +487,7 @@ int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_typ
   args[n_inputs] = &ptrs[n_inputs];
   long long n = d.n;
   args[n_inputs + 1] = &n;
-  const unsigned grid = grid_for(d.n, 256, 8);
+  const unsigned grid = grid_for(d.pairs ? (d.n + 1) / 2 : d.n, 256, 8);
   ProfileScope prof("fused", static_cast<cudaStream_t>(stream));
   if (driver().launch(fn, grid, 1, 1, 256, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
                       nullptr) != CUDA_SUCCESS)

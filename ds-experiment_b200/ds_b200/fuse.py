@@ -250,14 +250,14 @@ class jit:
             t = a.t if isinstance(a, Packed) else a
             types.append(_lib.DS_FUSED_PACKED if isinstance(a, Packed) else _TYPES[a.dtype])
             logical.append(tuple(t.shape[:-1]) if isinstance(a, Packed) else tuple(t.shape))
-            b, d = _lib.make_buffer(1, tuple(t.shape))  # pointer unused
+            b, d = _lib.make_buffer(256, tuple(t.shape))  # aligned stand-in pointer
             bufs.append(b)
             keep.append(d)
         shape = _broadcast(logical)
         out_type = _OUT[self.out_dtype] if self.out_dtype else (
             _lib.DS_FUSED_F64 if _lib.DS_FUSED_F64 in types else _lib.DS_FUSED_F32)
         oshape = shape + ((2,) if out_type == _lib.DS_FUSED_PACKED else ())
-        ob, od = _lib.make_buffer(1, oshape)
+        ob, od = _lib.make_buffer(256, oshape)
         arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
             *[ctypes.pointer(b) for b in bufs])
         ty = (ctypes.c_int32 * max(len(types), 1))(*types)

@@ -45,13 +45,18 @@ def test_broadcast_index_expressions():
     assert "out[i] = to_f64(" in src
 
 
-def test_output_types():
+def test_output_types_and_pair_path():
     x32 = torch.zeros(8, dtype=torch.float32)
-    assert "__fadd_rn(" in fuse.jit(lambda a: a * a).source(x32)          # f32 result
+    src = fuse.jit(lambda a: a * a).source(x32)                          # f32 result
+    assert "__fadd_rn(" in src and "reinterpret_cast<const float2*>(in0) + p" in src
     src = fuse.jit(lambda a: a + a, out_dtype="packed").source(torch.zeros(8, dtype=torch.float64))
-    assert "make_float2(" in src
+    assert "make_float4(" in src and "reinterpret_cast<const double2*>(in0) + p" in src
     src = fuse.jit(lambda a: a - 1.0).source(fuse.Packed(torch.zeros(8, 2)))
-    assert "float2 p0" in src
+    assert "ds2{x0.x, x0.y}" in src and "ds2{x0.z, x0.w}" in src
+    # a broadcast input takes the one-element loop only
+    src = fuse.jit(lambda a, b: a * b).source(torch.zeros(4, 8, dtype=torch.float64),
+                                              torch.zeros(8, dtype=torch.float64))
+    assert "npairs" not in src and "% 8LL" in src
 
 
 def test_bad_broadcast_is_rejected():
