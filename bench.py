@@ -241,8 +241,8 @@ def run_ours(args):
     fam = "ozaki_gemm"
     k_ms, k_n = _lib.profile_read(fam)
     launches = {}
-    for f in ("ozaki_split", "ozaki_split_rows", "ozaki_colmax", "ozaki_split_cols",
-              "ozaki_gemm", "ozaki_crt",
+    for f in ("ozaki_split", "ozaki_split_rows", "ozaki_colmax", "ozaki_split_rows_colmax",
+              "ozaki_split_cols", "ozaki_gemm", "ozaki_crt",
               "dot_simt", "dot_vec", "elementwise",
               "reduce", "recurrence"):
         t, n = _lib.profile_read(f)
@@ -775,7 +775,8 @@ def run_large(args):
     k_ms, k_n = _lib.profile_read(fam)
     per = k_ms / args.steps  # device time of the family per step (all its launches)
     launches = {}
-    for f in ("ozaki_split_rows", "ozaki_colmax", "ozaki_split_cols", "ozaki_gemm",
+    for f in ("ozaki_split_rows", "ozaki_colmax", "ozaki_split_rows_colmax", "ozaki_split_cols",
+              "ozaki_gemm",
               "ozaki_crt", "dot_vec"):
         t_, n_ = _lib.profile_read(f)
         if n_:

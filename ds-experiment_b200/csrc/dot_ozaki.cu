@@ -336,13 +336,12 @@ __host__ __device__ constexpr int split_rows_threads(int64_t K) {
   return K > 4096 && K <= 16 * kSplitRowsMaxThreads ? kSplitRowsMaxThreads : 256;
 }
 
-__global__ void __launch_bounds__(kSplitRowsMaxThreads, 2)
-split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
-                    int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts,
-                    int64_t row0) {
+__device__ __forceinline__ void split_rows_body(const DotOperand& o, int64_t rows, int64_t K,
+                                                int64_t rows_pad, int64_t Kp, int64_t batch,
+                                                int P, uint8_t* __restrict__ planes,
+                                                int* __restrict__ shifts, int64_t r, int64_t b) {
   __shared__ double s_max[kSplitRowsMaxThreads / 32];
   __shared__ int s_bad[kSplitRowsMaxThreads / 32];
-  const int64_t r = row0 + blockIdx.x, b = blockIdx.y;
   const bool live = r < rows;
   const int64_t base = b * o.s_b + r * o.s_r;
   const bool vec = o.f64 && o.s_k == 1 && (reinterpret_cast<uintptr_t>(o.f64 + base) & 15) == 0;
@@ -438,6 +437,14 @@ split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int
   }
 }
 
+__global__ void __launch_bounds__(kSplitRowsMaxThreads, 2)
+split_kmajor_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
+                    int64_t batch, int P, uint8_t* __restrict__ planes, int* __restrict__ shifts,
+                    int64_t row0) {
+  split_rows_body(o, rows, K, rows_pad, Kp, batch, P, planes, shifts, row0 + blockIdx.x,
+                  blockIdx.y);
+}
+
 // Operand rows contiguous across rows (s_r == 1, e.g. B[K, N] row-major):
 // blocks of 64 rows x 256 K.  Pairs of adjacent rows load as one 16-byte
 // value when the layout allows it (paired_rows).
@@ -469,15 +476,15 @@ __device__ __forceinline__ void load_row_pair(const DotOperand& o, bool paired, 
 // across blocks with atomicMax on an encoded exponent (codes start at 0).
 constexpr int kColmaxSlab = 128;
 
-__global__ void __launch_bounds__(256, 6)
-colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
-              int* __restrict__ codes) {
+__device__ __forceinline__ void colmax_body(const DotOperand& o, int64_t rows, int64_t K,
+                                            int64_t rows_pad, int* __restrict__ codes,
+                                            int64_t bx, int64_t by, int64_t b) {
   __shared__ double s_max[8][kColTileR];
   __shared__ int s_bad[8][kColTileR];
   const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kColTileR, b = blockIdx.z;
+  const int64_t r0 = bx * kColTileR;
   const int64_t row = r0 + 2 * lane;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * kColmaxSlab;
+  const int64_t k0 = by * kColmaxSlab;
   double m0 = 0.0, m1 = 0.0;
   bool bad = false, bad1 = false;
   const int64_t k1 = k0 + kColmaxSlab < K ? k0 + kColmaxSlab : K;
@@ -516,6 +523,30 @@ colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
     }
     const int code = nf ? kExpNonFinite : (mx == 0.0 ? 0 : ilogb(mx) + 1 + kExpBias);
     if (r < rows && code != 0) atomicMax(&codes[b * rows_pad + r], code);
+  }
+}
+
+__global__ void __launch_bounds__(256, 6)
+colmax_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad,
+              int* __restrict__ codes) {
+  colmax_body(o, rows, K, rows_pad, codes, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
+// One launch for the row split of A (compute-bound) and the column maxima of
+// B (memory-bound), their blocks interleaved evenly so the two overlap on
+// every SM: block t is a column-maximum block when floor((t + 1) nc / total)
+// steps up.  256 threads (rows of at most 4096 values).
+__global__ void __launch_bounds__(256, 4)
+split_rows_colmax_kernel(DotOperand a, int64_t rows_a, int64_t rows_a_pad, DotOperand bop,
+                         int64_t rows_b, int64_t rows_b_pad, int64_t K, int64_t Kp, int P,
+                         uint8_t* __restrict__ planes_a, int* __restrict__ shifts_a,
+                         int* __restrict__ codes_b, int64_t nc, int64_t cgx, int64_t cgy) {
+  const int64_t t = blockIdx.x, total = rows_a_pad + nc;
+  const int64_t c0 = t * nc / total, c1 = (t + 1) * nc / total;
+  if (c1 > c0) {
+    colmax_body(bop, rows_b, K, rows_b_pad, codes_b, c0 % cgx, c0 / cgx % cgy, c0 / (cgx * cgy));
+  } else {
+    split_rows_body(a, rows_a, K, rows_a_pad, Kp, 1, P, planes_a, shifts_a, t - c0, 0);
   }
 }
 
@@ -1542,7 +1573,26 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   // CTA pairs of the GEMM blocked in tcgen05.alloc on some SMs; it is not
   // used.
   DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
-  {
+  // A split by rows and B by columns (the usual row-major A and B): the
+  // column maxima of B are taken in the same launch as A's row split.
+  const bool merged = p.batch == 1 && split_by_rows(p.a, p.M) && !split_by_rows(p.b, p.N) &&
+                      split_rows_threads(p.K) == 256;
+  if (merged) {
+    ProfileScope prof("ozaki_split", s);
+    DSB_CUDA_TRY(cudaMemsetAsync(cb, 0, sizeof(int) * g.Np, s));
+    const int64_t cgx = g.Np / kColTileR, cgy = (p.K + kColmaxSlab - 1) / kColmaxSlab;
+    const int64_t nc = cgx * cgy;
+    {
+      ProfileScope prof2("ozaki_split_rows_colmax", s);
+      split_rows_colmax_kernel<<<static_cast<unsigned>(g.Mp + nc), 256, 0, s>>>(
+          p.a, p.M, g.Mp, p.b, p.N, g.Np, p.K, g.Kp, P, planes_a, sa, cb, nc, cgx, cgy);
+      if (int st = launch_status()) return st;
+    }
+    ProfileScope prof3("ozaki_split_cols", s);
+    dim3 g2(static_cast<unsigned>(g.Np / kColTileR), static_cast<unsigned>(g.Kp / kColTileK), 1);
+    split_cols_kernel<<<g2, 256, 0, s>>>(p.b, p.N, p.K, g.Np, g.Kp, 1, P, cb, planes_b, sb);
+    if (int st = launch_status()) return st;
+  } else {
     ProfileScope prof("ozaki_split", s);
     if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
       return st;
