@@ -823,11 +823,13 @@ def run_large(args):
         line["value"] = round(flops / (ms * 1e-3) / 1e9, 1)
         info = _lib.gemm_info(L.shape[0], LARGE_N, LARGE_K)
         ach = info["tensor_ops_per_launch"] / (per * 1e-3) / 1e12
-        peak = 2.0 * peaks["bf16_tflops"]
+        # a ~50 ms kernel back to back for seconds: the sustained figure
+        # (power cap) is its ceiling
+        peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         line["roofline"] = {"bound": "tensor", "kernel": fam, "achieved": round(ach, 1),
                             "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4),
                             "traffic": None, "kernel_ms_per_step": round(per, 4),
-                            "peak_source": f"2 x {peak_src} bf16_tflops"}
+                            "peak_source": f"2 x {peak_src} bf16_tflops_sustained"}
         line["config"] = {"workload": "ds_dot_general_f64 65536x8192x8192, A rows sharded, "
                                       "B replicated", "M": LARGE_M, "N": LARGE_N, "K": LARGE_K,
                           "rows_per_rank": int(L.shape[0]), "parallelism": f"rows{world}",
