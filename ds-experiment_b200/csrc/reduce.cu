@@ -191,6 +191,114 @@ reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
   }
 }
 
+// Full reduction of long aligned f64 input (add / subtract body), stage 1,
+// as a bulk-copy stream: each block owns every G-th chunk of kBulkChunk
+// values and keeps kBulkStages chunks in flight with cp.async.bulk into
+// shared memory (one mbarrier per stage), so the bytes in flight do not
+// depend on registers or occupancy.  The threads fold the values of a chunk
+// exactly in f64 (two_sum, as reduce_full_kernel) and the block writes one
+// DS partial.  Block 0 also folds the last n mod kBulkChunk values.  Every
+// wait is bounded; a block whose wait runs out stops issuing, waits (bounded)
+// for its copies in flight and writes a NaN partial, so the result is NaN.
+constexpr int kBulkChunk = 4096;  // values per chunk (32 KB)
+constexpr int kBulkStages = 3;
+constexpr int kBulkBlocksPerSm = 2;
+constexpr long long kBulkTimeoutCycles = 2000000000LL;  // ~1 s
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > kBulkTimeoutCycles) return false;
+  }
+}
+
+__device__ __forceinline__ void bulk_issue(double* dst, const double* src, uint32_t bytes,
+                                           uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads)
+reduce_bulk_kernel(const double* __restrict__ x, int64_t n, ds2* __restrict__ partials) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  double* buf = reinterpret_cast<double*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBulkStages * kBulkChunk * sizeof(double));
+  const int64_t nchunks = n / kBulkChunk;
+  const int64_t G = gridDim.x;
+  const int64_t mine = nchunks > blockIdx.x ? (nchunks - blockIdx.x + G - 1) / G : 0;
+  constexpr uint32_t kBytes = kBulkChunk * sizeof(double);
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kBulkStages; ++st)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[st])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int64_t i = 0; i < kBulkStages && i < mine; ++i)
+      bulk_issue(buf + i * kBulkChunk, x + (blockIdx.x + i * G) * kBulkChunk, kBytes, &full[i]);
+  }
+  __syncthreads();
+  double s0 = 0.0, c0 = 0.0, s1 = 0.0, c1 = 0.0;
+  bool failed = false;
+  int64_t consumed = 0;
+  for (int64_t i = 0; i < mine; ++i) {
+    const int st = static_cast<int>(i % kBulkStages);
+    const uint32_t parity = static_cast<uint32_t>((i / kBulkStages) & 1);
+    const bool arrived = bulk_wait(&full[st], parity);
+    if (__syncthreads_or(!arrived)) {
+      failed = true;
+      break;
+    }
+    const double2* p = reinterpret_cast<const double2*>(buf + st * kBulkChunk) + threadIdx.x;
+#pragma unroll
+    for (int u = 0; u < kBulkChunk / 2 / kThreads; ++u) {
+      const double2 v = p[u * kThreads];
+      two_sum_acc(s0, c0, v.x);
+      two_sum_acc(s1, c1, v.y);
+    }
+    consumed = i + 1;
+    __syncthreads();  // every read of this stage is done before it is refilled
+    if (threadIdx.x == 0 && i + kBulkStages < mine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bulk_issue(buf + st * kBulkChunk, x + (blockIdx.x + (i + kBulkStages) * G) * kBulkChunk,
+                 kBytes, &full[st]);
+    }
+  }
+  if (failed && threadIdx.x == 0) {
+    // wait (bounded) for the copies still in flight before the block exits
+    const int64_t issued = mine < consumed + kBulkStages ? mine : consumed + kBulkStages;
+    for (int64_t i = consumed; i < issued; ++i)
+      bulk_wait(&full[i % kBulkStages], static_cast<uint32_t>((i / kBulkStages) & 1));
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = nchunks * kBulkChunk + threadIdx.x; i < n; i += kThreads)
+      two_sum_acc(s0, c0, __ldcs(x + i));
+  }
+  two_sum_acc(s0, c0, s1);
+  ds2 acc = from_f64(__dadd_rn(s0, __dadd_rn(c0, c1)));
+  acc = block_combine(false, acc);
+  if (threadIdx.x == 0) {
+    const float nan = __int_as_float(0x7fffffff);
+    partials[blockIdx.x] = failed ? ds2{nan, nan} : acc;
+  }
+}
+
 // Full reduction, stage 2: one block folds the G partials.
 __global__ void __launch_bounds__(kThreads)
 reduce_partials_kernel(const ds2* __restrict__ partials, int g, int body, Dst dst,
@@ -249,6 +357,53 @@ size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {
   return g > 1 ? static_cast<size_t>(g) * sizeof(ds2) : 0;
 }
 
+namespace {
+
+// Long aligned f64 input with an add/subtract body takes the bulk-copy
+// kernel; 16 B alignment is what cp.async.bulk needs.
+constexpr int64_t kBulkMinElements = int64_t(1) << 20;
+
+bool use_bulk(const Src& src, int64_t n, int body) {
+  return src.f64 != nullptr && src.vec && body != 2 && n >= kBulkMinElements;
+}
+
+int bulk_blocks() { return sm_count() * kBulkBlocksPerSm; }
+
+size_t bulk_smem_bytes() {
+  return static_cast<size_t>(kBulkStages) * kBulkChunk * sizeof(double) +
+         kBulkStages * sizeof(uint64_t);
+}
+
+// Stage 1 of a full reduction into `partials`; returns the number of
+// partials, or -1 after a launch error (the error is set).  With one block
+// and !always_partials the old kernel writes the result directly.
+int full_stage1(const Src& src, int64_t n, int body, ds2* partials, Dst dst,
+                const double* init_f64, const float* init_hi, const float* init_lo,
+                bool always_partials, cudaStream_t s) {
+  if (use_bulk(src, n, body)) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+      attr_err = cudaFuncSetAttribute(reduce_bulk_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(bulk_smem_bytes()));
+    });
+    if (attr_err != cudaSuccess) {
+      cuda_status(attr_err);
+      return -1;
+    }
+    const int g = bulk_blocks();
+    reduce_bulk_kernel<<<g, kThreads, bulk_smem_bytes(), s>>>(src.f64, n, partials);
+    return launch_status() == DS_OK ? g : -1;
+  }
+  const int g = n == 0 ? 1 : reduce_full_blocks(n);
+  reduce_full_kernel<<<g, kThreads, 0, s>>>(src, n, body, partials, dst, init_f64, init_hi,
+                                            init_lo, always_partials);
+  return launch_status() == DS_OK ? g : -1;
+}
+
+}  // namespace
+
 int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
   Src src{a.in_f64, a.in_packed ? a.in_packed : a.in_hi, a.in_lo, false, a.in_packed != nullptr};
   src.vec = a.in_f64      ? aligned(a.in_f64, 16)
@@ -267,10 +422,11 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
     }
     ds2* partials = static_cast<ds2*>(a.workspace);
     ProfileScope prof("reduce", s);
-    reduce_full_kernel<<<g, kThreads, 0, s>>>(src, red, a.body, partials, dst, a.init_f64,
-                                              a.init_hi, a.init_lo);
-    if (g > 1) {
-      reduce_partials_kernel<<<1, kThreads, 0, s>>>(partials, g, a.body, dst, a.init_f64,
+    const int used = full_stage1(src, red, a.body, partials, dst, a.init_f64, a.init_hi,
+                                 a.init_lo, false, s);
+    if (used < 0) return DS_INTERNAL;
+    if (used > 1) {
+      reduce_partials_kernel<<<1, kThreads, 0, s>>>(partials, used, a.body, dst, a.init_f64,
                                                     a.init_hi, a.init_lo);
     }
     return launch_status();
@@ -493,9 +649,9 @@ int reduce_sharded_launch(const ShardedReduceArgs& a, cudaStream_t s) {
   Dst dst{a.out, nullptr, nullptr};
   ds2* partials = static_cast<ds2*>(a.workspace);
   ProfileScope prof("reduce", s);
-  reduce_full_kernel<<<g, kThreads, 0, s>>>(src, a.n, a.body, partials, dst, nullptr, nullptr,
-                                            nullptr, true);
-  reduce_exchange_kernel<<<1, kThreads, 0, s>>>(partials, g, a.n, a.body, dst, a.init, peers,
+  const int used = full_stage1(src, a.n, a.body, partials, dst, nullptr, nullptr, nullptr, true, s);
+  if (used < 0) return DS_INTERNAL;
+  reduce_exchange_kernel<<<1, kThreads, 0, s>>>(partials, used, a.n, a.body, dst, a.init, peers,
                                                 a.world, a.rank, a.epoch, a.timeout_ns);
   return launch_status();
 }
