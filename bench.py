@@ -348,6 +348,15 @@ def run_ours(args):
                               "reference_ds_path_max_abs_err": ref_err,
                               "sampled_entries": int(len(rows)),
                               "truth": "exact products summed with math.fsum"}
+        # the config's float32 variant: A and B rounded to f32, split as (v, 0)
+        A32 = A.astype(np.float32).astype(np.float64)
+        B32 = B.astype(np.float32).astype(np.float64)
+        C32 = ops.ds_matmul_f64(torch.from_numpy(A32).to(dev), torch.from_numpy(B32).to(dev),
+                                algorithm=algo).cpu().numpy()
+        e32, _, r32, c32, t32 = gemm_error(C32, A32, B32)
+        result["accuracy"]["f32_inputs"] = {
+            "max_abs_err_vs_exact": e32,
+            "reference_ds_path_max_abs_err": reference_gemm_error(A32, B32, r32, c32, t32)}
         if world == 1:
             result["cpu_baseline"] = cpu_baseline_gemm(A, B)
             if not args.no_secondary:
