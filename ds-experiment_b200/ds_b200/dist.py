@@ -109,7 +109,8 @@ class PeerExchange:
     Construction is collective: every rank allocates its buffer, the CUDA
     IPC handles are all-gathered through the process group, every rank maps
     the others' buffers, and a barrier ends it.  Every use (`next_epoch`)
-    must happen on all ranks in the same order, like a collective.
+    must happen on all ranks in the same order, like a collective, and on
+    one stream per rank (the calls share a cached workspace).
     `close()` is collective too.  At most 8 ranks.
     """
 
@@ -144,6 +145,7 @@ class PeerExchange:
             raise
         self.epoch = 0
         self.closed = False
+        self._call_state = None
         dist.barrier(group=group)
 
     def next_epoch(self) -> int:
@@ -183,21 +185,34 @@ def _sum_exchange_cuda(x_local: torch.Tensor, init: float, exchange: PeerExchang
                        body: int) -> torch.Tensor:
     import ctypes
     from . import _lib, ops
+    if x_local.dtype != torch.float64 or not x_local.is_cuda:
+        raise ValueError("the peer-exchange sum takes float64 CUDA tensors")
     x = x_local.contiguous()
     L = _lib.lib()
-    ib, idims = _lib.make_buffer(x.data_ptr(), tuple(x.shape))
+    # per-call host work is kept small: every rank's step waits for the
+    # slowest rank, so host time per call adds to the step
+    st = exchange._call_state
+    if st is None or st["shape"] != tuple(x.shape) or st["device"] != x.device:
+        ib, idims = _lib.make_buffer(0, tuple(x.shape))
+        ws_bytes = int(L.ds_reduce_f64_sharded_workspace_size(ctypes.byref(ib)))
+        st = exchange._call_state = {
+            "shape": tuple(x.shape), "device": x.device, "ib": ib, "idims": idims,
+            "ws": torch.empty(max(ws_bytes, 8), dtype=torch.uint8, device=x.device),
+            "ws_bytes": ws_bytes,
+            "ptrs": (ctypes.c_void_p * exchange.world)(*exchange.ptrs),
+            "out_dims": (ctypes.c_int64 * 1)(0)}
+        st["wsp"] = ctypes.c_void_p(st["ws"].data_ptr())
+    ib = st["ib"]
+    ib.data = x.data_ptr()
     it = ops._scalar(init, torch.float64, x.device)
-    tb, tdims = _lib.make_buffer(it.data_ptr(), ())
     out = torch.empty((), dtype=torch.float64, device=x.device)
-    ob, odims = _lib.make_buffer(out.data_ptr(), ())
-    ws_bytes = L.ds_reduce_f64_sharded_workspace_size(ctypes.byref(ib))
-    ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=x.device)
-    ptrs = (ctypes.c_void_p * exchange.world)(*exchange.ptrs)
+    tb = _lib.DsBuffer(it.data_ptr(), st["out_dims"], 0)
+    ob = _lib.DsBuffer(out.data_ptr(), st["out_dims"], 0)
     stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
     _lib.check(L.ds_reduce_f64_sharded(
-        ctypes.byref(ib), ctypes.byref(tb), body, ctypes.byref(ob), ptrs, exchange.world,
-        exchange.rank, exchange.next_epoch(), exchange.timeout_ms,
-        ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream), "ds_reduce_f64_sharded")
+        ctypes.byref(ib), ctypes.byref(tb), body, ctypes.byref(ob), st["ptrs"], exchange.world,
+        exchange.rank, exchange.next_epoch(), exchange.timeout_ms, st["wsp"], st["ws_bytes"],
+        stream), "ds_reduce_f64_sharded")
     return out
 
 
