@@ -121,6 +121,10 @@ def _scalar(value: float, dtype, device) -> torch.Tensor:
     """A 0-d device tensor holding `value`, cached per (device, stream, dtype,
     value) so that repeated calls launch no fill kernel; the cache key holds
     the stream because the fill is ordered only on the stream that made it."""
+    if torch.cuda.is_current_stream_capturing():
+        # made inside a CUDA graph capture: its fill runs at replay, so it is
+        # not kept for eager calls
+        return torch.full((), float(value), dtype=dtype, device=device)
     stream = torch.cuda.current_stream(device).cuda_stream
     key = (device.index, stream, dtype, float(value).hex())  # hex keeps -0.0 apart
     t = _SCALARS.get(key)
