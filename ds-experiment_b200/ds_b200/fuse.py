@@ -277,3 +277,36 @@ class jit:
         raises on a compilation error.  Needs no GPU."""
         self.source(*args)
         self._last_check()
+
+
+_KIND = {"f64": _lib.DS_FUSED_F64, "f32": _lib.DS_FUSED_F32, "packed": _lib.DS_FUSED_PACKED}
+
+
+def run_program(prog, inputs, out_kind: str, shape) -> torch.Tensor:
+    """Run an operation list directly: `prog` holds (code, a, b, value)
+    tuples in SSA order, `inputs` (kind, tensor) pairs with kind "f64",
+    "f32" or "packed"; the result has the logical `shape` and `out_kind`."""
+    tensors = [t.contiguous() for _, t in inputs]
+    device = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda or t.device != device:
+            raise ValueError("fused inputs must be CUDA tensors on one device")
+    types = [_KIND[k] for k, _ in inputs]
+    shape = tuple(shape)
+    if out_kind == "packed":
+        out = torch.empty(shape + (2,), dtype=torch.float32, device=device)
+    else:
+        out = torch.empty(shape, dtype=torch.float64 if out_kind == "f64" else torch.float32,
+                          device=device)
+    comp = _Compiled(prog, len(tensors))
+    bufs, keep = _buffers(tensors)
+    ob, od = _lib.make_buffer(out.data_ptr(), tuple(out.shape))
+    arr = (ctypes.POINTER(_lib.DsBuffer) * len(bufs))(*[ctypes.pointer(b) for b in bufs])
+    ty = (ctypes.c_int32 * len(types))(*types)
+    if device.index is not None and device.index != torch.cuda.current_device():
+        with torch.cuda.device(device):
+            st = jit._run(comp, ty, arr, len(bufs), _KIND[out_kind], ob)
+    else:
+        st = jit._run(comp, ty, arr, len(bufs), _KIND[out_kind], ob)
+    _lib.check(st, "ds_fused_run")
+    return out
