@@ -1439,12 +1439,36 @@ int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_
 
 }  // namespace
 
-bool dot_ozaki_supported(int64_t M, int64_t N, int64_t K) {
-  return M >= 2 && N >= 2 && K >= 1 && K <= kMaxK;
+// Contractions longer than kMaxK run as chunks of kMaxK: each chunk is one
+// exact integer product, rebuilt and rounded to f64, and the chunk results
+// are added in f64 (one more rounding per chunk, far below the DS level).
+bool dot_ozaki_supported(int64_t M, int64_t N, int64_t K) { return M >= 2 && N >= 2 && K >= 1; }
+
+namespace {
+
+int64_t k_chunks(int64_t K) { return (K + kMaxK - 1) / kMaxK; }
+
+size_t chunk_result_bytes(int64_t batch, int64_t M, int64_t N) {
+  return static_cast<size_t>(round_up(batch * M * N * static_cast<int64_t>(sizeof(double)), 1024));
 }
 
+__global__ void add_f64_kernel(double* __restrict__ acc, const double* __restrict__ part, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    acc[i] = __dadd_rn(acc[i], part[i]);
+}
+
+__global__ void store_result_kernel(DotResult c, const double* __restrict__ v, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    put_result(c, i, v[i]);
+}
+
+}  // namespace
+
 size_t dot_ozaki_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
-  return layout_of(batch, M, N, K).total;
+  if (K <= kMaxK) return layout_of(batch, M, N, K).total;
+  return layout_of(batch, M, N, kMaxK).total + 2 * chunk_result_bytes(batch, M, N);
 }
 
 int dot_ozaki_params(int64_t K, int* moduli, int* bits) {
@@ -1460,7 +1484,46 @@ int dot_ozaki_kernel_info(int* cta_pairs, int* query_error) {
   return g.err == cudaSuccess ? DS_OK : cuda_status(g.err);
 }
 
+namespace {
+int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s);
+}
+
 int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (p.K <= kMaxK || p.batch == 0 || p.M == 0 || p.N == 0)
+    return dot_ozaki_one(p, workspace, workspace_bytes, s);
+  const size_t need = dot_ozaki_workspace_bytes(p.batch, p.M, p.N, p.K);
+  if (workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(DS_INVALID_ARGUMENT, "dot_general: workspace too small (need " +
+                                              std::to_string(need) + " bytes, 256-byte aligned)");
+  const size_t one = layout_of(p.batch, p.M, p.N, kMaxK).total;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  double* acc = reinterpret_cast<double*>(ws + one);
+  double* part = reinterpret_cast<double*>(ws + one + chunk_result_bytes(p.batch, p.M, p.N));
+  const int64_t n = p.batch * p.M * p.N;
+  const unsigned grid = grid_for(n, 256, 8);
+  for (int64_t c = 0; c < k_chunks(p.K); ++c) {
+    const int64_t k0 = c * kMaxK;
+    DotProblem q = p;
+    q.K = p.K - k0 < kMaxK ? p.K - k0 : kMaxK;
+    auto shift = [k0](DotOperand& o) {
+      const int64_t off = k0 * o.s_k;
+      if (o.f64) o.f64 += off;
+      if (o.hi) o.hi += off;
+      if (o.lo) o.lo += off;
+    };
+    shift(q.a);
+    shift(q.b);
+    q.c = DotResult{c == 0 ? acc : part, nullptr, nullptr};
+    if (int st = dot_ozaki_one(q, ws, one, s)) return st;
+    if (c > 0) add_f64_kernel<<<grid, 256, 0, s>>>(acc, part, n);
+  }
+  store_result_kernel<<<grid, 256, 0, s>>>(p.c, acc, n);
+  return launch_status();
+}
+
+namespace {
+
+int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   if (p.batch == 0 || p.M == 0 || p.N == 0) return ok();
   const Layout g = layout_of(p.batch, p.M, p.N, p.K);
   if (workspace_bytes < g.total || !aligned(workspace, 256))
@@ -1602,5 +1665,7 @@ int dot_ozaki(const DotProblem& p, void* workspace, size_t workspace_bytes, cuda
   if (int st = launch_gemm(0, static_cast<int>(g.Mp / tile_rows), s)) return st;
   return launch_crt(0, p.batch * p.M, s);
 }
+
+}  // namespace
 
 }  // namespace dsb

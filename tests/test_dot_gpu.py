@@ -164,3 +164,19 @@ def test_precision_highest_256(ops):
     f32 = (A * A) @ B
     assert np.mean(np.abs(got - f64)) <= np.mean(np.abs(f32 - f64))
 
+
+
+def test_long_contraction_runs_in_chunks(ops):
+    """K above the int32 limit of one u8 residue product (32768) runs as
+    chunks on the tensor cores; accuracy stays at the DS level, and an Inf in
+    the second chunk reaches the outputs it touches."""
+    rng = np.random.default_rng(40)
+    M, N, K = 48, 40, 70_001
+    A = rng.uniform(-1, 1, (M, K))
+    B = rng.uniform(-1, 1, (K, N))
+    got = host(ops.ds_matmul_f64(cu(A), cu(B)))
+    check_gemm(got, A, B, samples=96, ref=ds_pass_ref.dot_general_f64(A, B))
+    A[3, 50_000] = np.inf
+    got = host(ops.ds_matmul_f64(cu(A), cu(B)))
+    assert np.all(np.isinf(got[3]) | np.isnan(got[3]))
+    assert np.all(np.isfinite(np.delete(got, 3, axis=0)))
