@@ -17,3 +17,29 @@ def test_shard_rows_tile_the_range():
         parts = [bench.shard_rows(n, r, world) for r in range(world)]
         assert parts[0][0] == 0 and parts[-1][1] == n
         assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+
+
+def _args(**kw):
+    import argparse
+    base = dict(gpus=1, steps=1, warmup=3, impl="reference", workload="gemm", algorithm="tensor",
+                no_secondary=True, kernels_only=False, n=0)
+    base.update(kw)
+    return argparse.Namespace(**base)
+
+
+REQUIRED = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "higher_is_better",
+            "scaling", "vs_baseline", "config", "cpu_baseline", "e2e"}
+
+
+def test_reference_arm_gemm_line():
+    line = bench.run_reference(_args())
+    assert REQUIRED <= set(line)
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+    assert line["metric"] == bench.METRIC
+
+
+def test_reference_arm_stream_line():
+    line = bench.run_reference_stream(_args(workload="fused_add_mul", n=1 << 20))
+    assert REQUIRED <= set(line)
+    assert line["cpu_baseline"]["kind"] == "port" and line["value"] > 0
