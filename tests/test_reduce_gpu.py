@@ -38,7 +38,8 @@ def ds_bound(x):
     return 2.0 ** -46 * (ax.max() * math.log2(max(ax.size, 2)) * 64 + 1e-300)
 
 
-@pytest.mark.parametrize("n", [1, 2, 3, 1000, 10_000, 65_537, 1 << 20])
+@pytest.mark.parametrize("n", [1, 2, 3, 1000, 10_000, 65_537, 1 << 20, (1 << 20) + 37,
+                               (1 << 22) + 4095])
 def test_config2_sum_error(ops, dso, n):
     x = config2_inputs(n)
     truth = exact.exact_sum(x)
@@ -195,3 +196,24 @@ def test_config2_large_property(ops, dso):
     h, l = dso.ds_reduce_f64_seq(x)
     ref_err = abs(float(h) + float(l) - truth)
     assert abs(got - truth) <= max(4 * ref_err, ds_bound(x))
+
+
+def test_bulk_stream_matches_per_thread_loads_in_accuracy(ops):
+    """Long aligned input takes the bulk-copy stream; an unaligned view of
+    the same values takes the per-thread-load kernel: both are exact sums
+    rounded once here (integers well inside 2^53)."""
+    from gpu_util import misaligned
+    rng = np.random.default_rng(21)
+    x = rng.integers(-2 ** 30, 2 ** 30, (1 << 21) + 3).astype(np.float64)
+    want = float(np.sum(x.astype(np.int64)))
+    assert float(host(ops.ds_sum_f64(cu(x)))) == want
+    assert float(host(ops.ds_sum_f64(misaligned(x)))) == want
+
+
+def test_bulk_stream_nan_inf(ops):
+    x = np.ones((1 << 21) + 9)
+    x[(1 << 20) + 3] = np.nan
+    assert math.isnan(float(host(ops.ds_sum_f64(cu(x)))))
+    x[(1 << 20) + 3] = np.inf
+    r = float(host(ops.ds_sum_f64(cu(x))))
+    assert math.isinf(r) or math.isnan(r)
