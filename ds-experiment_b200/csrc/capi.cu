@@ -439,6 +439,29 @@ int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init, const int64_t* dim
   return reduce_launch(a, as_stream(stream));
 }
 
+int ds_reduce_f64_multi(const ds_buffer* const* ins, const ds_buffer* const* inits,
+                        const int32_t* bodies, int32_t n_inputs, const int64_t* dimensions,
+                        int64_t n_dimensions, const ds_buffer* const* outs, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (n_inputs < 1 || !ins || !inits || !bodies || !outs)
+    return invalid("ds_reduce_f64_multi: at least one input, init, body and output");
+  for (int32_t k = 0; k < n_inputs; ++k) {
+    if (int st = check_buffers({ins[k], inits[k], outs[k]}, "ds_reduce_f64_multi")) return st;
+    if (ins[k]->rank != ins[0]->rank)
+      return invalid("ds_reduce_f64_multi: inputs must have the same shape");
+    for (int64_t d = 0; d < ins[k]->rank; ++d)
+      if (ins[k]->dims[d] != ins[0]->dims[d])
+        return invalid("ds_reduce_f64_multi: inputs must have the same shape");
+  }
+  // The reductions share the workspace one after another on the stream.
+  for (int32_t k = 0; k < n_inputs; ++k) {
+    if (int st = ds_reduce_f64(ins[k], inits[k], dimensions, n_dimensions, bodies[k], outs[k],
+                               workspace, workspace_bytes, stream))
+      return st;
+  }
+  return ok();
+}
+
 int ds_reduce_packed(const ds_buffer* in, const ds_buffer* init_hi, const ds_buffer* init_lo,
                      const int64_t* dimensions, int64_t n_dimensions, int32_t body,
                      const ds_buffer* out_hi, const ds_buffer* out_lo, void* workspace,

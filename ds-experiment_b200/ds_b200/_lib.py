@@ -93,6 +93,8 @@ SIGNATURES = {
     "ds_reduce_f64_noalloc": ([_BUF, _BUF, _I64P, _I64, _I32, _BUF, _VP], ctypes.c_int),
     "ds_reduce_packed": ([_BUF, _BUF, _BUF, _I64P, _I64, _I32, _BUF, _BUF, _VP, _SZ, _VP],
                          ctypes.c_int),
+    "ds_reduce_f64_multi": ([ctypes.POINTER(_BUF), ctypes.POINTER(_BUF), ctypes.POINTER(_I32), _I32,
+                             _I64P, _I64, ctypes.POINTER(_BUF), _VP, _SZ, _VP], ctypes.c_int),
     "ds_exchange_bytes": ([], _SZ),
     "ds_exchange_handle_bytes": ([], _SZ),
     "ds_exchange_alloc": ([ctypes.POINTER(_VP), _VP], ctypes.c_int),

@@ -179,6 +179,44 @@ def ds_reduce_from_f64(x: torch.Tensor, init: float = 0.0,
                                                       body=_BODIES[body], out=out)
 
 
+def ds_reduce_f64_multi(xs, inits=None, dimensions: Optional[Sequence[int]] = None,
+                        bodies=None):
+    """A variadic reduce: every f64 tensor in `xs` (one shape) reduced over
+    `dimensions` with its own body ("add", "sub", "mul") and init -> list."""
+    import ctypes
+    xs = [x.contiguous() for x in xs]
+    n = len(xs)
+    inits = [0.0] * n if inits is None else list(inits)
+    bodies = ["add"] * n if bodies is None else list(bodies)
+    if len(inits) != n or len(bodies) != n:
+        raise ValueError("one init and one body per input")
+    dims = _reduce_dims(xs[0].dim(), dimensions)
+    shape = _out_shape(xs[0].shape, dims)
+    dev = xs[0].device
+    outs = [torch.empty(shape, dtype=F64, device=dev) for _ in range(n)]
+    its = [_scalar(v, F64, dev) for v in inits]
+    keep = []
+
+    def bufs(ts):
+        arr = (ctypes.POINTER(_lib.DsBuffer) * n)()
+        for k, t in enumerate(ts):
+            b, d = _lib.make_buffer(t.data_ptr(), tuple(t.shape))
+            keep.append((b, d))
+            arr[k] = ctypes.pointer(b)
+        return arr
+    L = _lib.lib()
+    cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
+    ib = bufs(xs)
+    ws_bytes = int(L.ds_reduce_workspace_size(ib[0], cdims, len(dims)))
+    ws = torch.empty(max(ws_bytes, 8), dtype=torch.uint8, device=dev)
+    body_codes = (ctypes.c_int32 * n)(*[_BODIES[b] for b in bodies])
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(L.ds_reduce_f64_multi(ib, bufs(its), body_codes, n, cdims, len(dims), bufs(outs),
+                                     ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream),
+               "ds_reduce_f64_multi")
+    return outs
+
+
 def ds_sum_f64(x: torch.Tensor, dimensions=None) -> torch.Tensor:
     return ds_reduce_f64(x, 0.0, dimensions, "add")
 

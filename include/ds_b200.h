@@ -214,6 +214,18 @@ DS_API int ds_reduce_f64_noalloc(const ds_buffer* in, const ds_buffer* init,
                                  int32_t body, const ds_buffer* out,
                                  void* stream);
 
+/* A variadic reduce (stablehlo.reduce with several inputs, which the
+   reference pass leaves alone, DsTransformPass.cpp:377) whose body combines
+   each input with its own add / subtract / multiply: n_inputs f64 tensors of
+   one shape, each reduced over `dimensions` with bodies[k] and inits[k] into
+   outs[k].  The reductions run one after another on the stream and share the
+   workspace (ds_reduce_workspace_size of one input). */
+DS_API int ds_reduce_f64_multi(const ds_buffer* const* ins, const ds_buffer* const* inits,
+                               const int32_t* bodies, int32_t n_inputs,
+                               const int64_t* dimensions, int64_t n_dimensions,
+                               const ds_buffer* const* outs, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* DS reduce of a packed DS tensor in[..., 2] (the wire format of DsAdd and
    the other packed targets, cpp/ds_add.cpp:46-49) over `dimensions` of its
    logical shape in.dims[:-1]; init and result as in ds_reduce.  The

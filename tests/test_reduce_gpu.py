@@ -217,3 +217,19 @@ def test_bulk_stream_nan_inf(ops):
     x[(1 << 20) + 3] = np.inf
     r = float(host(ops.ds_sum_f64(cu(x))))
     assert math.isinf(r) or math.isnan(r)
+
+
+def test_variadic_reduce(ops):
+    """Several inputs, each with its own body and init, equal the single
+    reductions bit for bit (full and segmented)."""
+    import torch
+    rng = np.random.default_rng(31)
+    xs = [cu(rng.uniform(-1, 1, (64, 3001))) for _ in range(3)]
+    for dims in (None, (1,)):
+        outs = ops.ds_reduce_f64_multi(xs, inits=[0.0, 1.5, 1.0], bodies=["add", "sub", "mul"],
+                                       dimensions=dims)
+        for x, o, init, body in zip(xs, outs, [0.0, 1.5, 1.0], ["add", "sub", "mul"]):
+            want = ops.ds_reduce_f64(x, init=init, dimensions=dims, body=body)
+            assert_bits_equal(host(o), host(want), f"{body} {dims}")
+    with pytest.raises(Exception):
+        ops.ds_reduce_f64_multi([xs[0], torch.zeros(5, dtype=torch.float64, device="cuda")])
