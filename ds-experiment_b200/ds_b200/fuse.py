@@ -282,31 +282,51 @@ class jit:
 _KIND = {"f64": _lib.DS_FUSED_F64, "f32": _lib.DS_FUSED_F32, "packed": _lib.DS_FUSED_PACKED}
 
 
+class Prepared:
+    """An operation list with its input kinds and result kind, converted to
+    the C structures once and run many times: `prog` holds (code, a, b,
+    value) tuples in SSA order (the last is the result), `kinds` the kind of
+    each input ("f64", "f32" or "packed"), `out_kind` the result's."""
+
+    def __init__(self, prog, kinds: Sequence[str], out_kind: str):
+        if out_kind not in _KIND or any(k not in _KIND for k in kinds):
+            raise ValueError("fused kinds are 'f64', 'f32' or 'packed'")
+        self.ops = [tuple(o) for o in prog]
+        self.kinds = tuple(kinds)
+        self.out_kind = out_kind
+        self._comp = _Compiled(self.ops, len(self.kinds))
+        self._types = (ctypes.c_int32 * max(len(self.kinds), 1))(*[_KIND[k] for k in self.kinds])
+
+    def __call__(self, tensors: Sequence[torch.Tensor], shape) -> torch.Tensor:
+        """Run on `tensors` (one per input kind); the result has the logical
+        `shape` (the inputs broadcast to it)."""
+        if len(tensors) != len(self.kinds) or not tensors:
+            raise ValueError(f"the program takes {len(self.kinds)} input tensors")
+        tensors = [t.contiguous() for t in tensors]
+        device = tensors[0].device
+        for t in tensors:
+            if not t.is_cuda or t.device != device:
+                raise ValueError("fused inputs must be CUDA tensors on one device")
+        shape = tuple(shape)
+        if self.out_kind == "packed":
+            out = torch.empty(shape + (2,), dtype=torch.float32, device=device)
+        else:
+            out = torch.empty(shape, dtype=torch.float64 if self.out_kind == "f64"
+                              else torch.float32, device=device)
+        bufs, keep = _buffers(tensors)
+        ob, od = _lib.make_buffer(out.data_ptr(), tuple(out.shape))
+        arr = (ctypes.POINTER(_lib.DsBuffer) * len(bufs))(*[ctypes.pointer(b) for b in bufs])
+        if device.index is not None and device.index != torch.cuda.current_device():
+            with torch.cuda.device(device):
+                st = jit._run(self._comp, self._types, arr, len(bufs), _KIND[self.out_kind], ob)
+        else:
+            st = jit._run(self._comp, self._types, arr, len(bufs), _KIND[self.out_kind], ob)
+        _lib.check(st, "ds_fused_run")
+        return out
+
+
 def run_program(prog, inputs, out_kind: str, shape) -> torch.Tensor:
     """Run an operation list directly: `prog` holds (code, a, b, value)
     tuples in SSA order, `inputs` (kind, tensor) pairs with kind "f64",
     "f32" or "packed"; the result has the logical `shape` and `out_kind`."""
-    tensors = [t.contiguous() for _, t in inputs]
-    device = tensors[0].device
-    for t in tensors:
-        if not t.is_cuda or t.device != device:
-            raise ValueError("fused inputs must be CUDA tensors on one device")
-    types = [_KIND[k] for k, _ in inputs]
-    shape = tuple(shape)
-    if out_kind == "packed":
-        out = torch.empty(shape + (2,), dtype=torch.float32, device=device)
-    else:
-        out = torch.empty(shape, dtype=torch.float64 if out_kind == "f64" else torch.float32,
-                          device=device)
-    comp = _Compiled(prog, len(tensors))
-    bufs, keep = _buffers(tensors)
-    ob, od = _lib.make_buffer(out.data_ptr(), tuple(out.shape))
-    arr = (ctypes.POINTER(_lib.DsBuffer) * len(bufs))(*[ctypes.pointer(b) for b in bufs])
-    ty = (ctypes.c_int32 * len(types))(*types)
-    if device.index is not None and device.index != torch.cuda.current_device():
-        with torch.cuda.device(device):
-            st = jit._run(comp, ty, arr, len(bufs), _KIND[out_kind], ob)
-    else:
-        st = jit._run(comp, ty, arr, len(bufs), _KIND[out_kind], ob)
-    _lib.check(st, "ds_fused_run")
-    return out
+    return Prepared(prog, [k for k, _ in inputs], out_kind)([t for _, t in inputs], shape)

@@ -1,0 +1,162 @@
+"""The DS transform of torch programs on the GPU.
+
+Elementwise results equal, bit for bit, the C oracle composing the same DS
+operations (the pass's emitDsAdd / emitDsSub / emitDsMul chain,
+DsTransformPass.cpp:282-321, with emitFromFloat at entry and emitToFloat at
+the return).  Reductions and products equal the library's own targets
+called by hand on the same values (one code path), and their errors
+against exact sums stay within the DS bound.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_bits_equal
+from gpu_util import cu, host
+from oracle import exact
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tr():
+    from ds_b200 import transform
+    return transform
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from ds_b200 import ops as _ops
+    return _ops
+
+
+def test_config1_chain_bits(tr, dso):
+    """(a + b) * c on 2^20 f64 values (uniform [-1, 1], seed 0) is the
+    oracle's ds_fused_add_mul3_to_f64."""
+    rng = np.random.default_rng(0)
+    a, b, c = (rng.uniform(-1, 1, 1 << 20) for _ in range(3))
+    f = tr.ds_transform(lambda a, b, c: (a + b) * c)
+    assert f.plan(cu(a), cu(b), cu(c)).launches() == {"fused": 1}
+    got = host(f(cu(a), cu(b), cu(c)))
+    assert_bits_equal(got, dso.ds_fused_add_mul3_to_f64(a, b, c), "config 1")
+
+
+def test_mixed_program_bits(tr, dso):
+    rng = np.random.default_rng(1)
+    x = rng.uniform(-1, 1, (64, 257))
+    y = rng.uniform(-1, 1, 257).astype(np.float32)
+
+    @tr.ds_transform
+    def f(x, y):
+        z = (x + y) * x - 0.1
+        return z, -z * 3.0
+
+    z, w = f(cu(x), cu(y))
+    X, Y = dso.ds_from_f64(x), dso.ds_from_f32(np.broadcast_to(y, x.shape))
+    C = np.broadcast_to(dso.ds_from_f64(np.array(0.1)), x.shape + (2,))
+    Z = dso.ds_sub(dso.ds_mul(dso.ds_add(X, Y), X), C)
+    W = dso.ds_mul(-Z, np.broadcast_to(dso.ds_from_f64(np.array(3.0)), x.shape + (2,)))
+    assert_bits_equal(host(z), dso.ds_to_f64(Z), "z")
+    assert_bits_equal(host(w), dso.ds_to_f64(W), "w")
+
+
+def test_long_chain_bits(tr, dso):
+    """600 DS operations, cut into several programs, keep the bits."""
+    rng = np.random.default_rng(2)
+    x, a = rng.uniform(-1, 1, 4099), rng.uniform(0.999, 1.001, 4099)
+
+    @tr.ds_transform
+    def f(x, a):
+        for _ in range(300):
+            x = x * a + a
+        return x
+
+    assert f.plan(cu(x), cu(a)).launches()["fused"] >= 3
+    X, A = dso.ds_from_f64(x), dso.ds_from_f64(a)
+    for _ in range(300):
+        X = dso.ds_add(dso.ds_mul(X, A), A)
+    assert_bits_equal(host(f(cu(x), cu(a))), dso.ds_to_f64(X), "chain")
+
+
+def test_reduce_matches_target(tr, ops, dso):
+    rng = np.random.default_rng(3)
+    x = rng.uniform(-1, 1, (37, 3001)) * 1e8 + rng.uniform(0, 1, (37, 3001)) * 1e-3
+
+    @tr.ds_transform
+    def f(x):
+        return (x * x).sum(dim=1), x.sum()
+
+    s1, s = f(cu(x))
+    packed = ops.ds_mul(ops.ds_from_f64(cu(x)), ops.ds_from_f64(cu(x)))
+    hi, lo = ops.ds_reduce_packed(packed, dimensions=(1,))
+    want = host(hi).astype(np.float64) + host(lo).astype(np.float64)
+    assert_bits_equal(host(s1), want, "row sums")
+    flat = x.ravel()
+    truth = exact.exact_sum(flat)
+    h, l = dso.ds_reduce_f64_seq(flat)
+    ref_err = abs(float(h) + float(l) - truth)
+    bound = 2.0 ** -46 * np.abs(flat).max() * math.log2(flat.size) * 64
+    assert abs(float(host(s)) - truth) <= max(4 * ref_err, bound)
+
+
+def test_matmul_matches_target(tr, ops):
+    rng = np.random.default_rng(4)
+    A, B = rng.uniform(-1, 1, (256, 512)), rng.uniform(-1, 1, (512, 384))
+
+    @tr.ds_transform
+    def f(a, b):
+        return (a @ b) * 2.0, a @ b
+
+    scaled, p = f(cu(A), cu(B))
+    want = host(ops.ds_matmul_f64(cu(A), cu(B)))
+    assert_bits_equal(host(p), want, "product")
+    assert np.max(np.abs(host(p) - A @ B)) < 1e-12
+    # the product enters the multiply as its DS split: 2^-48 relative
+    assert np.all(np.abs(host(scaled) - 2 * want) <= 2.0 ** -46 * np.abs(want))
+
+
+def test_batched_and_vector_matmul(tr):
+    rng = np.random.default_rng(5)
+    f = tr.ds_transform(lambda a, b: a @ b)
+    for sa, sb in [((3, 64, 96), (3, 96, 32)), ((2, 64, 96), (96, 32)), ((96,), (96, 32)),
+                   ((64, 96), (96,))]:
+        a, b = rng.uniform(-1, 1, sa), rng.uniform(-1, 1, sb)
+        got = host(f(cu(a), cu(b)))
+        assert got.shape == np.matmul(a, b).shape
+        assert np.max(np.abs(got - np.matmul(a, b))) < 1e-12, (sa, sb)
+
+
+def test_layout_and_untouched_ops(tr, dso):
+    rng = np.random.default_rng(6)
+    a, b = rng.uniform(-1, 1, (48, 80)), rng.uniform(-1, 1, (80, 48))
+
+    @tr.ds_transform
+    def f(a, b):
+        y = a * b.T
+        return y.T + b, torch.exp(y)
+
+    g, e = f(cu(a), cu(b))
+    Y = dso.ds_mul(dso.ds_from_f64(a), dso.ds_from_f64(np.ascontiguousarray(b.T)))
+    YT = np.ascontiguousarray(Y.transpose(1, 0, 2))
+    assert_bits_equal(host(g), dso.ds_to_f64(dso.ds_add(YT, dso.ds_from_f64(b))), "layout")
+    assert np.allclose(host(e), np.exp(dso.ds_to_f64(Y)), rtol=1e-15, atol=0)
+
+
+def test_graph_capture(tr, dso):
+    """A transformed function replays inside a CUDA graph."""
+    rng = np.random.default_rng(7)
+    x, y = cu(rng.uniform(-1, 1, 100_000)), cu(rng.uniform(-1, 1, 100_000))
+    f = tr.ds_transform(lambda x, y: ((x + y) * y).sum())
+    eager = host(f(x, y))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        f(x, y)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = f(x, y)
+    g.replay()
+    assert_bits_equal(host(out), eager, "graph")
