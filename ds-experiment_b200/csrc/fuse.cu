@@ -131,6 +131,7 @@ struct Desc {
   int64_t dims[kMaxRank] = {};
   int64_t n = 1;
   bool pairs = false;  // all inputs full and 16-byte aligned, output too
+  int reduce_body = -1;  // DS_BODY_ADD / DS_BODY_MUL: a full reduction of the results
 };
 
 const char* ctype(int type) {
@@ -222,7 +223,15 @@ const char* pair_type(int type) {
   return type == DS_FUSED_F64 ? "double2" : (type == DS_FUSED_F32 ? "float2" : "float4");
 }
 
+// The kernel for program `d`.  A map writes every element's result to
+// `out`.  A reduction folds each thread's results with the body, in the
+// order it visits them, into a DS accumulator.  It then combines the
+// accumulators of a warp (shuffles) and of the block (shared memory), and
+// writes one (hi, lo) pair per block to `out`.
 std::string generate(const Desc& d) {
+  const bool reduce = d.reduce_body >= 0;
+  const std::string body = d.reduce_body == DS_BODY_MUL ? "mul" : "add";
+  const std::string ident = d.reduce_body == DS_BODY_MUL ? "ds2{1.0f, 0.0f}" : "ds2{0.0f, 0.0f}";
   std::string s;
   s += kDsArithSource;
   s += "\nusing namespace dsb;\n";
@@ -230,9 +239,10 @@ std::string generate(const Desc& d) {
   for (size_t k = 0; k < d.in.size(); ++k)
     s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
          ", ";
-  s += std::string(ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
+  s += std::string(reduce ? "float2" : ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
   s += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
   s += "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
+  if (reduce) s += "  ds2 acc = " + ident + ";\n";
   const std::string last = std::to_string(d.ops.size() - 1);
   // element i, one at a time
   auto scalar_loop = [&](const std::string& first) {
@@ -241,7 +251,10 @@ std::string generate(const Desc& d) {
       const InputView& in = d.in[k];
       return from_value(in.type, "__ldg(in" + std::to_string(k) + " + (" + index_expr(d, in) + "))");
     });
-    t += "    out[i] = " + to_value(d.out_type, "v" + last) + ";\n  }\n";
+    if (reduce)
+      t += "    acc = " + body + "(acc, v" + last + ");\n  }\n";
+    else
+      t += "    out[i] = " + to_value(d.out_type, "v" + last) + ";\n  }\n";
     return t;
   };
   if (d.pairs) {
@@ -264,7 +277,9 @@ std::string generate(const Desc& d) {
       });
     }
     const std::string r0 = "v" + last + "_0", r1 = "v" + last + "_1";
-    if (d.out_type == DS_FUSED_F64)
+    if (reduce)
+      s += "    acc = " + body + "(" + body + "(acc, " + r0 + "), " + r1 + ");\n";
+    else if (d.out_type == DS_FUSED_F64)
       s += "    __stcs(reinterpret_cast<double2*>(out) + p, make_double2(to_f64(" + r0 +
            "), to_f64(" + r1 + ")));\n";
     else if (d.out_type == DS_FUSED_F32)
@@ -277,6 +292,25 @@ std::string generate(const Desc& d) {
     s += scalar_loop("2 * npairs + tid");  // the odd last element
   } else {
     s += scalar_loop("tid");
+  }
+  if (reduce) {
+    // warp, then block: 8 warp totals through shared memory to warp 0
+    s += "  for (int o = 16; o > 0; o >>= 1) {\n";
+    s += "    const ds2 t = ds2{__shfl_xor_sync(0xffffffffu, acc.hi, o), "
+         "__shfl_xor_sync(0xffffffffu, acc.lo, o)};\n";
+    s += "    acc = " + body + "(acc, t);\n  }\n";
+    s += "  __shared__ float2 part[8];\n";
+    s += "  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = make_float2(acc.hi, acc.lo);\n";
+    s += "  __syncthreads();\n";
+    s += "  if (threadIdx.x < 32) {\n";
+    s += "    acc = threadIdx.x < 8 ? ds2{part[threadIdx.x].x, part[threadIdx.x].y} : " + ident +
+         ";\n";
+    s += "    for (int o = 4; o > 0; o >>= 1) {\n";
+    s += "      const ds2 t = ds2{__shfl_xor_sync(0xffffffffu, acc.hi, o), "
+         "__shfl_xor_sync(0xffffffffu, acc.lo, o)};\n";
+    s += "      acc = " + body + "(acc, t);\n    }\n";
+    s += "    if (threadIdx.x == 0) out[blockIdx.x] = make_float2(acc.hi, acc.lo);\n";
+    s += "  }\n";
   }
   s += "}\n";
   return s;
@@ -422,6 +456,27 @@ int compile(const std::string& src, CUfunction* fn) {
   return DS_OK;
 }
 
+// Compile without loading (no GPU needed): the NVRTC log on failure.
+int nvrtc_check(const std::string& src) {
+  const Nvrtc& nv = nvrtc();
+  if (!nv.error.empty()) return set_error(DS_INTERNAL, "ds_fused: " + nv.error);
+  nvrtcProgram_t prog = nullptr;
+  if (nv.create(&prog, src.c_str(), "ds_fused.cu", 0, nullptr, nullptr) != 0)
+    return set_error(DS_INTERNAL, "ds_fused: nvrtcCreateProgram failed");
+  const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-std=c++17", "-default-device"};
+  const int rc = nv.compile(prog, 4, opts);
+  std::string log;
+  if (rc != 0) {
+    size_t n = 0;
+    nv.log_size(prog, &n);
+    log.assign(n, '\0');
+    if (n) nv.log(prog, &log[0]);
+  }
+  nv.destroy(&prog);
+  if (rc != 0) return set_error(DS_INTERNAL, "ds_fused: NVRTC compilation failed: " + log);
+  return ok();
+}
+
 }  // namespace
 }  // namespace dsb
 
@@ -449,24 +504,7 @@ int ds_fused_compile_check(const ds_fused_op* ops, int32_t n_ops, const int32_t*
                            const ds_buffer* out) {
   Desc d;
   if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, out_type, out, d)) return st;
-  const Nvrtc& nv = nvrtc();
-  if (!nv.error.empty()) return set_error(DS_INTERNAL, "ds_fused: " + nv.error);
-  const std::string src = generate(d);
-  nvrtcProgram_t prog = nullptr;
-  if (nv.create(&prog, src.c_str(), "ds_fused.cu", 0, nullptr, nullptr) != 0)
-    return set_error(DS_INTERNAL, "ds_fused: nvrtcCreateProgram failed");
-  const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-std=c++17", "-default-device"};
-  const int rc = nv.compile(prog, 4, opts);
-  std::string log;
-  if (rc != 0) {
-    size_t n = 0;
-    nv.log_size(prog, &n);
-    log.assign(n, '\0');
-    if (n) nv.log(prog, &log[0]);
-  }
-  nv.destroy(&prog);
-  if (rc != 0) return set_error(DS_INTERNAL, "ds_fused: NVRTC compilation failed: " + log);
-  return ok();
+  return nvrtc_check(generate(d));
 }
 
 int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
@@ -493,6 +531,94 @@ int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_typ
                       nullptr) != CUDA_SUCCESS)
     return set_error(DS_INTERNAL, "ds_fused: cuLaunchKernel failed");
   return ok();
+}
+
+// A fused program reduced to one DS value: stage 1 is the generated kernel
+// with its reduction sink (one partial pair per block into the workspace),
+// stage 2 the library's packed reduce over those partials with the init.
+static int64_t fused_reduce_max_blocks() { return static_cast<int64_t>(sm_count()) * 8; }
+
+static size_t fused_reduce_partial_bytes() {
+  return static_cast<size_t>((fused_reduce_max_blocks() * 8 + 255) / 256 * 256);
+}
+
+size_t ds_fused_reduce_workspace_size(const int64_t* dims, int32_t rank) {
+  if (rank < 0 || rank > kMaxRank || (rank > 0 && dims == nullptr)) return 0;
+  const int64_t blocks = fused_reduce_max_blocks();
+  const int64_t pdims[1] = {blocks};
+  alignas(16) static char stand_in[16];
+  const ds_buffer logical{stand_in, pdims, 1};
+  const int64_t dim0 = 0;
+  return fused_reduce_partial_bytes() + ds_reduce_workspace_size(&logical, &dim0, 1) + 256;
+}
+
+int ds_fused_reduce(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                    const ds_buffer* const* inputs, int32_t n_inputs, const int64_t* dims,
+                    int32_t rank, int32_t body, const ds_buffer* init_hi,
+                    const ds_buffer* init_lo, const ds_buffer* out_hi, const ds_buffer* out_lo,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (body != DS_BODY_ADD && body != DS_BODY_MUL)
+    return invalid("ds_fused_reduce: the body is DS_BODY_ADD or DS_BODY_MUL");
+  if (rank < 0 || rank > kMaxRank || (rank > 0 && dims == nullptr))
+    return invalid("ds_fused_reduce: at most 8 dimensions");
+  if (!init_hi || !init_lo || !out_hi || !out_lo || !init_hi->data || !init_lo->data ||
+      !out_hi->data || !out_lo->data)
+    return invalid("ds_fused_reduce: null init or output buffer");
+  const size_t need = ds_fused_reduce_workspace_size(dims, rank);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256))
+    return invalid("ds_fused_reduce: workspace too small or not 256-byte aligned (need " +
+                   std::to_string(need) + " bytes)");
+  // the map's logical shape, written by no one: the partials stand in for
+  // its data pointer (16-byte aligned, so the pair path is decided by the inputs)
+  const ds_buffer shape{workspace, dims, rank};
+  Desc d;
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, DS_FUSED_F64, &shape, d))
+    return st;
+  d.reduce_body = body;
+  float2* partials = static_cast<float2*>(workspace);
+  unsigned grid = 0;
+  if (d.n > 0) {
+    CUfunction fn = nullptr;
+    if (int st = compile(generate(d), &fn)) return st;
+    std::vector<void*> ptrs(n_inputs + 1);
+    std::vector<void*> args(n_inputs + 2);
+    for (int32_t k = 0; k < n_inputs; ++k) {
+      ptrs[k] = inputs[k]->data;
+      args[k] = &ptrs[k];
+    }
+    ptrs[n_inputs] = partials;
+    args[n_inputs] = &ptrs[n_inputs];
+    long long n = d.n;
+    args[n_inputs + 1] = &n;
+    grid = grid_for(d.pairs ? (d.n + 1) / 2 : d.n, 256, 8);
+    ProfileScope prof("fused_reduce", static_cast<cudaStream_t>(stream));
+    if (driver().launch(fn, grid, 1, 1, 256, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
+                        nullptr) != CUDA_SUCCESS)
+      return set_error(DS_INTERNAL, "ds_fused_reduce: cuLaunchKernel failed");
+  }
+  const int64_t pdims[2] = {static_cast<int64_t>(grid), 2};
+  const ds_buffer pbuf{partials, pdims, 2};
+  const int64_t dim0 = 0;
+  const size_t off = fused_reduce_partial_bytes();
+  return ds_reduce_packed(&pbuf, init_hi, init_lo, &dim0, 1, body, out_hi, out_lo,
+                          static_cast<char*>(workspace) + off, workspace_bytes - off, stream);
+}
+
+int ds_fused_reduce_compile_check(const ds_fused_op* ops, int32_t n_ops,
+                                  const int32_t* input_types, const ds_buffer* const* inputs,
+                                  int32_t n_inputs, const int64_t* dims, int32_t rank,
+                                  int32_t body) {
+  if (body != DS_BODY_ADD && body != DS_BODY_MUL)
+    return invalid("ds_fused_reduce: the body is DS_BODY_ADD or DS_BODY_MUL");
+  if (rank < 0 || rank > kMaxRank || (rank > 0 && dims == nullptr))
+    return invalid("ds_fused_reduce: at most 8 dimensions");
+  alignas(16) static char stand_in[16];
+  const ds_buffer shape{stand_in, dims, rank};
+  Desc d;
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, DS_FUSED_F64, &shape, d))
+    return st;
+  d.reduce_body = body;
+  return nvrtc_check(generate(d));
 }
 
 }  // extern "C"

@@ -164,7 +164,13 @@ class DSTensor:
     # ---- reduce and contraction ---------------------------------------------
 
     def sum(self, dimensions=None) -> "DSTensor":
-        """DS sum over `dimensions` (default: all), the result kept as DS."""
+        """DS sum over `dimensions` (default: all), the result kept as DS.
+        A pending expression summed over all its dimensions runs as one
+        kernel that never stores its values (ds_fused_reduce)."""
+        if self._packed is None and dimensions is None and len(self._shape) > 0:
+            prepared, tensors = _prepare(self._expr, self._leaves, "packed")
+            hi, lo = prepared.reduce(tensors, self._shape, "add")
+            return DSTensor(torch.stack([hi, lo], dim=-1))
         p = self.packed
         dims = None if dimensions is None else tuple(dimensions)
         hi, lo = ops.ds_reduce_packed(p, dimensions=dims)
@@ -206,6 +212,18 @@ def _force(operand, device):
 
 def _run(expr, leaves, shape, device, out_kind) -> torch.Tensor:
     """Emit the expression as a fused program over its leaves and run it."""
+    prog, inputs = _emit(expr, leaves)
+    return fuse.run_program(prog, inputs, out_kind, shape)
+
+
+def _prepare(expr, leaves, out_kind):
+    prog, inputs = _emit(expr, leaves)
+    return fuse.Prepared(prog, [k for k, _ in inputs], out_kind), [t for _, t in inputs]
+
+
+def _emit(expr, leaves):
+    """The expression as an operation list over its distinct leaves:
+    (ops, [(kind, tensor)])."""
     prog: List[Tuple[int, int, int, float]] = []
     inputs: List[Tuple[str, torch.Tensor]] = []
     input_of: Dict[int, int] = {}
@@ -238,4 +256,4 @@ def _run(expr, leaves, shape, device, out_kind) -> torch.Tensor:
     emit(expr)
     if not inputs:
         raise ValueError("a DSTensor expression needs at least one tensor")
-    return fuse.run_program(prog, inputs, out_kind, shape)
+    return prog, inputs

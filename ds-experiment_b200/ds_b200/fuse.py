@@ -325,6 +325,66 @@ class Prepared:
         return out
 
 
+    def _reduce_args(self, tensors, shape, body):
+        if body not in _BODY:
+            raise ValueError("a fused reduction's body is 'add' or 'mul'")
+        shape = tuple(int(d) for d in shape)
+        dims = (ctypes.c_int64 * max(len(shape), 1))(*shape)
+        bufs, keep = _buffers(tensors)
+        arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
+            *[ctypes.pointer(b) for b in bufs])
+        return shape, dims, bufs, keep, arr
+
+    def reduce(self, tensors: Sequence[torch.Tensor], shape, body: str = "add",
+               init=(0.0, 0.0)) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The program over the logical `shape`, its results combined with
+        `body` ("add" or "mul") and the init pair, in one pass over the
+        inputs (ds_fused_reduce): (hi, lo) as 0-d f32 tensors."""
+        from . import ops  # the init scalars' cache
+        if len(tensors) != len(self.kinds) or not tensors:
+            raise ValueError(f"the program takes {len(self.kinds)} input tensors")
+        tensors = [t.contiguous() for t in tensors]
+        device = tensors[0].device
+        for t in tensors:
+            if not t.is_cuda or t.device != device:
+                raise ValueError("fused inputs must be CUDA tensors on one device")
+        shape, dims, bufs, keep, arr = self._reduce_args(tensors, shape, body)
+        L = _lib.lib()
+        with torch.cuda.device(device):
+            ws_bytes = int(L.ds_fused_reduce_workspace_size(dims, len(shape)))
+            ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
+            ih = ops._scalar(init[0], torch.float32, device)
+            il = ops._scalar(init[1], torch.float32, device)
+            hi = torch.empty((), dtype=torch.float32, device=device)
+            lo = torch.empty((), dtype=torch.float32, device=device)
+            scal = [_lib.make_buffer(t.data_ptr(), ()) for t in (ih, il, hi, lo)]
+            stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            st = L.ds_fused_reduce(self._comp.ops, self._comp.n_ops, self._types, arr, len(bufs),
+                                   dims, len(shape), _BODY[body],
+                                   *[ctypes.byref(b) for b, _ in scal],
+                                   ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream)
+        _lib.check(st, "ds_fused_reduce")
+        return hi, lo
+
+    def reduce_compile_check(self, shapes: Sequence[tuple], shape, body: str = "add") -> None:
+        """Generate and compile the reduction kernel for inputs of these
+        shapes (no GPU needed; raises on a compilation error)."""
+        shape, dims, _, _, _ = self._reduce_args([], shape, body)
+        bufs, keep = [], []
+        for s in shapes:
+            b, d = _lib.make_buffer(256, tuple(s))
+            bufs.append(b)
+            keep.append(d)
+        arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
+            *[ctypes.pointer(b) for b in bufs])
+        _lib.check(_lib.lib().ds_fused_reduce_compile_check(
+            self._comp.ops, self._comp.n_ops, self._types, arr, len(bufs), dims, len(shape),
+            _BODY[body]), "compile")
+
+
+_BODY = {"add": _lib.DS_BODY_ADD, "mul": _lib.DS_BODY_MUL}
+
+
 def run_program(prog, inputs, out_kind: str, shape) -> torch.Tensor:
     """Run an operation list directly: `prog` holds (code, a, b, value)
     tuples in SSA order, `inputs` (kind, tensor) pairs with kind "f64",

@@ -18,7 +18,8 @@ interception), and it is lowered onto this library's targets by the same rules:
 - a connected elementwise DAG of add / sub / mul / neg becomes ONE
   generated kernel (ds_fused_run), where the pass emits a chain of f32 ops;
 - `sum` / `prod` over DS values become ds_reduce_packed (ds_reduce_from_f64
-  for an f64 argument, which splits as it loads);
+  for an f64 argument, which splits as it loads); a full reduction of an
+  elementwise DAG runs in the DAG's own kernel (ds_fused_reduce);
 - `matmul` / `mm` / `bmm` / `@` become ds_dot_general_f64 (tensor cores);
 - layout operations (reshape, view, unsqueeze, squeeze, expand, transpose,
   permute, t, T, mT, flatten, contiguous) act on hi and lo alike, as the
@@ -186,6 +187,24 @@ class _ReduceStep:
                 x = x.reshape(1)
             hi, lo = ops.ds_reduce_from_f64(x.contiguous(), init=self.init, dimensions=self.dims,
                                             body=self.body)
+        env[self.out] = torch.stack([hi, lo], dim=-1).reshape(self.shape + (2,))
+
+
+class _FusedReduceStep:
+    """A pending elementwise value reduced over all its dimensions in the
+    same kernel (ds_fused_reduce): its values are never written."""
+
+    def __init__(self, out, prog, inputs, kinds, map_shape, body, init, shape):
+        self.out, self.inputs = out, list(inputs)
+        self.map_shape, self.body, self.init, self.shape = tuple(map_shape), body, init, tuple(shape)
+        self.prepared = fuse.Prepared(prog, kinds, "packed")
+        names = ", ".join(f"%{s}:{k}" for s, k in zip(inputs, kinds))
+        self.text = (f"%{out} = ds_fused_reduce[{len(prog)} ops]({names}) over "
+                     f"{list(self.map_shape)}, body={body}, init={init} -> packed {list(self.shape)}")
+
+    def run(self, env):
+        hi, lo = self.prepared.reduce([env[s] for s in self.inputs], self.map_shape, self.body,
+                                      (self.init, 0.0))
         env[self.out] = torch.stack([hi, lo], dim=-1).reshape(self.shape + (2,))
 
 
@@ -672,6 +691,15 @@ class _Lowering:
     def _emit_reduce(self, node: fx.Node, cls):
         _, src, dims, keepdim, body, init = cls
         st = self.state[src]
+        rank = len(self._shape(src))
+        if isinstance(st, _Pending) and rank > 0 and tuple(dims) == tuple(range(rank)):
+            # a full reduction of an elementwise DAG: one kernel, no stores
+            prog, slots, kinds = self._program(src)
+            out = self.slot(node.name)
+            self.steps.append(_FusedReduceStep(out, prog, slots, kinds, self._shape(src), body,
+                                               init, self._shape(node)))
+            self.state[node] = _Leaf(out, "packed", False)
+            return
         if isinstance(st, _Leaf) and st.kind == "f64":
             slot, kind = st.slot, "f64"
         else:

@@ -345,6 +345,30 @@ DS_API int ds_fused_compile_check(const ds_fused_op* ops, int32_t n_ops,
                                   const int32_t* input_types, const ds_buffer* const* inputs,
                                   int32_t n_inputs, int32_t out_type, const ds_buffer* out);
 
+/* A fused program reduced to one DS value: the program of ds_fused_run
+   evaluated over every element of the logical shape `dims` (its inputs
+   broadcast to it), and the results combined with `body` (DS_BODY_ADD or
+   DS_BODY_MUL) and the init pair (0-d f32 device buffers, as ds_reduce).
+   The result (out_hi, out_lo) is 0-d f32.  This is the pass's reduce
+   (DsTransformPass.cpp:376-448) of an elementwise DAG (:282-321) without
+   writing the DAG's values to memory.  Each thread folds the elements it
+   visits; warp and block trees follow, and ds_reduce_packed combines the
+   per-block partials with the init.  The order is fixed for a given size,
+   so results are deterministic.  The workspace is 256-byte aligned and
+   ds_fused_reduce_workspace_size bytes. */
+DS_API size_t ds_fused_reduce_workspace_size(const int64_t* dims, int32_t rank);
+DS_API int ds_fused_reduce(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                           const ds_buffer* const* inputs, int32_t n_inputs,
+                           const int64_t* dims, int32_t rank, int32_t body,
+                           const ds_buffer* init_hi, const ds_buffer* init_lo,
+                           const ds_buffer* out_hi, const ds_buffer* out_lo,
+                           void* workspace, size_t workspace_bytes, void* stream);
+/* Generate and compile (NVRTC) the reduction kernel without running it. */
+DS_API int ds_fused_reduce_compile_check(const ds_fused_op* ops, int32_t n_ops,
+                                         const int32_t* input_types,
+                                         const ds_buffer* const* inputs, int32_t n_inputs,
+                                         const int64_t* dims, int32_t rank, int32_t body);
+
 /* ---- diagnostics (no reference counterpart) ------------------------------ */
 
 /* Per-kernel GPU time.  While enabled, each op brackets its main kernel with

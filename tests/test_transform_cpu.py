@@ -5,7 +5,7 @@ layout steps or stay torch operations, and where values are recombined)
 runs here on CPU tensors with the library's launches replaced by the C
 oracle: fused programs are evaluated operation by operation with the
 oracle's ds_add / ds_sub / ds_mul (cpp/ds_add.cpp, ds_sub.cpp, ds_mul.cpp
-restated), reductions with its sequential DS fold.  The results must equal,
+restated), reductions (fused or not) with its sequential DS fold.  The results must equal,
 bit for bit, the same DS operations composed by hand, which is what the
 reference's pass emits for the program (DsTransformPass.cpp:211-461).
 """
@@ -74,7 +74,13 @@ def oracle_backend(monkeypatch, dso):
     def dot_f64(a, b, lhs_batch=(), rhs_batch=(), **kw):
         return torch.matmul(a, b)
 
+    def reduce_prepared(self, tensors, shape, body="add", init=(0.0, 0.0)):
+        flat = run_prepared(self, tensors, shape).numpy().reshape(-1, 2)
+        h, l = dso.ds_reduce_ds_seq(flat[:, 0], flat[:, 1], body, init)
+        return torch.tensor(h), torch.tensor(l)
+
     monkeypatch.setattr(fuse.Prepared, "__call__", run_prepared)
+    monkeypatch.setattr(fuse.Prepared, "reduce", reduce_prepared)
     monkeypatch.setattr(ops, "ds_reduce_packed", reduce_packed)
     monkeypatch.setattr(ops, "ds_reduce_from_f64", reduce_from_f64)
     monkeypatch.setattr(ops, "ds_dot_general_f64", dot_f64)
@@ -370,3 +376,36 @@ def test_integer_and_comparison_operations_stay_torch(oracle_backend):
     got, k = f(x, n)
     assert torch.equal(k, n * 2)
     assert got.dtype == torch.float64 and got.shape == (7,)
+
+
+def test_full_reduction_of_a_dag_is_one_kernel(oracle_backend):
+    dso = oracle_backend
+
+    @tr.ds_transform
+    def f(a, b, c):
+        return ((a + b) * c).sum(), (a * b).sum(dim=0)
+
+    a, b, c = rand((40, 3), 21), rand((40, 3), 22), rand((3,), 23)
+    plan = f.plan(a, b, c)
+    kinds = [type(st).__name__ for st in plan.steps]
+    assert kinds.count("_FusedReduceStep") == 1      # the full sum, no packed store
+    assert kinds.count("_ReduceStep") == 1           # the partial one reads a packed value
+    assert "ds_fused_reduce" in f.explain(a, b, c)
+    s, p = f(a, b, c)
+    Z = dso.ds_mul(dso.ds_add(P(dso, a), P(dso, b)), P(dso, c.expand(40, 3).contiguous()))
+    h, l = dso.ds_reduce_ds_seq(Z[..., 0].ravel(), Z[..., 1].ravel())
+    assert_bits_equal(s.numpy(), dso.ds_to_f64(np.array([h, l], np.float32)), "fused sum")
+
+
+def test_reduce_kernels_compile():
+    """The generated reduction kernels compile with NVRTC for sm_100a."""
+    I, Cn, A, M = (_lib.DS_FUSED_INPUT, _lib.DS_FUSED_CONST, _lib.DS_FUSED_ADD,
+                   _lib.DS_FUSED_MUL)
+    p = fuse.Prepared([(I, 0, 0, 0.0), (I, 1, 0, 0.0), (A, 0, 1, 0.0), (I, 2, 0, 0.0),
+                       (M, 2, 3, 0.0)], ["f64", "f64", "f32"], "packed")
+    p.reduce_compile_check([(1000,), (1000,), (1000,)], (1000,), "add")
+    p.reduce_compile_check([(10, 1), (1, 7), (7,)], (10, 7), "mul")
+    q = fuse.Prepared([(I, 0, 0, 0.0), (Cn, 0, 0, 0.5), (M, 0, 1, 0.0)], ["packed"], "packed")
+    q.reduce_compile_check([(33, 2)], (33,), "add")
+    with pytest.raises(ValueError):
+        q.reduce_compile_check([(33, 2)], (33,), "sub")
