@@ -561,6 +561,18 @@ def run_stream(args):
                 "GB/s": round(world * bpe * n / (fms * 1e-3) / 1e9, 1), "ms_per_step": round(fms, 4),
                 "bit_exact_vs_hand_written": bool(torch.equal(fout.view(torch.int64),
                                                               out.view(torch.int64)))}
+            # sum((a + b) * c): the chain reduced in its own kernel, no stores
+            # (24 B read per element), against the chain's packed values
+            # written and then read by the packed reduce (8 + 8 B more)
+            red = fuse.Prepared([(0, 0, 0, 0.0), (0, 1, 0, 0.0), (2, 0, 1, 0.0), (0, 2, 0, 0.0),
+                                 (4, 2, 3, 0.0)], ["f64"] * 3, "packed")
+            rms, _ = timed(lambda: red.reduce([a, b, c], (n,)), args.steps)
+            two = fuse.jit(lambda a_, b_, c_: (a_ + b_) * c_, out_dtype="packed")
+            tms, _ = timed(lambda: ops.ds_reduce_packed(two(a, b, c)), args.steps)
+            line["fused_map_reduce"] = {
+                "what": "sum((a + b) * c) per rank, one kernel (ds_fused_reduce)",
+                "GB/s": round(world * 24.0 * n / (rms * 1e-3) / 1e9, 1),
+                "ms_per_step": round(rms, 4), "unfused_ms_per_step": round(tms, 4)}
         k_ms, k_n = _lib.profile_read(fam)
         # device time of the family per step: at N > 1 the reduce family
         # also holds the tiny combine of the gathered pairs
