@@ -816,6 +816,8 @@ class DsFunction:
         key = _signature_key(args)
         p = self._plans.get(key)
         if p is None:
+            if len(self._plans) >= _MAX_PLANS:
+                self._plans.clear()  # many baked-in values: start over
             p = self._plans[key] = self._build(args)
         return p
 
@@ -831,6 +833,7 @@ class DsFunction:
                 raise TypeError(f"{self.__name__} needs argument {q.name!r}")
             concrete[q.name] = q.default
         gm = fx.symbolic_trace(self.fn, concrete_args=concrete or None)
+        _expand_linear(gm)
         full = list(args) + [concrete[q.name] for q in params[len(args):]]
         _propagate_shapes(gm, full)
         inputs, steps, output, consts = _Lowering(gm, full).lower()
@@ -848,10 +851,50 @@ class DsFunction:
         return self.plan(*args).explain()
 
 
+_MAX_PLANS = 64
+
+
+def _expand_linear(gm: fx.GraphModule) -> None:
+    """nn.Linear modules and F.linear calls as the operations they are,
+    x @ W.T (+ b), which is how a dense layer reaches the pass: a
+    dot_general and an add (DsTransformPass.cpp:282-370)."""
+    g = gm.graph
+    for node in list(g.nodes):
+        if node.op == "call_module" and isinstance(gm.get_submodule(node.target), torch.nn.Linear):
+            mod = gm.get_submodule(node.target)
+            x = node.args[0] if node.args else node.kwargs.get("input")
+            with g.inserting_before(node):
+                w = g.get_attr(f"{node.target}.weight")
+                b = g.get_attr(f"{node.target}.bias") if mod.bias is not None else None
+        elif node.op == "call_function" and node.target is torch.nn.functional.linear:
+            args = list(node.args) + [None] * (3 - len(node.args))
+            x = args[0] if args[0] is not None else node.kwargs.get("input")
+            w = args[1] if args[1] is not None else node.kwargs.get("weight")
+            b = args[2] if args[2] is not None else node.kwargs.get("bias")
+        else:
+            continue
+        with g.inserting_before(node):
+            wt = g.call_function(getattr, (w, "T"))
+            y = g.call_function(operator.matmul, (x, wt))
+            if b is not None:
+                y = g.call_function(operator.add, (y, b))
+        node.replace_all_uses_with(y)
+        g.erase_node(node)
+    g.lint()
+    gm.recompile()
+
+
 def _propagate_shapes(gm: fx.GraphModule, args):
-    """dtype and shape of every node: on meta tensors when every operation
-    supports them, else by running the captured program once as it is."""
+    """dtype and shape of every node, without running the program: with fake
+    tensors (module parameters and constants included), else on meta
+    tensors; a program that supports neither runs once as it is."""
     from torch.fx.passes.shape_prop import ShapeProp
+    try:
+        from torch._subclasses.fake_tensor import FakeTensorMode
+        ShapeProp(gm, fake_mode=FakeTensorMode(allow_non_fake_inputs=True)).propagate(*args)
+        return
+    except Exception:
+        pass
     meta = [torch.empty_strided(a.shape, a.stride(), dtype=a.dtype, device="meta")
             if isinstance(a, torch.Tensor) else a for a in args]
     try:

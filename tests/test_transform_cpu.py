@@ -30,7 +30,7 @@ def oracle_backend(monkeypatch, dso):
         vals = []
         for code, a, b, v in self.ops:
             if code == _lib.DS_FUSED_INPUT:
-                t, k = tensors[a].numpy(), self.kinds[a]
+                t, k = tensors[a].detach().numpy(), self.kinds[a]
                 p = dso.ds_from_f64(t) if k == "f64" else (dso.ds_from_f32(t) if k == "f32" else t)
                 vals.append(full(p))
             elif code == _lib.DS_FUSED_CONST:
@@ -53,7 +53,7 @@ def oracle_backend(monkeypatch, dso):
         return moved.reshape((int(np.prod(out_shape)), -1) + x.shape[rank:]), out_shape
 
     def reduce_packed(x, init=(0.0, 0.0), dimensions=None, body="add"):
-        p = x.numpy()
+        p = x.detach().numpy()
         rank = p.ndim - 1
         dims = tuple(range(rank)) if dimensions is None else tuple(dimensions)
         r, shape = rows(p, dims, rank)
@@ -63,7 +63,7 @@ def oracle_backend(monkeypatch, dso):
         return torch.from_numpy(hi), torch.from_numpy(lo)
 
     def reduce_from_f64(x, init=0.0, dimensions=None, body="add"):
-        p = x.numpy()
+        p = x.detach().numpy()
         dims = tuple(range(p.ndim)) if dimensions is None else tuple(dimensions)
         r, shape = rows(p, dims, p.ndim)
         res = [dso.ds_reduce_f64_seq(q, body, (init, 0.0)) for q in r]
@@ -72,7 +72,8 @@ def oracle_backend(monkeypatch, dso):
         return torch.from_numpy(hi), torch.from_numpy(lo)
 
     def dot_f64(a, b, lhs_batch=(), rhs_batch=(), **kw):
-        return torch.matmul(a, b)
+        with torch.no_grad():
+            return torch.matmul(a, b)
 
     def reduce_prepared(self, tensors, shape, body="add", init=(0.0, 0.0)):
         flat = run_prepared(self, tensors, shape).numpy().reshape(-1, 2)
@@ -409,3 +410,32 @@ def test_reduce_kernels_compile():
     q.reduce_compile_check([(33, 2)], (33,), "add")
     with pytest.raises(ValueError):
         q.reduce_compile_check([(33, 2)], (33,), "sub")
+
+
+def test_linear_layers_lower_to_product_and_add(oracle_backend):
+    """nn.Linear and F.linear become x @ W.T + b: a product, then a DS add."""
+    dso = oracle_backend
+
+    class Net(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = torch.nn.Linear(6, 4).double()
+            self.w2 = torch.nn.Parameter(rand((3, 4), 24), requires_grad=False)
+
+        def forward(self, x):
+            h = self.fc(x) * 2.0
+            return torch.nn.functional.linear(h, self.w2)
+
+    torch.manual_seed(0)
+    net = Net()
+    f = tr.ds_transform(net)
+    x = rand((5, 6), 25)
+    counts = f.plan(x).launches()
+    assert counts.get("dot") == 2 and "plain" not in counts
+    got = f(x)
+    with torch.no_grad():
+        h = (x @ net.fc.weight.T)
+        H = dso.ds_mul(dso.ds_add(P(dso, h), P(dso, net.fc.bias.expand(5, 4).contiguous())),
+                       C(dso, 2.0, (5, 4)))
+        want = torch.from_numpy(dso.ds_to_f64(H)) @ net.w2.T
+    assert torch.allclose(got, want, rtol=1e-12, atol=1e-12)

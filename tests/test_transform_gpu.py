@@ -160,3 +160,19 @@ def test_graph_capture(tr, dso):
         out = f(x, y)
     g.replay()
     assert_bits_equal(host(out), eager, "graph")
+
+
+def test_linear_module(tr, ops, dso):
+    """nn.Linear lowers to the DS product then a DS add of the bias: the add
+    is the oracle's on the product's values, bit for bit."""
+    torch.manual_seed(1)
+    lin = torch.nn.Linear(96, 64).double().cuda()
+    f = tr.ds_transform(lin)
+    x = cu(np.random.default_rng(8).uniform(-1, 1, (128, 96)))
+    got = host(f(x))
+    with torch.no_grad():
+        prod = host(ops.ds_matmul_f64(x, lin.weight.T.contiguous()))
+        bias = host(lin.bias)
+    want = dso.ds_to_f64(dso.ds_add(dso.ds_from_f64(prod),
+                                    dso.ds_from_f64(np.broadcast_to(bias, prod.shape))))
+    assert_bits_equal(got, want, "linear")
