@@ -176,3 +176,26 @@ def test_linear_module(tr, ops, dso):
     want = dso.ds_to_f64(dso.ds_add(dso.ds_from_f64(prod),
                                     dso.ds_from_f64(np.broadcast_to(bias, prod.shape))))
     assert_bits_equal(got, want, "linear")
+
+
+def test_edge_shapes(tr, dso):
+    """0-d and empty tensors, keepdim on a fused full reduction, f32 programs."""
+    f = tr.ds_transform(lambda x, y: ((x * y + 1.0).sum(dim=(0, 1), keepdim=True), x * y - y))
+    x = np.random.default_rng(9).uniform(-1, 1, (5, 7))
+    s, d = f(cu(x), cu(x))
+    assert tuple(s.shape) == (1, 1) and tuple(d.shape) == (5, 7)
+    X = dso.ds_from_f64(x)
+    assert_bits_equal(host(d), dso.ds_to_f64(dso.ds_sub(dso.ds_mul(X, X), X)), "map")
+    e, _ = f(torch.zeros(0, 7, dtype=torch.float64, device="cuda"),
+             torch.zeros(0, 7, dtype=torch.float64, device="cuda"))
+    assert float(host(e).item()) == 0.0
+    g = tr.ds_transform(lambda a, b: a * b + 0.5)
+    a0 = torch.tensor(3.0, dtype=torch.float64, device="cuda")
+    assert float(host(g(a0, a0))) == 9.5
+    h = tr.ds_transform(lambda a, b: (a + b) * a)
+    u = np.random.default_rng(10).uniform(-1, 1, 1001).astype(np.float32)
+    v = np.random.default_rng(11).uniform(-1, 1, 1001).astype(np.float32)
+    got = host(h(cu(u), cu(v)))
+    U, V = dso.ds_from_f32(u), dso.ds_from_f32(v)
+    assert got.dtype == np.float32
+    assert_bits_equal(got, dso.ds_to_f32(dso.ds_mul(dso.ds_add(U, V), U)), "f32 program")
