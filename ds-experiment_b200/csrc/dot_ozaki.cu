@@ -305,6 +305,36 @@ __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* bas
   }
 }
 
+// The integer-path residue with the modulus picked at run time: the same
+// arithmetic as residue<l, false>, its constants read from the constant
+// bank by index (m = 256 works too: its weights select byte 0 and its
+// magic is 0).  A loop over the moduli built from it is a fourteenth of the
+// unrolled code, which keeps the column split's instruction stream in cache.
+__constant__ uint32_t c_mod_rt[kL] = {mod_of(0), mod_of(1), mod_of(2),  mod_of(3),  mod_of(4),
+                                      mod_of(5), mod_of(6), mod_of(7),  mod_of(8),  mod_of(9),
+                                      mod_of(10), mod_of(11), mod_of(12), mod_of(13)};
+
+__device__ __forceinline__ uint32_t residue_rt(const Limbs& x, int l) {
+  const SplitConsts c = c_split[l];
+  const uint32_t s = __dp4a(x.lo, c.w_lo, __dp4a(x.hi, c.w_hi, c.unbias));
+  return s - __umulhi(s, c.magic) * c_mod_rt[l];
+}
+
+// Residues of 16 consecutive values -> one 16-byte store per modulus plane,
+// the moduli looped at run time.
+__device__ __forceinline__ void store_planes_16_rt(const Limbs (&x)[16], uint8_t* base,
+                                                   size_t plane_stride) {
+#pragma unroll 1
+  for (int l = 0; l < kL; ++l) {
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      w[q] = pack4(residue_rt(x[q * 4], l), residue_rt(x[q * 4 + 1], l),
+                   residue_rt(x[q * 4 + 2], l), residue_rt(x[q * 4 + 3], l));
+    *reinterpret_cast<uint4*>(base + l * plane_stride) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 __device__ __forceinline__ int shift_for(double mx, bool nonfinite, int P) {
   if (nonfinite) return kShiftNonFinite;
   if (mx == 0.0) return 0;
@@ -324,12 +354,12 @@ __device__ __forceinline__ int shift_from_code(int code, int P) {
 
 // Operand rows contiguous in K (s_k == 1): one block per (row, batch), of
 // 256 threads, or 512 for rows longer than 4096.  An f64 row of at most 16
-// values per thread at a 16-byte aligned address is read once into
-// registers (four groups of four consecutive k, 4 * blockDim.x apart, so
-// every load is coalesced), reduced to the row maximum and quantised from
-// registers.  Other rows take two passes: the maximum, then the values again
-// (mostly from L2).  Four residues per thread per modulus make one coalesced
-// 4-byte store.
+// values per thread at a 16-byte aligned address is read into registers
+// (four groups of four consecutive k, 4 * blockDim.x apart, so every load
+// is coalesced) and reduced to the row maximum; the groups are then read
+// again one at a time (L1 hits) and quantised.  Other rows take the same two
+// passes with the second mostly from L2.  Four residues per thread per
+// modulus make one coalesced 4-byte store.
 constexpr int kSplitRowsMaxThreads = 512;
 
 __host__ __device__ constexpr int split_rows_threads(int64_t K) {
@@ -356,7 +386,7 @@ __device__ __forceinline__ void split_rows_body(const DotOperand& o, int64_t row
       const int64_t k0 = g * group + threadIdx.x * 4;
       if (live && k0 + 4 <= K) {
         const double2* p = reinterpret_cast<const double2*>(o.f64 + base + k0);
-        const double2 v01 = __ldcs(p), v23 = __ldcs(p + 1);
+        const double2 v01 = __ldg(p), v23 = __ldg(p + 1);
         v[g * 4 + 0] = v01.x;
         v[g * 4 + 1] = v01.y;
         v[g * 4 + 2] = v23.x;
@@ -402,13 +432,27 @@ __device__ __forceinline__ void split_rows_body(const DotOperand& o, int64_t row
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
   uint8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
   if (in_regs) {
-#pragma unroll
+    // the groups again, one at a time from L1 (the first pass read them
+    // through it): the residue code appears once rather than four times
+#pragma unroll 1
     for (int g = 0; g < 4; ++g) {
       const int64_t k0 = g * group + threadIdx.x * 4;
       if (k0 < Kp) {
+        double w[4];
+        if (!zero && k0 + 4 <= K) {
+          const double2* p = reinterpret_cast<const double2*>(o.f64 + base + k0);
+          const double2 v01 = __ldg(p), v23 = __ldg(p + 1);
+          w[0] = v01.x;
+          w[1] = v01.y;
+          w[2] = v23.x;
+          w[3] = v23.y;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) w[j] = (zero || k0 + j >= K) ? 0.0 : o.f64[base + k0 + j];
+        }
         Limbs x[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(zero ? 0.0 : v[g * 4 + j], sh));
+        for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(w[j], sh));
         store_planes_n<4, true>(x, row_out + k0, plane_stride);
       }
     }
@@ -592,9 +636,9 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
 #pragma unroll
   for (int j = 0; j < 16; ++j) q[j] = limbs_of(tile[my_grp * 16 + j][my_row]);
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
-  store_planes_n<16, false>(q, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp +
-                                   kc + my_grp * 16,
-                            plane_stride);
+  store_planes_16_rt(q, planes + (static_cast<size_t>(b) * rows_pad + r0 + my_row) * Kp +
+                            kc + my_grp * 16,
+                     plane_stride);
 }
 
 // ---------------------------------------------------------------------------
