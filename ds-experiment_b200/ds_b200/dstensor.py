@@ -21,7 +21,7 @@ same DS operations, in the same order, as one target call per operation.
 """
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Tuple, Union
+from typing import Dict, List, Tuple, Union
 
 import torch
 

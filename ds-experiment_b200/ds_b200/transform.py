@@ -760,13 +760,18 @@ class _Lowering:
 
 
 class _Plan:
-    def __init__(self, gm, inputs, steps, output, consts):
+    """The lowered program for one argument signature: its steps, the slots
+    of the captured inputs, the constants, the output template and the
+    values of the trailing parameters the call left at their defaults."""
+
+    def __init__(self, gm, inputs, steps, output, consts, defaults=()):
         self.gm, self.inputs, self.steps = gm, inputs, steps
         self.output, self.consts = output, consts
+        self.defaults = list(defaults)
 
     def run(self, args):
         env = dict(self.consts)
-        env.update(zip(self.inputs, args))
+        env.update(zip(self.inputs, list(args) + self.defaults))
         for st in self.steps:
             st.run(env)
         return _subst(self.output, env)
@@ -837,14 +842,10 @@ class DsFunction:
         full = list(args) + [concrete[q.name] for q in params[len(args):]]
         _propagate_shapes(gm, full)
         inputs, steps, output, consts = _Lowering(gm, full).lower()
-        plan = _Plan(gm, inputs, steps, output, consts)
-        plan.n_args = len(args)
-        plan.defaults = full[len(args):]
-        return plan
+        return _Plan(gm, inputs, steps, output, consts, full[len(args):])
 
     def __call__(self, *args):
-        p = self.plan(*args)
-        return p.run(list(args) + p.defaults)
+        return self.plan(*args).run(args)
 
     def explain(self, *args) -> str:
         """The lowered program for these arguments, one line per step."""

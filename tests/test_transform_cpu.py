@@ -439,3 +439,16 @@ def test_linear_layers_lower_to_product_and_add(oracle_backend):
                        C(dso, 2.0, (5, 4)))
         want = torch.from_numpy(dso.ds_to_f64(H)) @ net.w2.T
     assert torch.allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_default_parameters_are_baked_in(oracle_backend):
+    dso = oracle_backend
+
+    def f(x, alpha=2.0):
+        return x * alpha
+
+    g = tr.ds_transform(f)
+    x = rand((6,), 26)
+    assert_bits_equal(g(x).numpy(), dso.ds_to_f64(dso.ds_mul(P(dso, x), C(dso, 2.0, (6,)))), "default")
+    assert_bits_equal(g(x, 0.5).numpy(), dso.ds_to_f64(dso.ds_mul(P(dso, x), C(dso, 0.5, (6,)))),
+                      "given")
