@@ -169,3 +169,36 @@ def test_cpu_tensor_rejected():
     from ds_b200 import ops
     with pytest.raises(ValueError, match="CUDA"):
         ops.ds_from_f64(torch.zeros(4, dtype=torch.float64))
+
+
+def test_fused_reduce_argument_errors(L):
+    """ds_fused_reduce checks its body, shape, buffers and workspace before
+    any launch."""
+    r = ctypes.byref
+    ops = (L.DsFusedOp * 1)(L.DsFusedOp(L.DS_FUSED_INPUT, 0, 0, 0, 0.0))
+    x, _1 = _b(L, (8,))
+    arr = (ctypes.POINTER(L.DsBuffer) * 1)(ctypes.pointer(x))
+    ty = (ctypes.c_int32 * 1)(L.DS_FUSED_F64)
+    dims = (ctypes.c_int64 * 1)(8)
+    s, _2 = _b(L, ())
+    lib = L.lib()
+
+    def call(body=L.DS_BODY_ADD, rank=1, init=s, ws=None, nbytes=0, d=dims):
+        st = lib.ds_fused_reduce(ops, 1, ty, arr, 1, d, rank, body, r(init), r(s), r(s), r(s),
+                                 ws, nbytes, None)
+        return st, L.last_error()
+    st, msg = call(body=L.DS_BODY_SUB)
+    assert st == L.DS_INVALID_ARGUMENT and "DS_BODY_ADD or DS_BODY_MUL" in msg
+    st, msg = call(rank=9)
+    assert st == L.DS_INVALID_ARGUMENT and "8 dimensions" in msg
+    null, _3 = _b(L, (), ptr=0)
+    st, msg = call(init=null)
+    assert st == L.DS_INVALID_ARGUMENT and "null" in msg
+    st, msg = call()
+    assert st == L.DS_INVALID_ARGUMENT and "workspace" in msg
+    need = int(lib.ds_fused_reduce_workspace_size(dims, 1))
+    assert need > 0
+    # the map's shape does not match the input: rejected by the program checks
+    bad = (ctypes.c_int64 * 1)(9)
+    st, msg = call(ws=ctypes.c_void_p(0x100000), nbytes=need, d=bad)
+    assert st == L.DS_INVALID_ARGUMENT and "broadcast" in msg
