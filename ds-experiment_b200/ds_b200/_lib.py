@@ -148,6 +148,24 @@ def gemm_kernel_info() -> dict:
             "kernel": "cta_pair" if p.value > 0 else "single_cta"}
 
 
+_raw_stream = getattr(__import__("torch")._C, "_cuda_getCurrentRawStream", None)
+
+
+def current_stream_ptr(device=None) -> int:
+    """The cudaStream_t of torch's current stream on `device` (a
+    torch.device, an index, or None for the current device), as an int.
+    Uses torch's raw-pointer query when it has one: building a Stream
+    object costs several microseconds per call."""
+    import torch
+    if isinstance(device, torch.device):
+        device = device.index
+    if device is None:
+        device = torch.cuda.current_device()
+    if _raw_stream is not None:
+        return int(_raw_stream(device))
+    return torch.cuda.current_stream(device).cuda_stream
+
+
 def profile_enable(on: bool = True) -> None:
     lib().ds_profile_enable(1 if on else 0)
 

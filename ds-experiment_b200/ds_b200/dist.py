@@ -208,7 +208,7 @@ def _sum_exchange_cuda(x_local: torch.Tensor, init: float, exchange: PeerExchang
     out = torch.empty((), dtype=torch.float64, device=x.device)
     tb = _lib.DsBuffer(it.data_ptr(), st["out_dims"], 0)
     ob = _lib.DsBuffer(out.data_ptr(), st["out_dims"], 0)
-    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    stream = ctypes.c_void_p(_lib.current_stream_ptr(x.device))
     _lib.check(L.ds_reduce_f64_sharded(
         ctypes.byref(ib), ctypes.byref(tb), body, ctypes.byref(ob), st["ptrs"], exchange.world,
         exchange.rank, exchange.next_epoch(), exchange.timeout_ms, st["wsp"], st["ws_bytes"],

@@ -121,14 +121,15 @@ def register_ffi_target(name: str, target, platform: str = "CUDA") -> None:
     if sym not in CONVENTIONS:
         raise ValueError(f"{sym!r} is not a libds_b200 entry point")
     _registry[name] = sym
+    _calls.clear()
 
 
 def registered_targets():
     return sorted(_registry)
 
 
-def _stream_handle() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+def _stream_handle(device=None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(_lib.current_stream_ptr(device))
 
 
 def _check_tensor(t, dtype, what):
@@ -150,14 +151,34 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
+# (target, result specs) -> the callable ffi_call built for them
+_calls: Dict[tuple, object] = {}
+_MAX_CALLS = 512
+
+
 def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
     """Return a callable running target `target_name` on torch CUDA tensors.
 
     result_shape_dtypes: a ShapeDtypeStruct or a sequence of them, one per
     result.  Attributes are keyword arguments, as in jax.ffi.ffi_call.
     vmap_method is accepted for signature compatibility; the entry points
-    already take arbitrary leading (batch) dimensions.
+    already take arbitrary leading (batch) dimensions.  Callables are cached
+    per target and result specs, so a call site that asks again each time
+    pays a dictionary lookup.
     """
+    key = (target_name, result_shape_dtypes if isinstance(result_shape_dtypes, ShapeDtypeStruct)
+           else tuple(result_shape_dtypes))
+    hit = _calls.get(key)
+    if hit is not None:
+        return hit
+    call = _make_call(target_name, result_shape_dtypes)
+    if len(_calls) >= _MAX_CALLS:
+        _calls.clear()
+    _calls[key] = call
+    return call
+
+
+def _make_call(target_name: str, result_shape_dtypes):
     if target_name not in _registry:
         raise KeyError(f"custom-call target {target_name!r} is not registered")
     sym = _registry[target_name]
@@ -206,7 +227,7 @@ def ffi_call(target_name: str, result_shape_dtypes, vmap_method=None):
             keep.append(d)
             bufs.append(b)
         refs = [ctypes.byref(b) for b in bufs]
-        stream = _stream_handle()
+        stream = _stream_handle(device)
         if conv.kind == "plain":
             call_args = refs[:len(args)]
             for name in conv.attrs:

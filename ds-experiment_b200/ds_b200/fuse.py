@@ -235,7 +235,7 @@ class jit:
 
     @staticmethod
     def _run(comp, ty, arr, n, out_type, ob):
-        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        stream = ctypes.c_void_p(_lib.current_stream_ptr())
         return _lib.lib().ds_fused_run(comp.ops, comp.n_ops, ty, arr, n, out_type,
                                        ctypes.byref(ob), stream)
 
@@ -358,7 +358,7 @@ class Prepared:
             hi = torch.empty((), dtype=torch.float32, device=device)
             lo = torch.empty((), dtype=torch.float32, device=device)
             scal = [_lib.make_buffer(t.data_ptr(), ()) for t in (ih, il, hi, lo)]
-            stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            stream = ctypes.c_void_p(_lib.current_stream_ptr())
             st = L.ds_fused_reduce(self._comp.ops, self._comp.n_ops, self._types, arr, len(bufs),
                                    dims, len(shape), _BODY[body],
                                    *[ctypes.byref(b) for b, _ in scal],

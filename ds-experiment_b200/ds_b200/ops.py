@@ -125,7 +125,7 @@ def _scalar(value: float, dtype, device) -> torch.Tensor:
         # made inside a CUDA graph capture: its fill runs at replay, so it is
         # not kept for eager calls
         return torch.full((), float(value), dtype=dtype, device=device)
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _lib.current_stream_ptr(device)
     key = (device.index, stream, dtype, float(value).hex())  # hex keeps -0.0 apart
     t = _SCALARS.get(key)
     if t is None:
@@ -210,7 +210,7 @@ def ds_reduce_f64_multi(xs, inits=None, dimensions: Optional[Sequence[int]] = No
     ws_bytes = int(L.ds_reduce_workspace_size(ib[0], cdims, len(dims)))
     ws = torch.empty(max(ws_bytes, 8), dtype=torch.uint8, device=dev)
     body_codes = (ctypes.c_int32 * n)(*[_BODIES[b] for b in bodies])
-    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    stream = ctypes.c_void_p(_lib.current_stream_ptr(dev))
     _lib.check(L.ds_reduce_f64_multi(ib, bufs(its), body_codes, n, cdims, len(dims), bufs(outs),
                                      ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream),
                "ds_reduce_f64_multi")
