@@ -573,6 +573,18 @@ def run_stream(args):
                 "what": "sum((a + b) * c) per rank, one kernel (ds_fused_reduce)",
                 "GB/s": round(world * 24.0 * n / (rms * 1e-3) / 1e9, 1),
                 "ms_per_step": round(rms, 4), "unfused_ms_per_step": round(tms, 4)}
+            # the same kernel over 2^20 .. 2^28 values per rank (uniform
+            # [-1, 1) drawn on the device: timing only, no data-dependent path)
+            sweep = []
+            for lg in (20, 22, 24, 26, 28):
+                m = 1 << lg
+                xs = [torch.rand(m, dtype=torch.float64, device=dev) * 2 - 1 for _ in range(3)]
+                sms, _ = timed(lambda: ops.ds_fused_add_mul3_to_f64(*xs), args.steps)
+                sweep.append({"n": m, "GB/s": round(world * 32.0 * m / (sms * 1e-3) / 1e9, 1),
+                              "ms_per_step": round(sms, 4),
+                              "l2": "fits in L2" if 32.0 * m < 126e6 else "exceeds L2"})
+                del xs
+            line["size_sweep"] = sweep
         k_ms, k_n = _lib.profile_read(fam)
         # device time of the family per step: at N > 1 the reduce family
         # also holds the tiny combine of the gathered pairs
