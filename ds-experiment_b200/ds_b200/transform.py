@@ -776,6 +776,39 @@ class _Plan:
             st.run(env)
         return _subst(self.output, env)
 
+    def run_graph(self, args):
+        """Run as a CUDA graph: the first call runs the plan once (compiling
+        its programs), then captures it over static copies of the tensor
+        arguments; every call copies its tensors in and replays.  The
+        returned tensors are the graph's own and are overwritten by the
+        next call.  A plan that cannot be captured (a host sync in an
+        operation left to torch) runs eagerly from then on."""
+        g = getattr(self, "_graph", None)
+        if g is None:
+            out = self.run(args)  # compiles the programs and warms the allocator
+            try:
+                static = [a.clone() if isinstance(a, torch.Tensor) else a for a in args]
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    self.run(static)
+                torch.cuda.current_stream().wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    static_out = self.run(static)
+                self._graph = (graph, static, static_out)
+            except Exception:
+                self._graph = False
+            return out
+        if g is False:
+            return self.run(args)
+        graph, static, static_out = g
+        for dst, src in zip(static, args):
+            if isinstance(dst, torch.Tensor):
+                dst.copy_(src)
+        graph.replay()
+        return static_out
+
     def launches(self) -> Dict[str, int]:
         """How many steps of each kind the plan runs (fused programs,
         reductions, products, layout and untouched torch operations)."""
@@ -811,8 +844,9 @@ class DsFunction:
     Tensor arguments are captured symbolically; any other argument is baked
     into the capture, so each value gets its own plan."""
 
-    def __init__(self, fn: Callable):
+    def __init__(self, fn: Callable, graphs: bool = False):
         self.fn = fn
+        self.graphs = graphs
         self._plans: Dict[tuple, _Plan] = {}
         self.__doc__ = getattr(fn, "__doc__", None)
         self.__name__ = getattr(fn, "__name__", type(fn).__name__)
@@ -845,7 +879,8 @@ class DsFunction:
         return _Plan(gm, inputs, steps, output, consts, full[len(args):])
 
     def __call__(self, *args):
-        return self.plan(*args).run(args)
+        p = self.plan(*args)
+        return p.run_graph(args) if self.graphs else p.run(args)
 
     def explain(self, *args) -> str:
         """The lowered program for these arguments, one line per step."""
@@ -904,7 +939,16 @@ def _propagate_shapes(gm: fx.GraphModule, args):
         ShapeProp(gm).propagate(*args)
 
 
-def ds_transform(fn: Callable) -> DsFunction:
+def ds_transform(fn: Optional[Callable] = None, *, graphs: bool = False):
     """Decorator: run `fn` (a function or module of torch tensors) with its
-    f64 / f32 arithmetic rewritten to DS, as the reference's DS pass does."""
-    return DsFunction(fn)
+    f64 / f32 arithmetic rewritten to DS, as the reference's DS pass does.
+    With graphs=True each plan is captured once as a CUDA graph and
+    replayed (one host call per invocation however many launches the plan
+    has; results are overwritten by the next call):
+
+        @ds_transform(graphs=True)
+        def f(x, y): ...
+    """
+    if fn is None:
+        return lambda f: DsFunction(f, graphs)
+    return DsFunction(fn, graphs)

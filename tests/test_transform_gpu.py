@@ -199,3 +199,23 @@ def test_edge_shapes(tr, dso):
     U, V = dso.ds_from_f32(u), dso.ds_from_f32(v)
     assert got.dtype == np.float32
     assert_bits_equal(got, dso.ds_to_f32(dso.ds_mul(dso.ds_add(U, V), U)), "f32 program")
+
+
+def test_graph_mode_replays_with_new_values(tr, dso):
+    """graphs=True: the plan is captured once; later calls copy their
+    tensors in and replay, with the eager results bit for bit."""
+    rng = np.random.default_rng(12)
+
+    def prog(a, b):
+        y = (a + b) * b - 0.25
+        return y.sum(), y * 2.0
+
+    f = tr.ds_transform(prog, graphs=True)
+    eager = tr.ds_transform(prog)
+    for i in range(4):
+        a, b = cu(rng.uniform(-1, 1, 5000)), cu(rng.uniform(-1, 1, 5000))
+        s, y = f(a, b)
+        es, ey = eager(a, b)
+        assert_bits_equal(host(s), host(es), f"sum {i}")
+        assert_bits_equal(host(y), host(ey), f"map {i}")
+    assert f.plan(a, b)._graph  # captured
