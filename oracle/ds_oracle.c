@@ -1,7 +1,7 @@
 /*
  * CPU oracle for the double-single (DS) hot path.  TEST INFRASTRUCTURE ONLY:
  * the parity tests, the smoke check and the CPU-baseline leg of bench.py call
- * it as the checker.  The product path never links or calls it.
+ * it to check results against.  The product path never links or calls it.
  *
  * Each function restates, operation for operation, a CPU handler of the
  * reference (rcast915/ds-experiment, cpp/).  The reference sources need the
