@@ -684,9 +684,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: false (and an error code recorded) after ~2 s, or at once if
-// another role of any CTA has already given up.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// another role of any CTA has already given up.  The first try is inlined
+// into the pipeline loops; only a wait that has to spin makes the call (a
+// call per K-block cost the GEMM 9% of its time).
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*reinterpret_cast<volatile int*>(err) != 0) return false;
@@ -696,6 +697,10 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
     }
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, err, code);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
