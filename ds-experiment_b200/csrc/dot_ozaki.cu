@@ -971,8 +971,10 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // ---- CTA-pair variant (tcgen05 cta_group::2) ---------------------------------
 //
 // A cluster of two CTAs computes 256x256 tiles.  Each CTA stages its own 128
-// rows of A and its 128-row half of the B tile (16 + 16 KB per K-block
-// instead of 16 + 32 KB), the even CTA issues tcgen05.mma.cta_group::2
+// rows of A and its 128-row half of the B tile (16 + 16 KB per 128-byte
+// K sub-tile instead of 16 + 32 KB; a pipeline stage holds two sub-tiles,
+// so the barrier round trip, the commit and the TMA issues are paid once
+// per 256 bytes of K), the even CTA issues tcgen05.mma.cta_group::2
 // M=256 N=256 K=32 over both CTAs' shared memory, and each CTA drains its
 // own 128 rows from its own TMEM.  Both CTAs' TMA loads complete on the even
 // CTA's "full" barrier (addressed with mapa); the MMA commits arrive on both
@@ -980,7 +982,8 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // of the pair arrives on the even CTA's "tmem empty" barrier.  No load uses
 // multicast.
 
-constexpr int kStages2 = 6;
+constexpr int kStages2 = 3;
+constexpr int kSub2 = 2;  // 128-byte K sub-tiles per stage
 constexpr int kStage2 = kTileM * kTileK;  // 16 KB: A rows, or half of the B tile
 constexpr uint32_t kIdesc2 = (2u << 4) | (0u << 7) | (0u << 10) | ((256u >> 3) << 17) |
                              ((256u >> 4) << 24);
@@ -1084,8 +1087,8 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + kStages2 * kStage2;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages2 * kStage2);
+  uint8_t* smem_b = smem + kStages2 * kSub2 * kStage2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages2 * kSub2 * kStage2);
   uint64_t* empty = full + kStages2;
   uint64_t* tfull = empty + kStages2;
   uint64_t* tempty = tfull + 2;
@@ -1133,15 +1136,19 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                         static_cast<int64_t>(w.tm) * 256 + rank * 128);
         const int yb = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Np +
                                         static_cast<int64_t>(w.tn) * 256 + rank * 128);
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = 0; kb < (p.kblocks + kSub2 - 1) / kSub2; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 11)) {
             ok = false;
             break;
           }
-          if (leader) mbar_expect_tx(&full[stage], 4 * kStage2);
+          if (leader) mbar_expect_tx(&full[stage], 4 * kSub2 * kStage2);
           const uint32_t full0 = in_rank0(&full[stage]);
-          tma_load_2d_pair(smem_a + stage * kStage2, &tmap_a, kb * kTileK, ya, full0);
-          tma_load_2d_pair(smem_b + stage * kStage2, &tmap_b, kb * kTileK, yb, full0);
+#pragma unroll
+          for (int sub = 0; sub < kSub2; ++sub) {
+            const int x = (kb * kSub2 + sub) * kTileK;
+            tma_load_2d_pair(smem_a + (stage * kSub2 + sub) * kStage2, &tmap_a, x, ya, full0);
+            tma_load_2d_pair(smem_b + (stage * kSub2 + sub) * kStage2, &tmap_b, x, yb, full0);
+          }
           if (++stage == kStages2) {
             stage = 0;
             phase ^= 1;
@@ -1166,17 +1173,21 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.err, 12)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc * 256);
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = 0; kb < (p.kblocks + kSub2 - 1) / kSub2; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, 13)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem_a + stage * kStage2);
-          const uint32_t b0 = smem_u32(smem_b + stage * kStage2);
 #pragma unroll
-          for (int k = 0; k < kTileK / 32; ++k) {
-            mma_i8_pair(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32), (kb | k) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < kSub2; ++sub) {
+            const uint32_t a0 = smem_u32(smem_a + (stage * kSub2 + sub) * kStage2);
+            const uint32_t b0 = smem_u32(smem_b + (stage * kSub2 + sub) * kStage2);
+#pragma unroll
+            for (int k = 0; k < kTileK / 32; ++k) {
+              mma_i8_pair(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32),
+                          (kb | sub | k) != 0 ? 1u : 0u);
+            }
           }
           mma_commit_pair(&empty[stage]);
           if (++stage == kStages2) {
@@ -1398,7 +1409,7 @@ size_t gemm_smem_bytes() {
 }
 
 size_t gemm2_smem_bytes() {
-  return 1024 + 2 * kStages2 * kStage2 + (2 * kStages2 + 5) * sizeof(uint64_t) + 16;
+  return 1024 + 2 * kStages2 * kSub2 * kStage2 + (2 * kStages2 + 5) * sizeof(uint64_t) + 16;
 }
 
 // Kernel choice and per-device launch limits, set up once per device.

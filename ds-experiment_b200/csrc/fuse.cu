@@ -414,6 +414,51 @@ int describe(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
 std::mutex g_mu;
 std::map<std::pair<int, std::string>, CUfunction> g_funcs;
 
+// Everything the generated source depends on, as a short byte string: the
+// operations, each input's type, broadcast strides and layout, the output
+// type and shape, the pair path and the reduction body.  A call looks its
+// function up by this key and generates the source only on a miss.
+std::string key_of(const Desc& d) {
+  std::string k;
+  auto put = [&k](const void* p, size_t n) { k.append(static_cast<const char*>(p), n); };
+  const int32_t head[5] = {static_cast<int32_t>(d.ops.size()), static_cast<int32_t>(d.in.size()),
+                           d.out_type, d.rank, (d.pairs ? 1 : 0) | ((d.reduce_body + 1) << 1)};
+  put(head, sizeof head);
+  put(d.dims, sizeof(int64_t) * d.rank);
+  for (const ds_fused_op& o : d.ops) {
+    const int32_t c[3] = {o.code, o.a, o.b};
+    put(c, sizeof c);
+    put(&o.value, sizeof o.value);
+  }
+  for (const InputView& v : d.in) {
+    const int32_t t[2] = {v.type, v.full ? 1 : 0};
+    put(t, sizeof t);
+    put(v.stride, sizeof(int64_t) * d.rank);
+  }
+  return k;
+}
+std::map<std::pair<int, std::string>, CUfunction> g_by_key;
+
+int compile(const std::string& src, CUfunction* fn);
+
+int compile_desc(const Desc& d, CUfunction* fn) {
+  int dev = 0;
+  DSB_CUDA_TRY(cudaGetDevice(&dev));
+  const std::string key = key_of(d);
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_by_key.find({dev, key});
+    if (it != g_by_key.end()) {
+      *fn = it->second;
+      return DS_OK;
+    }
+  }
+  if (int st = compile(generate(d), fn)) return st;
+  std::lock_guard<std::mutex> lock(g_mu);
+  g_by_key[{dev, key}] = *fn;
+  return DS_OK;
+}
+
 int compile(const std::string& src, CUfunction* fn) {
   int dev = 0;
   DSB_CUDA_TRY(cudaGetDevice(&dev));
@@ -514,7 +559,7 @@ int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_typ
   if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, out_type, out, d)) return st;
   if (d.n == 0) return ok();
   CUfunction fn = nullptr;
-  if (int st = compile(generate(d), &fn)) return st;
+  if (int st = compile_desc(d, &fn)) return st;
   std::vector<void*> ptrs(n_inputs + 1);
   std::vector<void*> args(n_inputs + 2);
   for (int32_t k = 0; k < n_inputs; ++k) {
@@ -579,7 +624,7 @@ int ds_fused_reduce(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_
   unsigned grid = 0;
   if (d.n > 0) {
     CUfunction fn = nullptr;
-    if (int st = compile(generate(d), &fn)) return st;
+    if (int st = compile_desc(d, &fn)) return st;
     std::vector<void*> ptrs(n_inputs + 1);
     std::vector<void*> args(n_inputs + 2);
     for (int32_t k = 0; k < n_inputs; ++k) {
