@@ -1695,14 +1695,17 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
   // stream beside the split of band i + 1 and the CRT of band i - 1) left
   // CTA pairs of the GEMM blocked in tcgen05.alloc on some SMs; it is not
   // used.
-  DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
   // A split by rows and B by columns (the usual row-major A and B): the
   // column maxima of B are taken in the same launch as A's row split.
   const bool merged = p.batch == 1 && split_by_rows(p.a, p.M) && !split_by_rows(p.b, p.N) &&
                       split_rows_threads(p.K) == 256;
   if (merged) {
     ProfileScope prof("ozaki_split", s);
-    DSB_CUDA_TRY(cudaMemsetAsync(cb, 0, sizeof(int) * g.Np, s));
+    // B's column-maximum codes and the error word are neighbours in the
+    // workspace (in that order): one memset clears both
+    DSB_CUDA_TRY(cudaMemsetAsync(
+        cb, 0, static_cast<size_t>(reinterpret_cast<char*>(err + 1) - reinterpret_cast<char*>(cb)),
+        s));
     const int64_t cgx = g.Np / kColTileR, cgy = (p.K + kColmaxSlab - 1) / kColmaxSlab;
     const int64_t nc = cgx * cgy;
     {
@@ -1716,6 +1719,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
     split_cols_kernel<<<g2, 256, 0, s>>>(p.b, p.N, p.K, g.Np, g.Kp, 1, P, cb, planes_b, sb);
     if (int st = launch_status()) return st;
   } else {
+    DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
     ProfileScope prof("ozaki_split", s);
     if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
       return st;
