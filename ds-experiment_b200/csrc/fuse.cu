@@ -132,6 +132,7 @@ struct Desc {
   int64_t n = 1;
   bool pairs = false;  // all inputs full and 16-byte aligned, output too
   int reduce_body = -1;  // DS_BODY_ADD / DS_BODY_MUL: a full reduction of the results
+  int rows_reduced = 0;  // > 0: reduce only that many trailing dimensions, per row
 };
 
 const char* ctype(int type) {
@@ -316,6 +317,58 @@ std::string generate(const Desc& d) {
   return s;
 }
 
+// The kernel for a reduction over the trailing dimensions of the program's
+// shape: each block owns whole rows (grid-strided), its threads fold the
+// row's elements they visit, warp and block trees combine them, and thread 0
+// writes body(init, row total) -- init alone for an empty row.
+std::string generate_rows(const Desc& d) {
+  const std::string body = d.reduce_body == DS_BODY_MUL ? "mul" : "add";
+  const std::string ident = d.reduce_body == DS_BODY_MUL ? "ds2{1.0f, 0.0f}" : "ds2{0.0f, 0.0f}";
+  const std::string last = std::to_string(d.ops.size() - 1);
+  std::string s;
+  s += kDsArithSource;
+  s += "\nusing namespace dsb;\n";
+  s += "extern \"C\" __global__ void __launch_bounds__(256) ds_fused_kernel(";
+  for (size_t k = 0; k < d.in.size(); ++k)
+    s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
+         ", ";
+  s += "float* __restrict__ out_hi, float* __restrict__ out_lo, const float* __restrict__ init_hi, "
+       "const float* __restrict__ init_lo, long long rows, long long R) {\n";
+  s += "  const ds2 init = ds2{*init_hi, *init_lo};\n";
+  s += "  __shared__ float2 part[8];\n";
+  s += "  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {\n";
+  s += "    ds2 acc = " + ident + ";\n";
+  s += "    for (long long j = threadIdx.x; j < R; j += blockDim.x) {\n";
+  s += "      const long long i = row * R + j;\n";
+  s += program_body(d, "", [&](int k) {
+    const InputView& in = d.in[k];
+    return from_value(in.type, "__ldg(in" + std::to_string(k) + " + (" + index_expr(d, in) + "))");
+  });
+  s += "      acc = " + body + "(acc, v" + last + ");\n    }\n";
+  s += "    for (int o = 16; o > 0; o >>= 1) {\n";
+  s += "      const ds2 t = ds2{__shfl_xor_sync(0xffffffffu, acc.hi, o), "
+       "__shfl_xor_sync(0xffffffffu, acc.lo, o)};\n";
+  s += "      acc = " + body + "(acc, t);\n    }\n";
+  s += "    if (blockDim.x > 32) {\n";
+  s += "      if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = make_float2(acc.hi, acc.lo);\n";
+  s += "      __syncthreads();\n";
+  s += "      if (threadIdx.x < 32) {\n";
+  s += "        acc = threadIdx.x < (blockDim.x >> 5) ? ds2{part[threadIdx.x].x, part[threadIdx.x].y} : " +
+       ident + ";\n";
+  s += "        for (int o = 4; o > 0; o >>= 1) {\n";
+  s += "          const ds2 t = ds2{__shfl_xor_sync(0xffffffffu, acc.hi, o), "
+       "__shfl_xor_sync(0xffffffffu, acc.lo, o)};\n";
+  s += "          acc = " + body + "(acc, t);\n        }\n";
+  s += "      }\n";
+  s += "      __syncthreads();  // part is refilled by the next row\n";
+  s += "    }\n";
+  s += "    if (threadIdx.x == 0) {\n";
+  s += "      const ds2 r = R == 0 ? init : " + body + "(init, acc);\n";
+  s += "      out_hi[row] = r.hi;\n      out_lo[row] = r.lo;\n    }\n";
+  s += "  }\n}\n";
+  return s;
+}
+
 int invalid(const std::string& m) { return set_error(DS_INVALID_ARGUMENT, m); }
 
 int64_t prod(const int64_t* d, int64_t r) {
@@ -422,7 +475,8 @@ std::string key_of(const Desc& d) {
   std::string k;
   auto put = [&k](const void* p, size_t n) { k.append(static_cast<const char*>(p), n); };
   const int32_t head[5] = {static_cast<int32_t>(d.ops.size()), static_cast<int32_t>(d.in.size()),
-                           d.out_type, d.rank, (d.pairs ? 1 : 0) | ((d.reduce_body + 1) << 1)};
+                           d.out_type, d.rank,
+                           (d.pairs ? 1 : 0) | ((d.reduce_body + 1) << 1) | (d.rows_reduced << 4)};
   put(head, sizeof head);
   put(d.dims, sizeof(int64_t) * d.rank);
   for (const ds_fused_op& o : d.ops) {
@@ -453,7 +507,7 @@ int compile_desc(const Desc& d, CUfunction* fn) {
       return DS_OK;
     }
   }
-  if (int st = compile(generate(d), fn)) return st;
+  if (int st = compile(d.rows_reduced > 0 ? generate_rows(d) : generate(d), fn)) return st;
   std::lock_guard<std::mutex> lock(g_mu);
   g_by_key[{dev, key}] = *fn;
   return DS_OK;
@@ -647,6 +701,95 @@ int ds_fused_reduce(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_
   const size_t off = fused_reduce_partial_bytes();
   return ds_reduce_packed(&pbuf, init_hi, init_lo, &dim0, 1, body, out_hi, out_lo,
                           static_cast<char*>(workspace) + off, workspace_bytes - off, stream);
+}
+
+// The per-row reduction: checks shared by the entry point and its compile
+// check; fills `d` and the row count and length.
+static int describe_rows(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                         const ds_buffer* const* inputs, int32_t n_inputs, const int64_t* dims,
+                         int32_t rank, int32_t n_reduced, int32_t body, void* stand_in,
+                         Desc& d, int64_t& rows, int64_t& row_len) {
+  if (body != DS_BODY_ADD && body != DS_BODY_MUL)
+    return invalid("ds_fused_reduce_rows: the body is DS_BODY_ADD or DS_BODY_MUL");
+  if (rank < 1 || rank > kMaxRank || dims == nullptr)
+    return invalid("ds_fused_reduce_rows: 1 to 8 dimensions");
+  if (n_reduced < 1 || n_reduced > rank)
+    return invalid("ds_fused_reduce_rows: 1 to rank trailing dimensions are reduced");
+  const ds_buffer shape{stand_in, dims, rank};
+  if (int st = describe(ops, n_ops, input_types, inputs, n_inputs, DS_FUSED_F64, &shape, d))
+    return st;
+  d.reduce_body = body;
+  d.rows_reduced = n_reduced;
+  rows = prod(dims, rank - n_reduced);
+  row_len = prod(dims + (rank - n_reduced), n_reduced);
+  return DS_OK;
+}
+
+int ds_fused_reduce_rows(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_types,
+                         const ds_buffer* const* inputs, int32_t n_inputs, const int64_t* dims,
+                         int32_t rank, int32_t n_reduced, int32_t body, const ds_buffer* init_hi,
+                         const ds_buffer* init_lo, const ds_buffer* out_hi,
+                         const ds_buffer* out_lo, void* stream) {
+  if (!init_hi || !init_lo || !out_hi || !out_lo || !init_hi->data || !init_lo->data ||
+      !out_hi->data || !out_lo->data)
+    return invalid("ds_fused_reduce_rows: null init or output buffer");
+  Desc d;
+  int64_t rows = 0, row_len = 0;
+  if (int st = describe_rows(ops, n_ops, input_types, inputs, n_inputs, dims, rank, n_reduced,
+                             body, out_hi->data, d, rows, row_len))
+    return st;
+  auto total = [](const ds_buffer* b) {
+    int64_t n = 1;
+    for (int64_t i = 0; i < b->rank; ++i) n *= b->dims[i];
+    return n;
+  };
+  if ((out_hi->rank && !out_hi->dims) || (out_lo->rank && !out_lo->dims) ||
+      total(out_hi) != rows || total(out_lo) != rows)
+    return invalid("ds_fused_reduce_rows: outputs must hold one value per row (" +
+                   std::to_string(rows) + ")");
+  if ((init_hi->rank && !init_hi->dims) || (init_lo->rank && !init_lo->dims) ||
+      total(init_hi) != 1 || total(init_lo) != 1)
+    return invalid("ds_fused_reduce_rows: init values must be scalars");
+  if (rows == 0) return ok();
+  CUfunction fn = nullptr;
+  if (int st = compile_desc(d, &fn)) return st;
+  std::vector<void*> ptrs(n_inputs + 4);
+  std::vector<void*> args(n_inputs + 6);
+  for (int32_t k = 0; k < n_inputs; ++k) {
+    ptrs[k] = inputs[k]->data;
+    args[k] = &ptrs[k];
+  }
+  ptrs[n_inputs] = out_hi->data;
+  ptrs[n_inputs + 1] = out_lo->data;
+  ptrs[n_inputs + 2] = init_hi->data;
+  ptrs[n_inputs + 3] = init_lo->data;
+  for (int q = 0; q < 4; ++q) args[n_inputs + q] = &ptrs[n_inputs + q];
+  long long nrows = rows, len = row_len;
+  args[n_inputs + 4] = &nrows;
+  args[n_inputs + 5] = &len;
+  // long rows: a block of 256 per row; short ones: a warp per row
+  const unsigned threads = row_len >= 2048 ? 256u : 32u;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (threads == 256u ? 8 : 32);
+  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  ProfileScope prof("fused_reduce", static_cast<cudaStream_t>(stream));
+  if (driver().launch(fn, grid, 1, 1, threads, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
+                      nullptr) != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused_reduce_rows: cuLaunchKernel failed");
+  return ok();
+}
+
+int ds_fused_reduce_rows_compile_check(const ds_fused_op* ops, int32_t n_ops,
+                                       const int32_t* input_types,
+                                       const ds_buffer* const* inputs, int32_t n_inputs,
+                                       const int64_t* dims, int32_t rank, int32_t n_reduced,
+                                       int32_t body) {
+  alignas(16) static char stand_in[16];
+  Desc d;
+  int64_t rows = 0, row_len = 0;
+  if (int st = describe_rows(ops, n_ops, input_types, inputs, n_inputs, dims, rank, n_reduced,
+                             body, stand_in, d, rows, row_len))
+    return st;
+  return nvrtc_check(generate_rows(d));
 }
 
 int ds_fused_reduce_compile_check(const ds_fused_op* ops, int32_t n_ops,

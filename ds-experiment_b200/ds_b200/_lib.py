@@ -120,6 +120,10 @@ SIGNATURES = {
                          _I32, _BUF, _BUF, _BUF, _BUF, _VP, _SZ, _VP], ctypes.c_int),
     "ds_fused_reduce_compile_check": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF), _I32,
                                        _I64P, _I32, _I32], ctypes.c_int),
+    "ds_fused_reduce_rows": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF), _I32, _I64P,
+                              _I32, _I32, _I32, _BUF, _BUF, _BUF, _BUF, _VP], ctypes.c_int),
+    "ds_fused_reduce_rows_compile_check": ([_OPS, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_BUF),
+                                            _I32, _I64P, _I32, _I32, _I32], ctypes.c_int),
     "ds_dot_tensor_plan": ([_I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_dot_tensor_kernel_info": ([ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_profile_enable": ([ctypes.c_int], None),

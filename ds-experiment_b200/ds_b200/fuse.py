@@ -382,6 +382,51 @@ class Prepared:
             _BODY[body]), "compile")
 
 
+    def reduce_rows(self, tensors: Sequence[torch.Tensor], shape, n_reduced: int,
+                    body: str = "add", init=(0.0, 0.0)) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The program over the logical `shape`, reduced over its last
+        `n_reduced` dimensions in the same kernel (ds_fused_reduce_rows):
+        (hi, lo) f32 tensors of shape shape[:-n_reduced]."""
+        from . import ops  # the init scalars' cache
+        if len(tensors) != len(self.kinds) or not tensors:
+            raise ValueError(f"the program takes {len(self.kinds)} input tensors")
+        tensors = [t.contiguous() for t in tensors]
+        device = tensors[0].device
+        for t in tensors:
+            if not t.is_cuda or t.device != device:
+                raise ValueError("fused inputs must be CUDA tensors on one device")
+        shape, dims, bufs, keep, arr = self._reduce_args(tensors, shape, body)
+        out_shape = shape[:len(shape) - int(n_reduced)]
+        with torch.cuda.device(device):
+            ih = ops._scalar(init[0], torch.float32, device)
+            il = ops._scalar(init[1], torch.float32, device)
+            hi = torch.empty(out_shape, dtype=torch.float32, device=device)
+            lo = torch.empty(out_shape, dtype=torch.float32, device=device)
+            scal = [_lib.make_buffer(t.data_ptr(), tuple(t.shape)) for t in (ih, il, hi, lo)]
+            stream = ctypes.c_void_p(_lib.current_stream_ptr(device))
+            st = _lib.lib().ds_fused_reduce_rows(
+                self._comp.ops, self._comp.n_ops, self._types, arr, len(bufs), dims, len(shape),
+                int(n_reduced), _BODY[body], *[ctypes.byref(b) for b, _ in scal], stream)
+        _lib.check(st, "ds_fused_reduce_rows")
+        return hi, lo
+
+    def reduce_rows_compile_check(self, shapes: Sequence[tuple], shape, n_reduced: int,
+                                  body: str = "add") -> None:
+        """Generate and compile the per-row kernel for inputs of these shapes
+        (no GPU needed; raises on a compilation error)."""
+        shape, dims, _, _, _ = self._reduce_args([], shape, body)
+        bufs, keep = [], []
+        for s in shapes:
+            b, d = _lib.make_buffer(256, tuple(s))
+            bufs.append(b)
+            keep.append(d)
+        arr = (ctypes.POINTER(_lib.DsBuffer) * max(len(bufs), 1))(
+            *[ctypes.pointer(b) for b in bufs])
+        _lib.check(_lib.lib().ds_fused_reduce_rows_compile_check(
+            self._comp.ops, self._comp.n_ops, self._types, arr, len(bufs), dims, len(shape),
+            int(n_reduced), _BODY[body]), "compile")
+
+
 _BODY = {"add": _lib.DS_BODY_ADD, "mul": _lib.DS_BODY_MUL}
 
 

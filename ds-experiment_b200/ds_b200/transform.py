@@ -18,8 +18,9 @@ interception), and it is lowered onto this library's targets by the same rules:
 - a connected elementwise DAG of add / sub / mul / neg becomes ONE
   generated kernel (ds_fused_run), where the pass emits a chain of f32 ops;
 - `sum` / `prod` over DS values become ds_reduce_packed (ds_reduce_from_f64
-  for an f64 argument, which splits as it loads); a full reduction of an
-  elementwise DAG runs in the DAG's own kernel (ds_fused_reduce);
+  for an f64 argument, which splits as it loads); a reduction of an
+  elementwise DAG over all or over its trailing dimensions runs in the DAG's
+  own kernel (ds_fused_reduce, ds_fused_reduce_rows);
 - `matmul` / `mm` / `bmm` / `@` become ds_dot_general_f64 (tensor cores);
 - layout operations (reshape, view, unsqueeze, squeeze, expand, transpose,
   permute, t, T, mT, flatten, contiguous) act on hi and lo alike, as the
@@ -205,6 +206,26 @@ class _FusedReduceStep:
     def run(self, env):
         hi, lo = self.prepared.reduce([env[s] for s in self.inputs], self.map_shape, self.body,
                                       (self.init, 0.0))
+        env[self.out] = torch.stack([hi, lo], dim=-1).reshape(self.shape + (2,))
+
+
+class _FusedReduceRowsStep:
+    """A pending elementwise value reduced over its trailing dimensions in
+    the same kernel (ds_fused_reduce_rows): one block folds a whole row."""
+
+    def __init__(self, out, prog, inputs, kinds, map_shape, n_reduced, body, init, shape):
+        self.out, self.inputs = out, list(inputs)
+        self.map_shape, self.n_reduced = tuple(map_shape), int(n_reduced)
+        self.body, self.init, self.shape = body, init, tuple(shape)
+        self.prepared = fuse.Prepared(prog, kinds, "packed")
+        names = ", ".join(f"%{s}:{k}" for s, k in zip(inputs, kinds))
+        self.text = (f"%{out} = ds_fused_reduce_rows[{len(prog)} ops]({names}) over "
+                     f"{list(self.map_shape)}, last {self.n_reduced} dims, body={body}, "
+                     f"init={init} -> packed {list(self.shape)}")
+
+    def run(self, env):
+        hi, lo = self.prepared.reduce_rows([env[s] for s in self.inputs], self.map_shape,
+                                           self.n_reduced, self.body, (self.init, 0.0))
         env[self.out] = torch.stack([hi, lo], dim=-1).reshape(self.shape + (2,))
 
 
@@ -698,6 +719,15 @@ class _Lowering:
             out = self.slot(node.name)
             self.steps.append(_FusedReduceStep(out, prog, slots, kinds, self._shape(src), body,
                                                init, self._shape(node)))
+            self.state[node] = _Leaf(out, "packed", False)
+            return
+        k = len(dims)
+        if isinstance(st, _Pending) and 0 < k < rank and tuple(dims) == tuple(range(rank - k, rank)):
+            # its trailing dimensions: one kernel, a block per row, no stores
+            prog, slots, kinds = self._program(src)
+            out = self.slot(node.name)
+            self.steps.append(_FusedReduceRowsStep(out, prog, slots, kinds, self._shape(src), k,
+                                                   body, init, self._shape(node)))
             self.state[node] = _Leaf(out, "packed", False)
             return
         if isinstance(st, _Leaf) and st.kind == "f64":

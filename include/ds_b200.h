@@ -369,6 +369,26 @@ DS_API int ds_fused_reduce_compile_check(const ds_fused_op* ops, int32_t n_ops,
                                          const ds_buffer* const* inputs, int32_t n_inputs,
                                          const int64_t* dims, int32_t rank, int32_t body);
 
+/* The same reduction over the trailing `n_reduced` dimensions of `dims`
+   only: one DS value per row of the leading dimensions, written to
+   out_hi / out_lo (f32, one element per row, row-major), each
+   body(init, row total) -- the pass's reduce of an elementwise DAG over its
+   last dimensions (DsTransformPass.cpp:376-448) without writing the DAG's
+   values.  A block (256 threads for rows of at least 2048 values, else 32)
+   folds a whole row, so the order is fixed per row length.  No workspace. */
+DS_API int ds_fused_reduce_rows(const ds_fused_op* ops, int32_t n_ops,
+                                const int32_t* input_types, const ds_buffer* const* inputs,
+                                int32_t n_inputs, const int64_t* dims, int32_t rank,
+                                int32_t n_reduced, int32_t body, const ds_buffer* init_hi,
+                                const ds_buffer* init_lo, const ds_buffer* out_hi,
+                                const ds_buffer* out_lo, void* stream);
+/* Generate and compile (NVRTC) the per-row kernel without running it. */
+DS_API int ds_fused_reduce_rows_compile_check(const ds_fused_op* ops, int32_t n_ops,
+                                              const int32_t* input_types,
+                                              const ds_buffer* const* inputs, int32_t n_inputs,
+                                              const int64_t* dims, int32_t rank,
+                                              int32_t n_reduced, int32_t body);
+
 /* ---- diagnostics (no reference counterpart) ------------------------------ */
 
 /* Per-kernel GPU time.  While enabled, each op brackets its main kernel with

@@ -134,3 +134,68 @@ def test_dstensor_sum_uses_one_kernel(dso):
     X = dso.ds_from_f64(x)
     Z = dso.ds_mul(dso.ds_add(X, dso.ds_from_f64(y)), X)
     check_sum([s.packed[0], s.packed[1]], Z, dso)
+
+
+# ---- reductions over the trailing dimensions (ds_fused_reduce_rows) ----
+
+
+def check_rows(hi, lo, Z, dso, init=(0.0, 0.0)):
+    """Each row's result against the exact sum of its DS values plus init."""
+    got = host(hi).astype(np.float64) + host(lo).astype(np.float64)
+    rows = Z.reshape(got.size, -1, 2)
+    for r, g in zip(rows, got.ravel()):
+        vals = np.concatenate([r[:, 0].astype(np.float64), r[:, 1].astype(np.float64),
+                               np.array(init, np.float64)])
+        truth = exact.exact_sum(vals)
+        h, l = dso.ds_reduce_ds_seq(r[:, 0], r[:, 1], "add", init)
+        ref_err = abs(float(h) + float(l) - truth)
+        bound = ds_bound(r[:, 0].astype(np.float64)) if r.shape[0] else 0.0
+        assert abs(g - truth) <= max(4 * ref_err, bound), (g, truth, ref_err)
+
+
+@pytest.mark.parametrize("shape,k", [((37, 3001), 1), ((5, 4096), 1), ((3, 7, 300), 2),
+                                     ((1000, 3), 1), ((2, 3, 4), 3)])
+def test_rows_add_mul_sum(fuse, dso, shape, k):
+    """sum over the last k dimensions of (a + b) * c: warp-per-row and
+    block-per-row kernels, several rank-k tails."""
+    rng = np.random.default_rng(sum(shape) + k)
+    a, b, c = (rng.uniform(-1, 1, shape) for _ in range(3))
+    p = fuse.Prepared([(I, 0, 0, 0.0), (I, 1, 0, 0.0), (ADD, 0, 1, 0.0), (I, 2, 0, 0.0),
+                       (MUL, 2, 3, 0.0)], ["f64"] * 3, "packed")
+    hi, lo = p.reduce_rows([cu(a), cu(b), cu(c)], shape, k)
+    assert tuple(hi.shape) == shape[:len(shape) - k]
+    Z = dso.ds_mul(dso.ds_add(dso.ds_from_f64(a), dso.ds_from_f64(b)), dso.ds_from_f64(c))
+    check_rows(hi, lo, Z, dso)
+
+
+def test_rows_broadcast_init_and_empty_rows(fuse, dso):
+    rng = np.random.default_rng(8)
+    x = rng.uniform(-1, 1, (64, 1))
+    y = rng.uniform(-1, 1, 2500).astype(np.float32)
+    p = fuse.Prepared([(I, 0, 0, 0.0), (I, 1, 0, 0.0), (MUL, 0, 1, 0.0)], ["f64", "f32"],
+                      "packed")
+    hi, lo = p.reduce_rows([cu(x), cu(y)], (64, 2500), 1, init=(0.5, 2.0 ** -30))
+    Z = dso.ds_mul(dso.ds_from_f64(np.broadcast_to(x, (64, 2500))),
+                   dso.ds_from_f32(np.broadcast_to(y, (64, 2500))))
+    check_rows(hi, lo, Z, dso, init=(0.5, 2.0 ** -30))
+    # rows of length 0 hold init, bit for bit
+    e = torch.zeros(4, 0, dtype=torch.float64, device="cuda")
+    q = fuse.Prepared([(I, 0, 0, 0.0)], ["f64"], "packed")
+    h0, l0 = q.reduce_rows([e], (4, 0), 1, init=(1.5, 2.0 ** -30))
+    assert np.all(host(h0) == 1.5) and np.all(host(l0) == np.float32(2.0 ** -30))
+
+
+def test_rows_product_body_and_determinism(fuse, dso):
+    rng = np.random.default_rng(9)
+    x = 1.0 + 1e-7 * rng.uniform(-1, 1, (16, 5000))
+    p = fuse.Prepared([(I, 0, 0, 0.0)], ["f64"], "packed")
+    hi, lo = p.reduce_rows([cu(x)], x.shape, 1, "mul", init=(2.0, 0.0))
+    first = (host(hi), host(lo))
+    hi2, lo2 = p.reduce_rows([cu(x)], x.shape, 1, "mul", init=(2.0, 0.0))
+    assert_bits_equal(host(hi2), first[0], "hi")
+    assert_bits_equal(host(lo2), first[1], "lo")
+    got = first[0].astype(np.float64) + first[1].astype(np.float64)
+    for i in range(16):
+        h, l = dso.ds_reduce_f64_seq(x[i], body="mul", init=(2.0, 0.0))
+        want = float(h) + float(l)
+        assert abs(got[i] - want) / abs(want) < 1e-12

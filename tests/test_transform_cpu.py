@@ -80,8 +80,18 @@ def oracle_backend(monkeypatch, dso):
         h, l = dso.ds_reduce_ds_seq(flat[:, 0], flat[:, 1], body, init)
         return torch.tensor(h), torch.tensor(l)
 
+    def reduce_rows_prepared(self, tensors, shape, n_reduced, body="add", init=(0.0, 0.0)):
+        vals = run_prepared(self, tensors, shape).numpy()
+        out_shape = tuple(shape)[:len(shape) - n_reduced]
+        rows = vals.reshape((int(np.prod(out_shape)), -1, 2))
+        res = [dso.ds_reduce_ds_seq(r[:, 0], r[:, 1], body, init) for r in rows]
+        hi = np.array([h for h, _ in res], np.float32).reshape(out_shape)
+        lo = np.array([l for _, l in res], np.float32).reshape(out_shape)
+        return torch.from_numpy(hi), torch.from_numpy(lo)
+
     monkeypatch.setattr(fuse.Prepared, "__call__", run_prepared)
     monkeypatch.setattr(fuse.Prepared, "reduce", reduce_prepared)
+    monkeypatch.setattr(fuse.Prepared, "reduce_rows", reduce_rows_prepared)
     monkeypatch.setattr(ops, "ds_reduce_packed", reduce_packed)
     monkeypatch.setattr(ops, "ds_reduce_from_f64", reduce_from_f64)
     monkeypatch.setattr(ops, "ds_dot_general_f64", dot_f64)
@@ -452,3 +462,38 @@ def test_default_parameters_are_baked_in(oracle_backend):
     assert_bits_equal(g(x).numpy(), dso.ds_to_f64(dso.ds_mul(P(dso, x), C(dso, 2.0, (6,)))), "default")
     assert_bits_equal(g(x, 0.5).numpy(), dso.ds_to_f64(dso.ds_mul(P(dso, x), C(dso, 0.5, (6,)))),
                       "given")
+
+
+def test_trailing_reduction_of_a_dag_is_one_kernel(oracle_backend):
+    """sum over the last dimensions of an elementwise DAG: ds_fused_reduce_rows;
+    over leading dimensions it still goes through a packed value."""
+    dso = oracle_backend
+
+    @tr.ds_transform
+    def f(a, b):
+        return (a * b - 1.0).sum(dim=-1), (a + b).sum(dim=(1, 2), keepdim=True), (a * a).sum(dim=0)
+
+    a, b = rand((3, 4, 5), 27), rand((3, 4, 5), 28)
+    plan = f.plan(a, b)
+    kinds = [type(st).__name__ for st in plan.steps]
+    assert kinds.count("_FusedReduceRowsStep") == 2 and kinds.count("_ReduceStep") == 1
+    assert "ds_fused_reduce_rows" in f.explain(a, b)
+    r1, r2, r0 = f(a, b)
+    A, B = P(dso, a), P(dso, b)
+    Z = dso.ds_sub(dso.ds_mul(A, B), C(dso, 1.0, (3, 4, 5))).reshape(12, 5, 2)
+    want = [dso.ds_reduce_ds_seq(z[:, 0], z[:, 1]) for z in Z]
+    assert_bits_equal(r1.numpy(), dso.ds_to_f64(np.array(want, np.float32)).reshape(3, 4), "rows")
+    assert r2.shape == (3, 1, 1) and r0.shape == (4, 5)
+    Y = dso.ds_add(A, B).reshape(3, 20, 2)
+    want2 = [dso.ds_reduce_ds_seq(y[:, 0], y[:, 1]) for y in Y]
+    assert_bits_equal(r2.numpy().ravel(), dso.ds_to_f64(np.array(want2, np.float32)), "keepdim")
+
+
+def test_row_reduce_kernels_compile():
+    I, A, M = _lib.DS_FUSED_INPUT, _lib.DS_FUSED_ADD, _lib.DS_FUSED_MUL
+    p = fuse.Prepared([(I, 0, 0, 0.0), (I, 1, 0, 0.0), (A, 0, 1, 0.0), (I, 2, 0, 0.0),
+                       (M, 2, 3, 0.0)], ["f64", "f64", "f32"], "packed")
+    p.reduce_rows_compile_check([(10, 100), (10, 100), (100,)], (10, 100), 1, "add")
+    p.reduce_rows_compile_check([(4, 5, 6), (4, 5, 6), (6,)], (4, 5, 6), 2, "mul")
+    with pytest.raises(_lib.DsInvalidArgument):
+        p.reduce_rows_compile_check([(10, 100), (10, 100), (100,)], (10, 100), 3, "add")
