@@ -165,14 +165,23 @@ class DSTensor:
 
     def sum(self, dimensions=None) -> "DSTensor":
         """DS sum over `dimensions` (default: all), the result kept as DS.
-        A pending expression summed over all its dimensions runs as one
-        kernel that never stores its values (ds_fused_reduce)."""
-        if self._packed is None and dimensions is None and len(self._shape) > 0:
+        A pending expression summed over all its dimensions, or over its
+        trailing ones, runs as one kernel that never stores its values
+        (ds_fused_reduce, ds_fused_reduce_rows)."""
+        rank = len(self._shape)
+        if self._packed is None and dimensions is None and rank > 0:
             prepared, tensors = _prepare(self._expr, self._leaves, "packed")
             hi, lo = prepared.reduce(tensors, self._shape, "add")
             return DSTensor(torch.stack([hi, lo], dim=-1))
+        dims = None if dimensions is None else tuple(sorted({int(d) % max(rank, 1)
+                                                              for d in dimensions}))
+        if self._packed is None and dims and 0 < len(dims) < rank and \
+                dims == tuple(range(rank - len(dims), rank)):
+            # the trailing dimensions of a pending expression: one kernel per row
+            prepared, tensors = _prepare(self._expr, self._leaves, "packed")
+            hi, lo = prepared.reduce_rows(tensors, self._shape, len(dims), "add")
+            return DSTensor(torch.stack([hi, lo], dim=-1))
         p = self.packed
-        dims = None if dimensions is None else tuple(dimensions)
         hi, lo = ops.ds_reduce_packed(p, dimensions=dims)
         return DSTensor(torch.stack([hi, lo], dim=-1))
 

@@ -199,3 +199,24 @@ def test_rows_product_body_and_determinism(fuse, dso):
         h, l = dso.ds_reduce_f64_seq(x[i], body="mul", init=(2.0, 0.0))
         want = float(h) + float(l)
         assert abs(got[i] - want) / abs(want) < 1e-12
+
+
+def test_dstensor_row_sum_uses_one_kernel(dso):
+    from ds_b200 import _lib
+    from ds_b200.dstensor import DSTensor
+    rng = np.random.default_rng(10)
+    x, y = rng.uniform(-1, 1, (40, 3000)), rng.uniform(-1, 1, 3000)
+    a = DSTensor.from_f64(cu(x))
+    expr = (a + cu(y)) * a
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    s = expr.sum(dimensions=(-1,))
+    torch.cuda.synchronize()
+    _lib.profile_enable(False)
+    assert _lib.profile_read("fused_reduce")[1] == 1
+    assert _lib.profile_read("fused")[1] == 0
+    assert s.shape == (40,)
+    X = dso.ds_from_f64(x)
+    Z = dso.ds_mul(dso.ds_add(X, dso.ds_from_f64(np.broadcast_to(y, x.shape))), X)
+    p = s.packed
+    check_rows(p[:, 0], p[:, 1], Z, dso)
