@@ -321,7 +321,26 @@ std::string generate(const Desc& d) {
 // shape: each block owns whole rows (grid-strided), its threads fold the
 // row's elements they visit, warp and block trees combine them, and thread 0
 // writes body(init, row total) -- init alone for an empty row.
+// Lanes that fold one row: a whole block for rows of at least 2048 values
+// (0 here), else the power of two nearest R / 8 (at least 1, at most 32),
+// so a lane folds about eight values before the group's shuffle tree.
+int rows_lanes(int64_t R) {
+  if (R >= 2048) return 0;
+  int L = 1;
+  while (L < 32 && static_cast<int64_t>(L) * 8 < R) L <<= 1;
+  return L;
+}
+
+int64_t rows_len(const Desc& d) {
+  int64_t R = 1;
+  for (int k = d.rank - d.rows_reduced; k < d.rank; ++k) R *= d.dims[k];
+  return R;
+}
+
+std::string generate_rows_groups(const Desc& d, int L);
+
 std::string generate_rows(const Desc& d) {
+  if (const int L = rows_lanes(rows_len(d))) return generate_rows_groups(d, L);
   const std::string body = d.reduce_body == DS_BODY_MUL ? "mul" : "add";
   const std::string ident = d.reduce_body == DS_BODY_MUL ? "ds2{1.0f, 0.0f}" : "ds2{0.0f, 0.0f}";
   const std::string last = std::to_string(d.ops.size() - 1);
@@ -363,6 +382,49 @@ std::string generate_rows(const Desc& d) {
   s += "      __syncthreads();  // part is refilled by the next row\n";
   s += "    }\n";
   s += "    if (threadIdx.x == 0) {\n";
+  s += "      const ds2 r = R == 0 ? init : " + body + "(init, acc);\n";
+  s += "      out_hi[row] = r.hi;\n      out_lo[row] = r.lo;\n    }\n";
+  s += "  }\n}\n";
+  return s;
+}
+
+// Short rows: groups of L lanes (L divides 32) each fold one row.  The row
+// loop advances a whole warp at a time so that every lane reaches every
+// shuffle; a group past the last row folds nothing and writes nothing.
+std::string generate_rows_groups(const Desc& d, int L) {
+  const std::string body = d.reduce_body == DS_BODY_MUL ? "mul" : "add";
+  const std::string ident = d.reduce_body == DS_BODY_MUL ? "ds2{1.0f, 0.0f}" : "ds2{0.0f, 0.0f}";
+  const std::string last = std::to_string(d.ops.size() - 1);
+  const std::string Ls = std::to_string(L), gpw = std::to_string(32 / L);
+  std::string s;
+  s += kDsArithSource;
+  s += "\nusing namespace dsb;\n";
+  s += "extern \"C\" __global__ void __launch_bounds__(256) ds_fused_kernel(";
+  for (size_t k = 0; k < d.in.size(); ++k)
+    s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
+         ", ";
+  s += "float* __restrict__ out_hi, float* __restrict__ out_lo, const float* __restrict__ init_hi, "
+       "const float* __restrict__ init_lo, long long rows, long long R) {\n";
+  s += "  const ds2 init = ds2{*init_hi, *init_lo};\n";
+  s += "  const int lane = threadIdx.x & 31, sub = lane % " + Ls + ";\n";
+  s += "  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;\n";
+  s += "  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;\n";
+  s += "  for (long long base = wid * " + gpw + "; base < rows; base += nw * " + gpw + ") {\n";
+  s += "    const long long row = base + lane / " + Ls + ";\n";
+  s += "    ds2 acc = " + ident + ";\n";
+  s += "    if (row < rows) {\n";
+  s += "      for (long long j = sub; j < R; j += " + Ls + ") {\n";
+  s += "        const long long i = row * R + j;\n";
+  s += program_body(d, "", [&](int k) {
+    const InputView& in = d.in[k];
+    return from_value(in.type, "__ldg(in" + std::to_string(k) + " + (" + index_expr(d, in) + "))");
+  });
+  s += "        acc = " + body + "(acc, v" + last + ");\n      }\n    }\n";
+  s += "    for (int o = " + std::to_string(L / 2) + "; o > 0; o >>= 1) {\n";
+  s += "      const ds2 t = ds2{__shfl_xor_sync(0xffffffffu, acc.hi, o), "
+       "__shfl_xor_sync(0xffffffffu, acc.lo, o)};\n";
+  s += "      acc = " + body + "(acc, t);\n    }\n";
+  s += "    if (sub == 0 && row < rows) {\n";
   s += "      const ds2 r = R == 0 ? init : " + body + "(init, acc);\n";
   s += "      out_hi[row] = r.hi;\n      out_lo[row] = r.lo;\n    }\n";
   s += "  }\n}\n";
@@ -767,10 +829,14 @@ int ds_fused_reduce_rows(const ds_fused_op* ops, int32_t n_ops, const int32_t* i
   long long nrows = rows, len = row_len;
   args[n_inputs + 4] = &nrows;
   args[n_inputs + 5] = &len;
-  // long rows: a block of 256 per row; short ones: a warp per row
-  const unsigned threads = row_len >= 2048 ? 256u : 32u;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * (threads == 256u ? 8 : 32);
-  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  // long rows: a block of 256 per row; short ones: groups of L lanes per
+  // row, 256 / L rows per block
+  const int L = rows_lanes(row_len);
+  const unsigned threads = 256u;
+  const int64_t per_block = L ? 256 / L : 1;
+  const int64_t need = (rows + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
   ProfileScope prof("fused_reduce", static_cast<cudaStream_t>(stream));
   if (driver().launch(fn, grid, 1, 1, threads, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
                       nullptr) != CUDA_SUCCESS)

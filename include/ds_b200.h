@@ -374,8 +374,9 @@ DS_API int ds_fused_reduce_compile_check(const ds_fused_op* ops, int32_t n_ops,
    out_hi / out_lo (f32, one element per row, row-major), each
    body(init, row total) -- the pass's reduce of an elementwise DAG over its
    last dimensions (DsTransformPass.cpp:376-448) without writing the DAG's
-   values.  A block (256 threads for rows of at least 2048 values, else 32)
-   folds a whole row, so the order is fixed per row length.  No workspace. */
+   values.  A block of 256 threads folds each row of at least 2048 values;
+   shorter rows are folded by groups of 1-32 lanes (about eight values per
+   lane), so the order is fixed per row length.  No workspace. */
 DS_API int ds_fused_reduce_rows(const ds_fused_op* ops, int32_t n_ops,
                                 const int32_t* input_types, const ds_buffer* const* inputs,
                                 int32_t n_inputs, const int64_t* dims, int32_t rank,

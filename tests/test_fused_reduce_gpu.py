@@ -154,10 +154,11 @@ def check_rows(hi, lo, Z, dso, init=(0.0, 0.0)):
 
 
 @pytest.mark.parametrize("shape,k", [((37, 3001), 1), ((5, 4096), 1), ((3, 7, 300), 2),
-                                     ((1000, 3), 1), ((2, 3, 4), 3)])
+                                     ((1000, 3), 1), ((2, 3, 4), 3), ((513, 64), 1),
+                                     ((300, 200), 1), ((7, 1000), 1), ((4099, 9), 1)])
 def test_rows_add_mul_sum(fuse, dso, shape, k):
-    """sum over the last k dimensions of (a + b) * c: warp-per-row and
-    block-per-row kernels, several rank-k tails."""
+    """sum over the last k dimensions of (a + b) * c: rows folded by a block,
+    a warp or smaller lane groups (1 to 16 lanes), several rank-k tails."""
     rng = np.random.default_rng(sum(shape) + k)
     a, b, c = (rng.uniform(-1, 1, shape) for _ in range(3))
     p = fuse.Prepared([(I, 0, 0, 0.0), (I, 1, 0, 0.0), (ADD, 0, 1, 0.0), (I, 2, 0, 0.0),
