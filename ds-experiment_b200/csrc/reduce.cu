@@ -310,7 +310,7 @@ reduce_partials_kernel(const ds2* __restrict__ partials, int g, int body, Dst ds
   if (threadIdx.x == 0) dst.put(0, finish(body, load_init(init_f64, init_hi, init_lo), acc));
 }
 
-// inner == 1, outer > 1: one block per row.
+// inner == 1, outer > 1, rows of at least kRowsBlockMin values: one block per row.
 __global__ void __launch_bounds__(kThreads)
 reduce_rows_kernel(Src src, int64_t outer, int64_t red, int body, Dst dst,
                    const double* init_f64, const float* init_hi, const float* init_lo) {
@@ -324,6 +324,41 @@ reduce_rows_kernel(Src src, int64_t outer, int64_t red, int body, Dst dst,
     acc = block_combine(is_mul, acc);
     if (threadIdx.x == 0) dst.put(row, red == 0 ? init : finish(body, init, acc));
     __syncthreads();
+  }
+}
+
+// inner == 1, rows shorter than kRowsBlockMin: groups of `lanes` lanes (a
+// power of two up to 32, about eight values per lane) fold one row each.
+// The row loop advances a warp at a time, so every lane reaches every
+// shuffle; a group past the last row folds nothing and writes nothing.
+constexpr int64_t kRowsBlockMin = 2048;
+
+int rows_lanes(int64_t red) {
+  int lanes = 1;
+  while (lanes < 32 && static_cast<int64_t>(lanes) * 8 < red) lanes <<= 1;
+  return lanes;
+}
+
+__global__ void __launch_bounds__(kThreads)
+reduce_rows_groups_kernel(Src src, int64_t outer, int64_t red, int lanes, int body, Dst dst,
+                          const double* init_f64, const float* init_hi, const float* init_lo) {
+  const bool is_mul = body == 2;
+  const ds2 init = load_init(init_f64, init_hi, init_lo);
+  const int lane = threadIdx.x & 31, sub = lane % lanes, per_warp = 32 / lanes;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t base = wid * per_warp; base < outer; base += nw * per_warp) {
+    const int64_t row = base + lane / lanes;
+    ds2 acc = identity(is_mul);
+    if (row < outer) {
+      const int64_t off = row * red;
+      for (int64_t r = sub; r < red; r += lanes) acc = combine(is_mul, acc, src.at(off + r));
+    }
+    for (int o = lanes >> 1; o > 0; o >>= 1) {
+      const ds2 t{__shfl_xor_sync(0xffffffffu, acc.hi, o), __shfl_xor_sync(0xffffffffu, acc.lo, o)};
+      acc = combine(is_mul, acc, t);
+    }
+    if (sub == 0 && row < outer) dst.put(row, red == 0 ? init : finish(body, init, acc));
   }
 }
 
@@ -432,7 +467,16 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
     return launch_status();
   }
   if (inner == 1) {
-    const unsigned g = static_cast<unsigned>(outer < sm_count() * 8 ? outer : sm_count() * 8);
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    if (red < kRowsBlockMin) {
+      const int lanes = rows_lanes(red);
+      const int64_t need = (outer + kThreads / lanes - 1) / (kThreads / lanes);
+      const unsigned g = static_cast<unsigned>(need < cap ? need : cap);
+      reduce_rows_groups_kernel<<<g, kThreads, 0, s>>>(src, outer, red, lanes, a.body, dst,
+                                                       a.init_f64, a.init_hi, a.init_lo);
+      return launch_status();
+    }
+    const unsigned g = static_cast<unsigned>(outer < cap ? outer : cap);
     reduce_rows_kernel<<<g, kThreads, 0, s>>>(src, outer, red, a.body, dst, a.init_f64,
                                               a.init_hi, a.init_lo);
     return launch_status();
