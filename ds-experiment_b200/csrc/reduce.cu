@@ -380,6 +380,35 @@ reduce_cols_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body,
   }
 }
 
+// inner > 1 with too few columns to fill the GPU one thread each: a block
+// owns 32 adjacent columns, its 8 warps split the reduced dimension (warp w
+// folds positions w, w + 8, ...; loads stay coalesced along the columns),
+// and the 8 partials of a column are folded in warp order.
+__global__ void __launch_bounds__(kThreads)
+reduce_cols_tile_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body, Dst dst,
+                        const double* init_f64, const float* init_hi, const float* init_lo) {
+  __shared__ ds2 part[kThreads / 32][32];
+  const bool is_mul = body == 2;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t cols = outer * inner;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * 32 + tx;
+  ds2 acc = identity(is_mul);
+  if (c < cols) {
+    const int64_t o = c / inner, j = c - o * inner;
+    const int64_t off = o * red * inner + j;
+    for (int64_t r = ty; r < red; r += kThreads / 32)
+      acc = combine(is_mul, acc, src.at(off + r * inner));
+  }
+  part[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    ds2 t = part[0][tx];
+    for (int w = 1; w < kThreads / 32; ++w) t = combine(is_mul, t, part[w][tx]);
+    const ds2 init = load_init(init_f64, init_hi, init_lo);
+    dst.put(c, red == 0 ? init : finish(body, init, t));
+  }
+}
+
 }  // namespace
 
 int reduce_full_blocks(int64_t n) {
@@ -479,6 +508,12 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
     const unsigned g = static_cast<unsigned>(outer < cap ? outer : cap);
     reduce_rows_kernel<<<g, kThreads, 0, s>>>(src, outer, red, a.body, dst, a.init_f64,
                                               a.init_hi, a.init_lo);
+    return launch_status();
+  }
+  if (outer * inner < static_cast<int64_t>(sm_count()) * kThreads * 8) {
+    const int64_t tiles = (outer * inner + 31) / 32;
+    reduce_cols_tile_kernel<<<static_cast<unsigned>(tiles), kThreads, 0, s>>>(
+        src, outer, red, inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
     return launch_status();
   }
   reduce_cols_kernel<<<grid_for(outer * inner, kThreads, 8), kThreads, 0, s>>>(
