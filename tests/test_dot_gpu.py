@@ -180,3 +180,35 @@ def test_long_contraction_runs_in_chunks(ops):
     got = host(ops.ds_matmul_f64(cu(A), cu(B)))
     assert np.all(np.isinf(got[3]) | np.isnan(got[3]))
     assert np.all(np.isfinite(np.delete(got, 3, axis=0)))
+
+
+_ONE_CTA_CHILD = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+from ds_b200 import _lib, ops
+assert _lib.gemm_kernel_info()["kernel"] == "single_cta"
+rng = np.random.default_rng(31)
+A, B = rng.uniform(-1, 1, (512, 1000)), rng.uniform(-1, 1, (1000, 768))
+C = ops.ds_matmul_f64(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+sys.stdout.buffer.write(C.cpu().numpy().tobytes())
+"""
+
+
+def test_single_cta_kernel_gives_the_pair_kernels_bits(ops):
+    """The one-CTA GEMM (taken when a device cannot co-schedule CTA pairs;
+    DS_B200_GEMM_1CTA=1 forces it) computes the same exact residue products,
+    so the result equals the pair kernel's bit for bit."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG_DIR, ROOT
+    rng = np.random.default_rng(31)
+    A, B = rng.uniform(-1, 1, (512, 1000)), rng.uniform(-1, 1, (1000, 768))
+    want = host(ops.ds_matmul_f64(cu(A), cu(B)))
+    env = dict(os.environ, DS_B200_GEMM_1CTA="1")
+    out = subprocess.run([sys.executable, "-c", _ONE_CTA_CHILD, PKG_DIR, ROOT], env=env,
+                         capture_output=True, timeout=600)
+    assert out.returncode == 0, out.stderr.decode()[-2000:]
+    got = np.frombuffer(out.stdout, dtype=np.float64).reshape(want.shape)
+    assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+    check_gemm(got, A, B)
