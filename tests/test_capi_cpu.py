@@ -202,3 +202,34 @@ def test_fused_reduce_argument_errors(L):
     bad = (ctypes.c_int64 * 1)(9)
     st, msg = call(ws=ctypes.c_void_p(0x100000), nbytes=need, d=bad)
     assert st == L.DS_INVALID_ARGUMENT and "broadcast" in msg
+
+
+def test_fused_reduce_rows_argument_errors(L):
+    """ds_fused_reduce_rows checks its body, reduced dimensions, buffers and
+    output shape before any launch."""
+    r = ctypes.byref
+    ops = (L.DsFusedOp * 1)(L.DsFusedOp(L.DS_FUSED_INPUT, 0, 0, 0, 0.0))
+    x, _1 = _b(L, (4, 8))
+    arr = (ctypes.POINTER(L.DsBuffer) * 1)(ctypes.pointer(x))
+    ty = (ctypes.c_int32 * 1)(L.DS_FUSED_F64)
+    dims = (ctypes.c_int64 * 2)(4, 8)
+    s, _2 = _b(L, ())
+    o4, _3 = _b(L, (4,))
+    o5, _4 = _b(L, (5,))
+    lib = L.lib()
+
+    def call(body=L.DS_BODY_ADD, k=1, out=o4, init=s):
+        st = lib.ds_fused_reduce_rows(ops, 1, ty, arr, 1, dims, 2, k, body, r(init), r(s),
+                                      r(out), r(out), None)
+        return st, L.last_error()
+    st, msg = call(body=L.DS_BODY_SUB)
+    assert st == L.DS_INVALID_ARGUMENT and "DS_BODY_ADD or DS_BODY_MUL" in msg
+    st, msg = call(k=0)
+    assert st == L.DS_INVALID_ARGUMENT and "trailing dimensions" in msg
+    st, msg = call(k=3)
+    assert st == L.DS_INVALID_ARGUMENT and "trailing dimensions" in msg
+    st, msg = call(out=o5)
+    assert st == L.DS_INVALID_ARGUMENT and "one value per row" in msg
+    null, _5 = _b(L, (), ptr=0)
+    st, msg = call(init=null)
+    assert st == L.DS_INVALID_ARGUMENT and "null" in msg
