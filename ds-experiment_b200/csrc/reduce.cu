@@ -409,6 +409,50 @@ reduce_cols_tile_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int 
   }
 }
 
+// The tile kernel's first stage when a few columns have long reductions:
+// grid (tiles, slices); block (x, s) folds rows [s * chunk, (s + 1) * chunk)
+// of its 32 columns (8 warps, as above) and writes the slice's DS partial
+// per column to partials[s * cols + c], without init.
+__global__ void __launch_bounds__(kThreads)
+reduce_cols_split_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int64_t chunk,
+                         int body, ds2* __restrict__ partials) {
+  __shared__ ds2 part[kThreads / 32][32];
+  const bool is_mul = body == 2;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t cols = outer * inner;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * 32 + tx;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * chunk;
+  const int64_t r1 = r0 + chunk < red ? r0 + chunk : red;
+  ds2 acc = identity(is_mul);
+  if (c < cols) {
+    const int64_t o = c / inner, j = c - o * inner;
+    const int64_t off = o * red * inner + j;
+    for (int64_t r = r0 + ty; r < r1; r += kThreads / 32)
+      acc = combine(is_mul, acc, src.at(off + r * inner));
+  }
+  part[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    ds2 t = part[0][tx];
+    for (int w = 1; w < kThreads / 32; ++w) t = combine(is_mul, t, part[w][tx]);
+    partials[static_cast<int64_t>(blockIdx.y) * cols + c] = t;
+  }
+}
+
+// Slices of the reduced dimension for the split column reduction: enough
+// blocks to fill the GPU, at least 1024 rows a slice, at most 512 slices;
+// 1 (no split) when the columns alone fill it or the rows are short.
+int64_t cols_slices(int64_t outer, int64_t red, int64_t inner) {
+  if (inner <= 1) return 1;
+  const int64_t tiles = (outer * inner + 31) / 32;
+  const int64_t want = static_cast<int64_t>(sm_count()) * 8;
+  if (tiles >= want / 2 || red < 4096) return 1;
+  int64_t sl = (want + tiles - 1) / tiles;
+  if (sl > red / 1024) sl = red / 1024;
+  if (sl > 512) sl = 512;
+  return sl < 2 ? 1 : sl;
+}
+
 }  // namespace
 
 int reduce_full_blocks(int64_t n) {
@@ -416,6 +460,10 @@ int reduce_full_blocks(int64_t n) {
 }
 
 size_t reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {
+  if (inner > 1) {
+    const int64_t sl = cols_slices(outer, red, inner);
+    return sl > 1 ? static_cast<size_t>(sl * outer * inner) * sizeof(ds2) : 0;
+  }
   if (outer != 1 || inner != 1) return 0;
   const int g = reduce_full_blocks(red);
   return g > 1 ? static_cast<size_t>(g) * sizeof(ds2) : 0;
@@ -512,6 +560,23 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
   }
   if (outer * inner < static_cast<int64_t>(sm_count()) * kThreads * 8) {
     const int64_t tiles = (outer * inner + 31) / 32;
+    const int64_t sl = cols_slices(outer, red, inner);
+    const size_t need = static_cast<size_t>(sl * outer * inner) * sizeof(ds2);
+    if (sl > 1 && a.workspace && a.workspace_bytes >= need && aligned(a.workspace, alignof(ds2))) {
+      // long reductions over few columns: slices in parallel, then the
+      // slices' partials folded in slice order with init (a workspace too
+      // small for them keeps the one-stage kernel below)
+      ds2* partials = static_cast<ds2*>(a.workspace);
+      const int64_t chunk = (red + sl - 1) / sl;
+      reduce_cols_split_kernel<<<dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(sl)),
+                                 kThreads, 0, s>>>(src, outer, red, inner, chunk, a.body,
+                                                   partials);
+      if (int st = launch_status()) return st;
+      Src ps{nullptr, reinterpret_cast<const float*>(partials), nullptr, false, true};
+      reduce_cols_tile_kernel<<<static_cast<unsigned>(tiles), kThreads, 0, s>>>(
+          ps, 1, sl, outer * inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
+      return launch_status();
+    }
     reduce_cols_tile_kernel<<<static_cast<unsigned>(tiles), kThreads, 0, s>>>(
         src, outer, red, inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
     return launch_status();

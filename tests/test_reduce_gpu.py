@@ -173,7 +173,9 @@ def test_nan_inf_propagate(ops):
 
 @pytest.mark.parametrize("shape,dims", [((37, 1000), (1,)), ((1000, 37), (0,)),
                                         ((6, 50, 7), (1,)), ((4, 3, 500), (1, 2)),
-                                        ((300, 2), (0, 1))])
+                                        ((300, 2), (0, 1)), ((1 << 18, 8), (0,)),
+                                        ((20000, 3, 5), (0,)), ((2, 9000, 4), (1,)),
+                                        ((3000, 64), (1,))])
 def test_segmented(ops, shape, dims):
     rng = np.random.default_rng(sum(shape))
     x = rng.uniform(-1, 1, shape) * 1e6 + rng.uniform(0, 1, shape) * 1e-6
