@@ -172,7 +172,11 @@ DS_API int ds_recurrence_mul_add_to_f64(const ds_buffer* x, const ds_buffer* a,
    ds_op(acc, elem).  Elements are folded per thread in index order, then in
    a fixed shuffle/block tree, then block partials in block order, so results
    are deterministic for a given shape; init is applied once, last
-   (subtract: init - sum; add: init + sum; multiply: init * product). */
+   (subtract: init - sum; add: init + sum; multiply: init * product).
+   The workspace (ds_reduce_workspace_size bytes) holds block partials: a
+   full reduction needs it; a reduction over a leading dimension with few
+   columns uses it to slice the reduced dimension across blocks, and runs
+   in one stage without it; other reductions need none. */
 DS_API size_t ds_reduce_workspace_size(const ds_buffer* in, const int64_t* dimensions,
                                 int64_t n_dimensions);
 DS_API int ds_reduce(const ds_buffer* in_hi, const ds_buffer* in_lo,
