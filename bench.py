@@ -242,7 +242,7 @@ def run_ours(args):
     k_ms, k_n = _lib.profile_read(fam)
     launches = {}
     for f in ("ozaki_split", "ozaki_split_rows", "ozaki_colmax", "ozaki_split_rows_colmax",
-              "ozaki_split_cols", "ozaki_gemm", "ozaki_crt",
+              "ozaki_split_cols", "ozaki_gemm", "ozaki_crt", "ozaki_fix",
               "dot_simt", "dot_vec", "elementwise",
               "reduce", "recurrence"):
         t, n = _lib.profile_read(f)

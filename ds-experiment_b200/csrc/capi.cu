@@ -94,7 +94,7 @@ int packed_binary(const char* op, int which, const ds_buffer* a, const ds_buffer
 }
 
 // Shape checks of the rank-1 fused handlers (cpp/ds_fused_add_mul_to_f64.cpp:
-// 265-274): rank-1 inputs of equal length, output [N] (or [N,2] when packed).
+// 77-86): rank-1 inputs of equal length, output [N] (or [N,2] when packed).
 int fused_checks(const char* op, std::initializer_list<const ds_buffer*> ins,
                  const ds_buffer* out, bool packed_out) {
   std::vector<const ds_buffer*> all(ins);

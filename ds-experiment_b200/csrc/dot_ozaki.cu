@@ -61,6 +61,9 @@ constexpr int kGemmThreads = 192;
 // u8 x u8 products summed in int32: K * 255^2 < 2^31 needs K <= 33025.
 constexpr int kMaxK = 1 << 15;
 constexpr int kShiftNonFinite = INT_MIN;
+// Shift code of a row (column) whose values are all zero: its products are
+// exactly zero, so its outputs need no error certificate.
+constexpr int kShiftZero = INT_MIN + 1;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 __host__ __device__ constexpr int mod_of(int l) {
@@ -121,9 +124,15 @@ int bits_for_k(int64_t K) {
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+// Uncertified outputs (see the CRT step) are listed, up to kFixListMax of
+// them, for a warp each; with more, every output is recomputed.
+constexpr int64_t kFixListMax = 1 << 20;
+constexpr int kFixTile = 64;
+
 struct Layout {
   int64_t batch, M, N, K, Mp, Np, Kp;
-  size_t off_a, off_b, off_c, off_sa, off_sb, off_ca, off_cb, off_err, total;
+  size_t off_a, off_b, off_c, off_sa, off_sb, off_ca, off_cb, off_err, off_fix_list, total;
+  int64_t fix_cap;
 };
 
 Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
@@ -148,7 +157,10 @@ Layout layout_of(int64_t batch, int64_t M, int64_t N, int64_t K) {
   g.off_sb = take(sizeof(int) * batch * g.Np);
   g.off_ca = take(sizeof(int) * batch * g.Mp);
   g.off_cb = take(sizeof(int) * batch * g.Np);
+  // error word ([0]) and the count of uncertified outputs ([1])
   g.off_err = take(sizeof(int) * 4);
+  g.fix_cap = batch * M * N < kFixListMax ? batch * M * N : kFixListMax;
+  g.off_fix_list = take(sizeof(uint64_t) * static_cast<size_t>(g.fix_cap));
   g.total = off;
   return g;
 }
@@ -337,7 +349,7 @@ __device__ __forceinline__ void store_planes_16_rt(const Limbs (&x)[16], uint8_t
 
 __device__ __forceinline__ int shift_for(double mx, bool nonfinite, int P) {
   if (nonfinite) return kShiftNonFinite;
-  if (mx == 0.0) return 0;
+  if (mx == 0.0) return kShiftZero;
   return P - (ilogb(mx) + 1);  // |v| <= mx < 2^(ilogb+1)
 }
 
@@ -348,7 +360,7 @@ constexpr int kExpNonFinite = 0x7FFFFFFF;
 
 __device__ __forceinline__ int shift_from_code(int code, int P) {
   if (code == kExpNonFinite) return kShiftNonFinite;
-  if (code == 0) return 0;
+  if (code == 0) return kShiftZero;
   return P - (code - kExpBias);
 }
 
@@ -427,7 +439,7 @@ __device__ __forceinline__ void split_rows_body(const DotOperand& o, int64_t row
   }
   const int shift = live ? shift_for(mx, bad, P) : 0;
   if (threadIdx.x == 0) shifts[b * rows_pad + r] = shift;
-  const bool zero = !live || shift == kShiftNonFinite;
+  const bool zero = !live || shift == kShiftNonFinite || shift == kShiftZero;
   const int sh = zero ? 0 : shift;
   const size_t plane_stride = static_cast<size_t>(batch) * rows_pad * Kp;
   uint8_t* row_out = planes + (static_cast<size_t>(b) * rows_pad + r) * Kp;
@@ -623,7 +635,8 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
   for (int i = 0; i < 8; ++i)
     load_row_pair(o, paired, b, r0 + 2 * lane, kc + warp + 8 * i, rows, K, x[i][0], x[i][1]);
   const int sh0 = s_shift[2 * lane], sh1 = s_shift[2 * lane + 1];
-  const bool z0 = sh0 == kShiftNonFinite, z1 = sh1 == kShiftNonFinite;
+  const bool z0 = sh0 == kShiftNonFinite || sh0 == kShiftZero;
+  const bool z1 = sh1 == kShiftNonFinite || sh1 == kShiftZero;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint64_t t0 = quantise(z0 ? 0.0 : x[i][0], z0 ? 0 : sh0);
@@ -1261,6 +1274,13 @@ struct CrtParams {
   double w[kL][2];
   double mlimb[2];
   double inv_m;
+  // Outputs whose rebuilt integer |C_int| lies below this bound are not
+  // certified by the quantisation error bound and are recomputed (below).
+  double certify_below;
+  int P;
+  int* fix_count;      // err[1]
+  uint64_t* fix_list;  // [fix_cap] flat output indices
+  int64_t fix_cap;
   int64_t batch, M, N, Mp, Np, K;
   int64_t row_begin, row_end;  // rows of the flattened [batch * M] output this launch covers
   const uint8_t* cres;
@@ -1295,6 +1315,19 @@ __device__ __forceinline__ double byte_to_f64(uint32_t word, int q) {
 __device__ __forceinline__ double pow2_normal(int e) {
   return __longlong_as_double(static_cast<long long>(1023 + e) << 52);
 }
+
+// Error certificate.  A row of A enters the GEMM as a_int = rint(a 2^sa)
+// with |a_int| <= 2^P, so |a 2^sa - a_int| <= 1/2; likewise for B.  In units
+// of C_int the quantisation error of an output is at most
+//     (||b_int||_1 + ||a_int||_1) / 2 + K / 4 <= K 2^P (+ K / 4),
+// and the CRT's low limb adds below 2^34.  An output is certified when
+// |C_int| >= 2^24 (K 2^P + 2^35): its error is then at most 2^-24 |C| (in
+// practice far less: the quantisation errors are not aligned).  This bound
+// is relative to the row maximum of A and the column maximum of B, so it
+// fails exactly where those maxima do not take part in the output: a large
+// entry facing zeros, values spread over many binades, or cancellation.
+// Such outputs are recomputed with a compensated dot product (fix_kernel).
+constexpr int kCertifyBits = 24;
 
 // blockIdx.x * 512 is the first column of the block; blockIdx.y strides over
 // the batch*M output rows, so each thread rebuilds 4 consecutive outputs of
@@ -1355,6 +1388,8 @@ crt_kernel(CrtParams p) {
           s += op_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
                op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
         out = s;
+      } else if (sa == kShiftZero || sb == kShiftZero) {
+        out = 0.0;  // a row or column of zeros
       } else {
         // C = S - round(S / Mprod) * Mprod: the quotient is exact (S / Mprod
         // lies within 0.22 of an integer), the high limb difference is an
@@ -1365,12 +1400,216 @@ crt_kernel(CrtParams p) {
         const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi[q]);
         const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo[q]);
         const double c = __fma_rn(t_hi, 0x1p70, t_lo);
+        if (!(fabs(c) >= p.certify_below)) {
+          // uncertified: listed for fix_kernel, which writes this output
+          const int slot = atomicAdd(p.fix_count, 1);
+          if (slot < p.fix_cap) p.fix_list[slot] = static_cast<uint64_t>(row * p.N + j);
+          continue;
+        }
         // scale by 2^-(sa + sb): one exact multiply when 2^-(sa+sb) is normal
         const int e = -(sa + sb);
         out = (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sb);
       }
       put_result(p.c, row * p.N + j, out);
     }
+  }
+}
+
+// ---- recomputation of uncertified outputs ----------------------------------
+//
+// sum_k a_ik b_kj by Ogita, Rump and Oishi's Dot2: each product split exactly
+// by an FMA, the products summed with two_sum and the error terms summed
+// aside, which is as accurate as the dot product evaluated in twice the
+// working precision and then rounded.  Operands are scaled by 2^(sa - P) and
+// 2^(sb - P) (below 1 in magnitude, so no product overflows); the scaling is
+// undone at the end.
+
+struct Dot2 {
+  double p = 0.0, s = 0.0;
+};
+
+__device__ __forceinline__ void two_sum64(double a, double b, double& s, double& e) {
+  s = __dadd_rn(a, b);
+  const double bb = __dsub_rn(s, a);
+  e = __dadd_rn(__dsub_rn(a, __dsub_rn(s, bb)), __dsub_rn(b, bb));
+}
+
+__device__ __forceinline__ void dot2_add(Dot2& d, double x, double y) {
+  const double h = __dmul_rn(x, y);
+  const double r = __fma_rn(x, y, -h);
+  double q;
+  two_sum64(d.p, h, d.p, q);
+  d.s = __dadd_rn(d.s, __dadd_rn(q, r));
+}
+
+__device__ __forceinline__ void dot2_merge(Dot2& d, const Dot2& o) {
+  double q;
+  two_sum64(d.p, o.p, d.p, q);
+  d.s = __dadd_rn(__dadd_rn(d.s, o.s), q);
+}
+
+struct FixParams {
+  DotOperand a, b;
+  DotResult c;
+  int64_t batch, M, N, Mp, Np, K;
+  int P;
+  const int* sa;
+  const int* sb;
+  const int* err;  // [0] error word, [1] uncertified outputs
+  const uint64_t* list;
+  int64_t cap;
+};
+
+constexpr int kFixThreads = 256;
+constexpr int kFixChains = 8;
+
+// One output by one block: thread t owns k = t + 256 (8 n + u) in chain u
+// (eight chains keep sixteen loads in flight), the chains are merged in a
+// fixed tree, then the lanes of each warp, then the warps in order, so the
+// result is deterministic.  Returns it on thread 0.
+__device__ double dot2_block(const FixParams& p, int64_t b, int64_t i, int64_t j, int da, int db) {
+  __shared__ Dot2 s_warp[kFixThreads / 32];
+  const int64_t abase = b * p.a.s_b + i * p.a.s_r, bbase = b * p.b.s_b + j * p.b.s_r;
+  constexpr int64_t kStep = static_cast<int64_t>(kFixThreads) * kFixChains;
+  Dot2 ch[kFixChains];
+  int64_t k = threadIdx.x;
+  for (; k + (kFixChains - 1) * kFixThreads < p.K; k += kStep) {
+    double x[kFixChains], y[kFixChains];
+#pragma unroll
+    for (int u = 0; u < kFixChains; ++u) {
+      x[u] = op_value(p.a, abase + (k + kFixThreads * u) * p.a.s_k);
+      y[u] = op_value(p.b, bbase + (k + kFixThreads * u) * p.b.s_k);
+    }
+#pragma unroll
+    for (int u = 0; u < kFixChains; ++u) dot2_add(ch[u], scale2(x[u], da), scale2(y[u], db));
+  }
+  for (; k < p.K; k += kFixThreads)
+    dot2_add(ch[0], scale2(op_value(p.a, abase + k * p.a.s_k), da),
+             scale2(op_value(p.b, bbase + k * p.b.s_k), db));
+#pragma unroll
+  for (int w = 1; w < kFixChains; w <<= 1)
+#pragma unroll
+    for (int u = 0; u + w < kFixChains; u += 2 * w) dot2_merge(ch[u], ch[u + w]);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    Dot2 o;
+    o.p = __shfl_down_sync(0xffffffffu, ch[0].p, off);
+    o.s = __shfl_down_sync(0xffffffffu, ch[0].s, off);
+    if (lane + off < 32) dot2_merge(ch[0], o);
+  }
+  if (lane == 0) s_warp[threadIdx.x >> 5] = ch[0];
+  __syncthreads();
+  double v = 0.0;
+  if (threadIdx.x == 0) {
+    Dot2 d = s_warp[0];
+    for (int w = 1; w < kFixThreads / 32; ++w) dot2_merge(d, s_warp[w]);
+    v = scale2(scale2(__dadd_rn(d.p, d.s), -da), -db);
+  }
+  __syncthreads();  // s_warp is reused by the next output
+  return v;
+}
+
+
+// A 64 x 64 output tile by one block: 16 x 16 threads, each with 4 x 4
+// outputs (rows ty + 16 u, columns tx + 16 v), k in slabs of 16 staged in
+// shared memory with the scaling applied.  Outputs of non-finite or zero
+// rows and columns keep what the CRT wrote.
+__device__ void dot2_tile(const FixParams& p, int64_t b, int64_t tm, int64_t tn) {
+  __shared__ double sA[kFixTile][17];
+  __shared__ double sB[16][kFixTile + 1];
+  __shared__ int sShA[kFixTile], sShB[kFixTile];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t i0 = tm * kFixTile, j0 = tn * kFixTile;
+  if (threadIdx.x < kFixTile) {
+    const int64_t i = i0 + threadIdx.x, j = j0 + threadIdx.x;
+    sShA[threadIdx.x] = i < p.M ? p.sa[b * p.Mp + i] : kShiftZero;
+    sShB[threadIdx.x] = j < p.N ? p.sb[b * p.Np + j] : kShiftZero;
+  }
+  __syncthreads();
+  auto usable = [](int sh) { return sh != kShiftNonFinite && sh != kShiftZero; };
+  Dot2 acc[4][4];
+  for (int64_t k0 = 0; k0 < p.K; k0 += 16) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int e = threadIdx.x + t * kFixThreads;  // 0 .. 1023
+      {  // A: 64 rows x 16 k
+        const int r = e >> 4, kk = e & 15;
+        const int64_t i = i0 + r, k = k0 + kk;
+        const int sh = sShA[r];
+        double v = 0.0;
+        if (k < p.K && usable(sh))
+          v = scale2(op_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k), sh - p.P);
+        sA[r][kk] = v;
+      }
+      {  // B: 16 k x 64 columns
+        const int kk = e >> 6, c = e & 63;
+        const int64_t j = j0 + c, k = k0 + kk;
+        const int sh = sShB[c];
+        double v = 0.0;
+        if (k < p.K && usable(sh))
+          v = scale2(op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k), sh - p.P);
+        sB[kk][c] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < 16; ++kk) {
+      double x[4], y[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = sA[ty + 16 * u][kk];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) y[v] = sB[kk][tx + 16 * v];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) dot2_add(acc[u][v], x[u], y[v]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t i = i0 + ty + 16 * u;
+    const int sha = sShA[ty + 16 * u];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int64_t j = j0 + tx + 16 * v;
+      const int shb = sShB[tx + 16 * v];
+      if (i < p.M && j < p.N && usable(sha) && usable(shb)) {
+        const double r = __dadd_rn(acc[u][v].p, acc[u][v].s);
+        put_result(p.c, (b * p.M + i) * p.N + j, scale2(scale2(r, p.P - sha), p.P - shb));
+      }
+    }
+  }
+}
+
+// Writes every uncertified output: with at most `cap` of them, one block per
+// listed output; with more (inputs whose rows or columns mostly defeat the
+// certificate), every output is recomputed by the tiled Dot2 product, at
+// CUDA-core FP64 speed.  Which of the two runs depends only on the count, so
+// the result is deterministic.  Nothing to do costs one read.
+__global__ void __launch_bounds__(kFixThreads, 2)
+fix_kernel(FixParams p) {
+  const int count = p.err[1];
+  if (count == 0 || p.err[0] != 0) return;
+  if (count <= p.cap) {
+    for (int64_t e = blockIdx.x; e < count; e += gridDim.x) {
+      const uint64_t flat = p.list[e];
+      const int64_t row = static_cast<int64_t>(flat / static_cast<uint64_t>(p.N));
+      const int64_t j = static_cast<int64_t>(flat) - row * p.N;
+      const int64_t b = row / p.M, i = row - b * p.M;
+      const int sa = p.sa[b * p.Mp + i], sb = p.sb[b * p.Np + j];
+      const double v = dot2_block(p, b, i, j, sa - p.P, sb - p.P);
+      if (threadIdx.x == 0) put_result(p.c, static_cast<int64_t>(flat), v);
+    }
+    return;
+  }
+  const int64_t tm = (p.M + kFixTile - 1) / kFixTile, tn = (p.N + kFixTile - 1) / kFixTile;
+  const int64_t tiles = p.batch * tm * tn;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t b = t / (tm * tn);
+    const int64_t r = t - b * tm * tn;
+    dot2_tile(p, b, r / tn, r % tn);
   }
 }
 
@@ -1629,6 +1868,12 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
   std::memcpy(cp.w, cc.w, sizeof(cp.w));
   std::memcpy(cp.mlimb, cc.mlimb, sizeof(cp.mlimb));
   cp.inv_m = cc.inv_m;
+  cp.P = P;
+  cp.certify_below =
+      std::ldexp(static_cast<double>(p.K) * std::ldexp(1.0, P) + 0x1p35, kCertifyBits);
+  cp.fix_count = err + 1;
+  cp.fix_list = reinterpret_cast<uint64_t*>(ws + g.off_fix_list);
+  cp.fix_cap = g.fix_cap;
   cp.batch = p.batch;
   cp.M = p.M;
   cp.N = p.N;
@@ -1697,15 +1942,15 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
   // used.
   // A split by rows and B by columns (the usual row-major A and B): the
   // column maxima of B are taken in the same launch as A's row split.
+  uint8_t* const clear_end = reinterpret_cast<uint8_t*>(err + 2);
   const bool merged = p.batch == 1 && split_by_rows(p.a, p.M) && !split_by_rows(p.b, p.N) &&
                       split_rows_threads(p.K) == 256;
   if (merged) {
     ProfileScope prof("ozaki_split", s);
-    // B's column-maximum codes and the error word are neighbours in the
-    // workspace (in that order): one memset clears both
-    DSB_CUDA_TRY(cudaMemsetAsync(
-        cb, 0, static_cast<size_t>(reinterpret_cast<char*>(err + 1) - reinterpret_cast<char*>(cb)),
-        s));
+    // B's column-maximum codes, the error word and the uncertified-output
+    // count are neighbours in the workspace (in that order): one memset
+    // clears them all
+    DSB_CUDA_TRY(cudaMemsetAsync(cb, 0, clear_end - reinterpret_cast<uint8_t*>(cb), s));
     const int64_t cgx = g.Np / kColTileR, cgy = (p.K + kColmaxSlab - 1) / kColmaxSlab;
     const int64_t nc = cgx * cgy;
     {
@@ -1719,7 +1964,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
     split_cols_kernel<<<g2, 256, 0, s>>>(p.b, p.N, p.K, g.Np, g.Kp, 1, P, cb, planes_b, sb);
     if (int st = launch_status()) return st;
   } else {
-    DSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+    DSB_CUDA_TRY(cudaMemsetAsync(err, 0, clear_end - reinterpret_cast<uint8_t*>(err), s));
     ProfileScope prof("ozaki_split", s);
     if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
       return st;
@@ -1727,7 +1972,26 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
       return st;
   }
   if (int st = launch_gemm(0, static_cast<int>(g.Mp / tile_rows), s)) return st;
-  return launch_crt(0, p.batch * p.M, s);
+  if (int st = launch_crt(0, p.batch * p.M, s)) return st;
+  FixParams fp{};
+  fp.a = p.a;
+  fp.b = p.b;
+  fp.c = p.c;
+  fp.batch = p.batch;
+  fp.M = p.M;
+  fp.N = p.N;
+  fp.Mp = g.Mp;
+  fp.Np = g.Np;
+  fp.K = p.K;
+  fp.P = P;
+  fp.sa = sa;
+  fp.sb = sb;
+  fp.err = err;
+  fp.list = cp.fix_list;
+  fp.cap = g.fix_cap;
+  ProfileScope prof("ozaki_fix", s);
+  fix_kernel<<<static_cast<unsigned>(2 * sm_count()), kFixThreads, 0, s>>>(fp);
+  return launch_status();
 }
 
 }  // namespace

@@ -87,19 +87,19 @@ DS_API const char* ds_version(void);
 
 /* ---- split / recombine -------------------------------------------------- */
 
-/* DsFromF64, cpp/ds_from_f64.cpp:91-122: x f64[...] -> y f32[..., 2],
+/* DsFromF64, cpp/ds_from_f64.cpp:18-49: x f64[...] -> y f32[..., 2],
    hi = f32(x), lo = f32(x - f64(hi)). */
 DS_API int ds_from_f64(const ds_buffer* x, const ds_buffer* y, void* stream);
 
-/* DsToF64, cpp/ds_to_f64.cpp:139-169: x f32[..., 2] -> y f64[...],
+/* DsToF64, cpp/ds_to_f64.cpp:17-47: x f32[..., 2] -> y f64[...],
    y = f64(hi) + f64(lo). */
 DS_API int ds_to_f64(const ds_buffer* x, const ds_buffer* y, void* stream);
 
-/* ds_from_f32 ("Host" target, cpp/ds_from_f32.cpp:185-210): x f32[...] ->
+/* ds_from_f32 ("Host" target, cpp/ds_from_f32.cpp:16-41): x f32[...] ->
    y f32[..., 2] = (x, 0). */
 DS_API int ds_from_f32(const ds_buffer* x, const ds_buffer* y, void* stream);
 
-/* ds_to_f32 ("Host" target, cpp/ds_to_f32.cpp:226-249): x f32[..., 2] ->
+/* ds_to_f32 ("Host" target, cpp/ds_to_f32.cpp:16-39): x f32[..., 2] ->
    y f32[...] = hi + lo (an f32 add). */
 DS_API int ds_to_f32(const ds_buffer* x, const ds_buffer* y, void* stream);
 

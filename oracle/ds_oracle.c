@@ -55,14 +55,14 @@ static inline void two_prod(float a, float b, float* p, float* e) {
   *e = ((ah * bh - pp) + ah * bl + al * bh) + al * bl;
 }
 
-/* f64 -> DS: cpp/ds_fused_add_mul_to_f64.cpp:29-32 (and ds_from_f64.cpp:108-109). */
+/* f64 -> DS: cpp/ds_fused_add_mul_to_f64.cpp:29-32 (and ds_from_f64.cpp:35-36). */
 static inline void from_double(double x, float* hi, float* lo) {
   float h = (float)x;
   *hi = h;
   *lo = (float)(x - (double)h);
 }
 
-/* DS -> f64: cpp/ds_fused_add_mul_to_f64.cpp:64-66 (and ds_to_f64.cpp:158). */
+/* DS -> f64: cpp/ds_fused_add_mul_to_f64.cpp:64-66 (and ds_to_f64.cpp:36). */
 static inline double to_double(float hi, float lo) {
   return (double)hi + (double)lo;
 }
@@ -89,7 +89,7 @@ static inline void sub_pair(float ah, float al, float bh, float bl,
   *ol = t2 + e2;
 }
 
-/* ds_mul_pair: cpp/ds_fused_add_mul_to_f64.cpp:50-62 (== cpp/ds_mul.cpp:168-176).
+/* ds_mul_pair: cpp/ds_fused_add_mul_to_f64.cpp:50-62 (== cpp/ds_mul.cpp:66-74).
  * out_lo = (e1 + e2) + al*bl, left to right as C evaluates it. */
 static inline void mul_pair(float ah, float al, float bh, float bl,
                             float* oh, float* ol) {
@@ -133,7 +133,7 @@ void dso_sub(const float* a, const float* b, float* y, int64_t n, int nthreads) 
   }
 }
 
-/* DsMulImpl hot loop: cpp/ds_mul.cpp:162-177. */
+/* DsMulImpl hot loop: cpp/ds_mul.cpp:60-75. */
 void dso_mul(const float* a, const float* b, float* y, int64_t n, int nthreads) {
   (void)nthreads;
   DSO_PARALLEL_FOR
@@ -147,7 +147,7 @@ void dso_mul(const float* a, const float* b, float* y, int64_t n, int nthreads) 
 
 /* ---- split / recombine --------------------------------------------------- */
 
-/* DsFromF64Impl: cpp/ds_from_f64.cpp:107-112. */
+/* DsFromF64Impl: cpp/ds_from_f64.cpp:34-39. */
 void dso_from_f64(const double* x, float* y, int64_t n, int nthreads) {
   (void)nthreads;
   DSO_PARALLEL_FOR
@@ -159,14 +159,14 @@ void dso_from_f64(const double* x, float* y, int64_t n, int nthreads) {
   }
 }
 
-/* DsToF64Impl: cpp/ds_to_f64.cpp:155-159. */
+/* DsToF64Impl: cpp/ds_to_f64.cpp:33-37. */
 void dso_to_f64(const float* x, double* y, int64_t n, int nthreads) {
   (void)nthreads;
   DSO_PARALLEL_FOR
   for (int64_t i = 0; i < n; ++i) y[i] = to_double(x[2 * i], x[2 * i + 1]);
 }
 
-/* DsFromF32Impl: cpp/ds_from_f32.cpp:198-201. */
+/* DsFromF32Impl: cpp/ds_from_f32.cpp:29-32. */
 void dso_from_f32(const float* x, float* y, int64_t n, int nthreads) {
   (void)nthreads;
   DSO_PARALLEL_FOR
@@ -176,7 +176,7 @@ void dso_from_f32(const float* x, float* y, int64_t n, int nthreads) {
   }
 }
 
-/* DsToF32Impl: cpp/ds_to_f32.cpp:239-240 (an f32 add of hi and lo). */
+/* DsToF32Impl: cpp/ds_to_f32.cpp:29-30 (an f32 add of hi and lo). */
 void dso_to_f32(const float* x, float* y, int64_t n, int nthreads) {
   (void)nthreads;
   DSO_PARALLEL_FOR

@@ -212,3 +212,117 @@ def test_single_cta_kernel_gives_the_pair_kernels_bits(ops):
     got = np.frombuffer(out.stdout, dtype=np.float64).reshape(want.shape)
     assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
     check_gemm(got, A, B)
+
+
+def _wide_cases():
+    """Operands whose rows of A or columns of B span many binades, so the
+    row (column) maximum that sets the quantisation step does not take part
+    in every output.  Seeded; 96 x 640 x 80."""
+    M, K, N = 96, 640, 80
+    out = {}
+    for span in (30, 60):
+        rng = np.random.default_rng(100 + span)
+        A = rng.uniform(-1, 1, (M, K)) * 2.0 ** -rng.uniform(0, span, (M, K))
+        B = rng.uniform(-1, 1, (K, N)) * 2.0 ** -rng.uniform(0, span, (K, N))
+        out[f"binades{span}"] = (A, B)
+        # a large entry facing a zero: each output is made of the small terms only
+        A = rng.uniform(-1, 1, (M, K)) * 2.0 ** -span
+        A[:, 0] = 1.0
+        B = rng.uniform(-1, 1, (K, N))
+        B[0, :] = 0.0
+        out[f"large_faces_zero{span}"] = (A, B)
+        # the same on the B side, and a large entry facing a small one
+        B = rng.uniform(-1, 1, (K, N)) * 2.0 ** -span
+        B[3, :] = -4.0
+        A = rng.uniform(-1, 1, (M, K))
+        A[:, 3] = 2.0 ** -span * rng.uniform(-1, 1, M)
+        out[f"large_faces_small{span}"] = (A, B)
+    # mixed-sign cancellation inside each row of A
+    rng = np.random.default_rng(7)
+    A = rng.uniform(-1, 1, (M, K))
+    A[:, 1::2] = -A[:, 0::2] * (1 + 2.0 ** -20 * rng.uniform(-1, 1, (M, K // 2)))
+    B = 1.0 + 1e-7 * rng.uniform(-1, 1, (K, N))
+    out["row_cancellation"] = (A, B)
+    # huge entries facing zeros beside ordinary values
+    A = rng.uniform(-1, 1, (M, K))
+    A[:, 5] = 2.0 ** 40
+    B = rng.uniform(-1, 1, (K, N))
+    B[5, :] = 0.0
+    out["huge_faces_zero"] = (A, B)
+    return out
+
+
+WIDE = _wide_cases()
+
+
+def assert_no_worse_than_reference(got, A, B, samples=600):
+    """Entry by entry: |ours - exact| <= |reference DS path - exact|, or ours
+    is within one f64 ulp of the exact value (a correctly rounded f64 cannot
+    be beaten, and the reference can land exactly by chance)."""
+    M, N = got.shape
+    rows, cols = exact.sample_indices(M, N, samples)
+    truth = exact.exact_gemm_entries(A, B, rows, cols)
+    ref = ds_pass_ref.dot_general_f64(A, B)
+    err = np.abs(got[rows, cols] - truth)
+    ref_err = np.abs(ref[rows, cols] - truth)
+    ulp = np.spacing(np.abs(truth))
+    bad = ~((err <= ref_err) | (err <= ulp))
+    assert not bad.any(), (int(bad.sum()), err[bad][:4], ref_err[bad][:4], truth[bad][:4])
+    return err, ref_err
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("case", sorted(WIDE))
+def test_wide_dynamic_range(ops, algo, case):
+    """Rows and columns spanning 2^0..2^-30 and 2^0..2^-60, large entries
+    facing zeros (outputs made only of small terms), and cancellation inside
+    a row: no sampled entry is worse than the reference DS path."""
+    A, B = WIDE[case]
+    got = host(ops.ds_matmul_f64(cu(A), cu(B), algorithm=algo))
+    assert_no_worse_than_reference(got, A, B)
+
+
+def test_wide_dynamic_range_ds_operands_and_result(ops):
+    """The same certificate on SoA DS operands (hi, lo) with a DS result."""
+    A, B = WIDE["large_faces_zero60"]
+    ah, al = ds_pass_ref.from_float(A)
+    bh, bl = ds_pass_ref.from_float(B)
+    hi, lo = ops.ds_dot_general(cu(ah), cu(al), cu(bh), cu(bl))
+    got = host(hi).astype(np.float64) + host(lo).astype(np.float64)
+    A64 = ah.astype(np.float64) + al.astype(np.float64)
+    B64 = bh.astype(np.float64) + bl.astype(np.float64)
+    # the DS result carries 48 bits: within 2^-46 of the exact value
+    rows, cols = exact.sample_indices(*got.shape, 300)
+    truth = exact.exact_gemm_entries(A64, B64, rows, cols)
+    assert np.all(np.abs(got[rows, cols] - truth) <= 2.0 ** -46 * np.abs(truth))
+
+
+def test_zero_rows_and_columns_are_exact_zeros(ops):
+    """All-zero rows of A and columns of B give +0 outputs without any
+    recomputation; the other outputs are unchanged by their presence."""
+    rng = np.random.default_rng(11)
+    A = rng.uniform(-1, 1, (200, 300))
+    B = rng.uniform(-1, 1, (300, 260))
+    A[[0, 17, 199]] = 0.0
+    B[:, [1, 100]] = 0.0
+    got = host(ops.ds_matmul_f64(cu(A), cu(B)))
+    assert np.all(got[[0, 17, 199]] == 0.0) and np.all(got[:, [1, 100]] == 0.0)
+    assert not np.signbit(got[[0, 17, 199]]).any()
+    check_gemm(got, A, B, samples=400, ref=ds_pass_ref.dot_general_f64(A, B))
+
+
+def test_many_uncertified_outputs_take_the_tiled_recompute(ops):
+    """More than 2^20 uncertified outputs (a large entry facing zeros in every
+    row): every output is recomputed by the tiled compensated product.  The
+    result is no worse than the reference path, and identical across calls."""
+    rng = np.random.default_rng(21)
+    M, K, N = 1100, 192, 1000
+    A = rng.uniform(-1, 1, (M, K)) * 2.0 ** -40
+    A[:, 0] = 1.0
+    B = rng.uniform(-1, 1, (K, N))
+    B[0, :] = 0.0
+    dA, dB = cu(A), cu(B)
+    got = host(ops.ds_matmul_f64(dA, dB))
+    again = host(ops.ds_matmul_f64(dA, dB))
+    assert np.array_equal(got.view(np.uint64), again.view(np.uint64))
+    assert_no_worse_than_reference(got, A, B, samples=400)

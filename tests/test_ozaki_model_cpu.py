@@ -174,3 +174,41 @@ def test_epilogue_modulo():
         for v in vals + [k * m - 1 for k in range(1, 2 ** 31 // m, 2 ** 31 // m // 1000)]:
             q = ((v * magic) >> 32) >> 7
             assert v - q * m == v % m
+
+
+def _ozaki_exact(A, B):
+    """C_int of the quantised operands (Python integers) and the shifts."""
+    K = A.shape[1]
+    P = bits_for_k(K)
+    qa, sa = quantise(A, P)
+    qb, sb = quantise(B.T, P)
+    C = [[sum(x * y for x, y in zip(ra, rb)) for rb in qb] for ra in qa]
+    return C, sa, sb, P
+
+
+def test_certificate_bounds_the_quantisation_error():
+    """An output with |C_int| >= 2^24 (K 2^P + 2^35) has error at most
+    2^-24 |C| against the exact product; the bound is checked on inputs that
+    defeat the row-maximum scaling (a large entry facing zeros, values over
+    60 binades) and on plain uniform ones."""
+    rng = np.random.default_rng(5)
+    M, K, N = 12, 96, 10
+    cases = [rng.uniform(-1, 1, (M, K)), rng.uniform(-1, 1, (M, K)) * 2.0 ** -rng.uniform(0, 60, (M, K))]
+    wide = rng.uniform(-1, 1, (M, K)) * 2.0 ** -30
+    wide[:, 0] = 1.0
+    cases.append(wide)
+    for A in cases:
+        B = rng.uniform(-1, 1, (K, N)) * 2.0 ** -rng.uniform(0, 20, (K, N))
+        B[0, ::2] = 0.0
+        C, sa, sb, P = _ozaki_exact(A, B)
+        bound = 2 ** 24 * (K * 2 ** P + 2 ** 35)
+        certified = 0
+        for i in range(M):
+            for j in range(N):
+                if abs(C[i][j]) < bound:
+                    continue
+                certified += 1
+                got = math.ldexp(float(C[i][j]), -(sa[i] + sb[j]))
+                truth = exact.exact_dot(A[i], B[:, j])
+                assert abs(got - truth) <= 2.0 ** -24 * abs(got), (i, j, got, truth)
+        assert certified > 0
