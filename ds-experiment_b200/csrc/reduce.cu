@@ -439,13 +439,17 @@ reduce_cols_split_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int
   }
 }
 
-// Slices of the reduced dimension for the split column reduction: enough
-// blocks to fill the GPU, at least 1024 rows a slice, at most 512 slices;
-// 1 (no split) when the columns alone fill it or the rows are short.
+// Slices of the reduced dimension for the split column reduction: about
+// kSliceBlocks blocks (a B200 holds 8 per SM, 1184), at least 1024 rows a
+// slice, at most 512 slices; 1 (no split) when the columns alone make half
+// that many blocks or the rows are short.  A function of the shape alone,
+// so the summation order (and the bits) do not depend on the device.
+constexpr int64_t kSliceBlocks = 1024;
+
 int64_t cols_slices(int64_t outer, int64_t red, int64_t inner) {
   if (inner <= 1) return 1;
   const int64_t tiles = (outer * inner + 31) / 32;
-  const int64_t want = static_cast<int64_t>(sm_count()) * 8;
+  const int64_t want = kSliceBlocks;
   if (tiles >= want / 2 || red < 4096) return 1;
   int64_t sl = (want + tiles - 1) / tiles;
   if (sl > red / 1024) sl = red / 1024;
@@ -589,17 +593,20 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
 // ---- allocation-free variant ------------------------------------------------
 //
 // For callers that cannot allocate device memory (see ds_reduce_f64_noalloc
-// in ds_b200.h), the block partials of a full reduction live in this
-// file-scope device array instead of caller workspace.  Every GPU that loads
-// the library holds it (32 KiB) until the process exits.  Host code cannot
+// in ds_b200.h), the partials that ds_reduce_f64 keeps in caller workspace
+// live in this file-scope device array instead: the block partials of a full
+// reduction (at most 8 per SM), or the slice partials of a reduction over a
+// leading dimension with few columns (slices * columns, below
+// 32 * (kSliceBlocks + 512) = 49152 by cols_slices).  Every GPU that loads
+// the library holds it (384 KiB) until the process exits.  Host code cannot
 // use the symbol itself as a pointer (on the host it names a stand-in, not
 // device memory), so its device address is looked up once per device with
 // cudaGetSymbolAddress, with that device current, and passed to the kernels.
-// All calls share the array: stage 1 overwrites every slot that stage 2
-// reads, so nothing needs clearing between calls, but two calls whose
+// All calls share the array: the first stage overwrites every slot that the
+// second reads, so nothing needs clearing between calls, but two calls whose
 // kernels overlap on the GPU (different streams, no ordering) race on it.
 
-constexpr int kStaticPartials = 4096;
+constexpr int kStaticPartials = 49152;
 static __device__ __align__(256) ds2 g_static_partials[kStaticPartials];
 
 namespace {
@@ -625,18 +632,18 @@ int static_partials_address(ds2** out) {
 }  // namespace
 
 int reduce_launch_noalloc(ReduceArgs a, cudaStream_t s) {
-  if (a.outer == 1 && a.inner == 1 && a.red > 0) {
-    const int g = reduce_full_blocks(a.red);
-    if (g > kStaticPartials) {
-      return set_error(DS_INVALID_ARGUMENT,
-                       "ds_reduce_f64_noalloc: needs " + std::to_string(g) +
-                           " block partials, more than its static maximum of " +
-                           std::to_string(kStaticPartials));
-    }
+  const size_t need = reduce_workspace_bytes(a.outer, a.red, a.inner);
+  if (need > sizeof(g_static_partials)) {
+    return set_error(DS_INVALID_ARGUMENT,
+                     "ds_reduce_f64_noalloc: needs " + std::to_string(need / sizeof(ds2)) +
+                         " partials, more than its static maximum of " +
+                         std::to_string(kStaticPartials));
+  }
+  if (need > 0) {
     ds2* partials = nullptr;
     if (int st = static_partials_address(&partials)) return st;
     a.workspace = partials;
-    a.workspace_bytes = sizeof(g_static_partials);
+    a.workspace_bytes = need;
   }
   return reduce_launch(a, s);
 }

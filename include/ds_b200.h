@@ -171,12 +171,16 @@ DS_API int ds_recurrence_mul_add_to_f64(const ds_buffer* x, const ds_buffer* a,
    shape without the reduced dimensions.  The body is the pass's: acc =
    ds_op(acc, elem).  Elements are folded per thread in index order, then in
    a fixed shuffle/block tree, then block partials in block order, so results
-   are deterministic for a given shape; init is applied once, last
-   (subtract: init - sum; add: init + sum; multiply: init * product).
+   are deterministic for a given shape and device model (a full reduction
+   uses up to 8 blocks per SM, so its order follows the SM count); init is
+   applied once, last (subtract: init - sum; add: init + sum; multiply:
+   init * product).
    The workspace (ds_reduce_workspace_size bytes) holds block partials: a
    full reduction needs it; a reduction over a leading dimension with few
-   columns uses it to slice the reduced dimension across blocks, and runs
-   in one stage without it; other reductions need none. */
+   columns uses it to slice the reduced dimension across blocks (the slice
+   count depends on the shape alone), and runs in one stage, in another
+   order, when given less than ds_reduce_workspace_size bytes; other
+   reductions need none. */
 DS_API size_t ds_reduce_workspace_size(const ds_buffer* in, const int64_t* dimensions,
                                 int64_t n_dimensions);
 DS_API int ds_reduce(const ds_buffer* in_hi, const ds_buffer* in_lo,
@@ -199,13 +203,16 @@ DS_API int ds_reduce_f64(const ds_buffer* in, const ds_buffer* init,
    whose caching allocator (XLA's BFC allocator, torch's) has already reserved
    most of HBM, where a cudaMalloc of its own can fail and, because it may
    synchronise the device, would also stall every stream.  This entry point
-   takes only inputs and outputs and allocates nothing: the block partials of
-   a full reduction live in a library-owned static device array of 4096
-   partials (32 KiB), which every GPU that loads the library holds until the
-   process exits.  Results are bit-identical to ds_reduce_f64.
-   - A reduction that would need more than 4096 block partials returns
-     DS_INVALID_ARGUMENT (the partial count is at most 8 per SM, so this does
-     not occur on B200).
+   takes only inputs and outputs and allocates nothing: the partials that
+   ds_reduce_f64 keeps in its workspace (the block partials of a full
+   reduction, the slice partials of a reduction over a leading dimension
+   with few columns) live in a library-owned static device array of 49152
+   partials (384 KiB), which every GPU that loads the library holds until
+   the process exits.  Results are bit-identical to ds_reduce_f64 given a
+   workspace of ds_reduce_workspace_size bytes.
+   - A reduction that would need more than 49152 partials returns
+     DS_INVALID_ARGUMENT (full reductions use at most 8 per SM and sliced
+     ones fewer than 49152, so this does not occur on B200).
    - The first call on each device looks up the array's device address
      (cudaGetSymbolAddress) with that device current; make that first call
      before any stream capture.

@@ -178,6 +178,7 @@ def make(ref_root, out_path):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    p = make(ref, os.path.join(HERE, "ds_ref_vectors.npz"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference tree root>")
+    p = make(sys.argv[1], os.path.join(HERE, "ds_ref_vectors.npz"))
     print("wrote", p, os.path.getsize(p), "bytes")

@@ -50,8 +50,12 @@ def _worker_body(rank, world, n, q):
         local = torch.from_numpy(x[start:stop])
 
         def local_pair(t):
-            h, l = dso.ds_reduce_f64_seq(t.numpy())
-            return torch.tensor([h, l], dtype=torch.float32)
+            # the GPU's f64 entry sums a shard exactly in f64 per thread
+            # before its DS tree: stood in for by the exact sum, split
+            import math
+            s = math.fsum(t.numpy().tolist())
+            p = dso.ds_from_f64(np.array([s]))
+            return torch.tensor([p[0, 0], p[0, 1]], dtype=torch.float32)
 
         def combine(pairs, init):
             p = pairs.numpy()
@@ -89,8 +93,8 @@ def test_sharded_sum_gloo(world):
     ranges = [rg for *_, rg in results]
     assert ranges[0][0] == 0 and ranges[-1][1] == n
     assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
-    # as close to the exact sum (+ init) as the reference-order DS fold: the
-    # running sum swings through +-1e8, where DS resolves about 1e8 * 2^-48
+    # no farther from the exact sum (+ init) than the reference-order DS
+    # fold, whose running sum swings through +-1e8 (DS resolves ~1e8 * 2^-48)
     import math
 
     from oracle import dso
@@ -99,7 +103,7 @@ def test_sharded_sum_gloo(world):
     truth = math.fsum(x.tolist()) + 0.5
     h, l = dso.ds_reduce_f64_seq(x, init=(0.5, 0.0))
     seq_err = abs(float(h) + float(l) - truth)
-    assert abs(results[0][1] - truth) <= 4 * seq_err + 1e-12
+    assert abs(results[0][1] - truth) <= seq_err
 
 
 def test_shard_range_covers():

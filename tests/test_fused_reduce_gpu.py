@@ -35,7 +35,12 @@ def ds_bound(v):
 
 
 def check_sum(got, Z, dso):
-    """got: (hi, lo) tensors; Z: the map's DS values (packed, from the oracle)."""
+    """got: (hi, lo) tensors; Z: the map's DS values (packed, from the oracle).
+
+    The kernel and the sequential fold add the same DS values exactly as
+    given, in different orders (a tree against a running sum), so neither
+    error bounds the other: the result is held to 4x the sequential error or
+    the DS bound of the values, whichever is larger."""
     vals = Z[..., 0].astype(np.float64).ravel()
     los = Z[..., 1].astype(np.float64).ravel()
     truth = exact.exact_sum(np.concatenate([vals, los]))
@@ -140,7 +145,9 @@ def test_dstensor_sum_uses_one_kernel(dso):
 
 
 def check_rows(hi, lo, Z, dso, init=(0.0, 0.0)):
-    """Each row's result against the exact sum of its DS values plus init."""
+    """Each row's result against the exact sum of its DS values plus init,
+    held as in check_sum (different fold orders: 4x the sequential error or
+    the DS bound)."""
     got = host(hi).astype(np.float64) + host(lo).astype(np.float64)
     rows = Z.reshape(got.size, -1, 2)
     for r, g in zip(rows, got.ravel()):

@@ -2,9 +2,10 @@
 
 The reference's reduce is XLA's tree over the pass's DS body
 (DsTransformPass.cpp:376-448) and no reference test pins its bits, so parity
-is measured as error: the GPU result's error against math.fsum must be no
-worse than a small multiple of the reference-order (sequential) DS fold's
-error, and within a DS-precision bound of the input magnitudes.
+is measured as error: on f64 input (the config-2 path) the GPU result's error
+against math.fsum must be no worse than the reference-order (sequential) DS
+fold's error.  Where a case cannot promise that (named in its docstring), it
+must stay within a DS-precision bound of the input magnitudes.
 """
 import math
 
@@ -41,6 +42,9 @@ def ds_bound(x):
 @pytest.mark.parametrize("n", [1, 2, 3, 1000, 10_000, 65_537, 1 << 20, (1 << 20) + 37,
                                (1 << 22) + 4095])
 def test_config2_sum_error(ops, dso, n):
+    """Config 2 (x = +-1e8 alternating + U[0,1) 1e-3): the f64 entry sums each
+    thread's values exactly in f64 before its DS tree, so its error is never
+    above the sequential DS fold's (which also pays for splitting every x)."""
     x = config2_inputs(n)
     truth = exact.exact_sum(x)
     got = float(host(ops.ds_sum_f64(cu(x))))
@@ -48,7 +52,7 @@ def test_config2_sum_error(ops, dso, n):
     ref = float(h) + float(l)
     f32 = float(np.sum(x.astype(np.float32), dtype=np.float32))
     err, ref_err, f32_err = abs(got - truth), abs(ref - truth), abs(f32 - truth)
-    assert err <= max(4 * ref_err, ds_bound(x)), (err, ref_err)
+    assert err <= ref_err, (err, ref_err)
     if n >= 1000:
         assert err < f32_err / 1000, (err, f32_err)
 
@@ -70,7 +74,12 @@ def test_triplet_cancellation(ops):
 def test_soa_entry_and_f64_entry(ops, dso):
     """ds_reduce on the split inputs (DS values) and the fused f64 entry (which
     sums the f64 inputs exactly per thread) are both within the DS bound, and
-    the f64 entry is at least as close to the exact sum of the f64 inputs."""
+    the f64 entry is at least as close to the exact sum of the f64 inputs.
+    The SoA entry and the sequential fold add the same DS values, whose
+    representation error (the sum of the split errors, common to both)
+    dominates; the two folds differ only in order, so neither error bounds the
+    other and the SoA entry is held to 4x the sequential error or the DS bound.
+    The f64 entry is held to the sequential error itself."""
     x = config2_inputs(100_003, seed=3)
     truth = exact.exact_sum(x)
     sp = dso.ds_from_f64(x)
@@ -81,6 +90,7 @@ def test_soa_entry_and_f64_entry(ops, dso):
     ref_err = abs(float(h) + float(l) - truth)
     assert abs(soa - truth) <= max(4 * ref_err, ds_bound(x))
     assert abs(f64 - truth) <= abs(soa - truth) + ds_bound(x) * 2.0 ** -8
+    assert abs(f64 - truth) <= ref_err
 
 
 @pytest.mark.parametrize("n", [1, 2, 7, 4096, 100_003])
@@ -190,14 +200,15 @@ def test_segmented(ops, shape, dims):
 
 @pytest.mark.slow
 def test_config2_large_property(ops, dso):
-    """N = 2^26 (512 MiB): error vs math.fsum against the sequential DS fold."""
+    """N = 2^26 (512 MiB): error vs math.fsum no worse than the sequential DS
+    fold's."""
     n = 1 << 26
     x = config2_inputs(n)
     got = float(host(ops.ds_sum_f64(cu(x))))
     truth = exact.exact_sum(x)
     h, l = dso.ds_reduce_f64_seq(x)
     ref_err = abs(float(h) + float(l) - truth)
-    assert abs(got - truth) <= max(4 * ref_err, ds_bound(x))
+    assert abs(got - truth) <= ref_err
 
 
 def test_bulk_stream_matches_per_thread_loads_in_accuracy(ops):
@@ -235,3 +246,102 @@ def test_variadic_reduce(ops):
             assert_bits_equal(host(o), host(want), f"{body} {dims}")
     with pytest.raises(Exception):
         ops.ds_reduce_f64_multi([xs[0], torch.zeros(5, dtype=torch.float64, device="cuda")])
+
+
+SLICED = [((1 << 18, 8), (0,)), ((20000, 3, 5), (0,))]
+
+
+def _reduce_f64_capi(x, dims, body, workspace_bytes):
+    """ds_reduce_f64 through the C ABI with a caller-sized workspace (0: none)."""
+    import ctypes
+    import torch
+    from ds_b200 import _lib as L
+    init = torch.zeros((), dtype=torch.float64, device=x.device)
+    shape = tuple(s for i, s in enumerate(x.shape) if i not in dims)
+    out = torch.empty(shape, dtype=torch.float64, device=x.device)
+    ws = torch.empty(max(workspace_bytes, 1), dtype=torch.uint8, device=x.device)
+    bx, kx = L.make_buffer(x.data_ptr(), x.shape)
+    bi, ki = L.make_buffer(init.data_ptr(), ())
+    bo, ko = L.make_buffer(out.data_ptr(), shape)
+    cd = (ctypes.c_int64 * len(dims))(*dims)
+    st = L.lib().ds_reduce_f64(ctypes.byref(bx), ctypes.byref(bi), cd, len(dims),
+                               {"add": L.DS_BODY_ADD, "mul": L.DS_BODY_MUL}[body],
+                               ctypes.byref(bo), ctypes.c_void_p(ws.data_ptr()),
+                               ctypes.c_size_t(workspace_bytes),
+                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    L.check(st, "ds_reduce_f64")
+    return host(out)
+
+
+def _columns(x, dims):
+    moved = np.moveaxis(x, dims, list(range(x.ndim - len(dims), x.ndim)))
+    return moved.reshape(-1, int(np.prod([x.shape[d] for d in dims])))
+
+
+@pytest.mark.parametrize("shape,dims", SLICED)
+def test_sliced_columns_mul_body(ops, dso, shape, dims):
+    """The sliced leading-dimension path with the multiply body: slice
+    partials start from the identity and init is applied once, at the end.
+    Each column's product of up to 2^18 factors 1 + 1e-7 u is checked
+    against the exact product (1.5 exp(fsum(log1p(1e-7 u))), good to about
+    2^-51), as is the oracle's sequential DS product.  The reference's DS
+    multiply (no renormalisation) carries a small systematic error, so 2^18
+    factors drift by about 2^-35 in either order (the oracle: 2^-35.2 and
+    2^-35.8 on the first two columns): both are held to 2^-32 of the
+    product, which a slice's init or identity gone wrong (a factor of 1.5 or
+    more) misses by far."""
+    rng = np.random.default_rng(41)
+    y = 1.0 + 1e-7 * rng.uniform(-1, 1, shape)
+    got = host(ops.ds_reduce_f64(cu(y), init=1.5, dimensions=dims, body="mul")).ravel()
+    for c, col in enumerate(_columns(y, dims)):
+        truth = 1.5 * math.exp(math.fsum(np.log1p(col - 1.0).tolist()))
+        h, l = dso.ds_reduce_f64_seq(col, body="mul", init=(1.5, 0.0))
+        seq = float(h) + float(l)
+        assert abs(seq - truth) <= 2.0 ** -32 * truth, (c, seq, truth)
+        assert abs(got[c] - truth) <= 2.0 ** -32 * truth, (c, got[c], truth)
+
+
+@pytest.mark.parametrize("shape,dims", SLICED)
+def test_sliced_columns_packed_and_soa(ops, dso, shape, dims):
+    """DS input on the sliced path: the packed and SoA entries give the same
+    bits, within the DS bound of the exact column sums of the DS values."""
+    rng = np.random.default_rng(43)
+    x = rng.uniform(-1, 1, shape) * 1e6 + rng.uniform(0, 1, shape) * 1e-6
+    sp = np.ascontiguousarray(dso.ds_from_f64(x.ravel()).reshape(shape + (2,)))
+    hi, lo = ops.ds_reduce(cu(np.ascontiguousarray(sp[..., 0])),
+                           cu(np.ascontiguousarray(sp[..., 1])), dimensions=dims)
+    ph, pl = ops.ds_reduce_packed(cu(sp), dimensions=dims)
+    assert_bits_equal(host(ph), host(hi), "hi")
+    assert_bits_equal(host(pl), host(lo), "lo")
+    got = (host(hi).astype(np.float64) + host(lo).astype(np.float64)).ravel()
+    vals = sp[..., 0].astype(np.float64) + sp[..., 1].astype(np.float64)
+    cols = _columns(vals, dims)
+    want = np.array([exact.exact_sum(c) for c in cols])
+    assert np.all(np.abs(got - want) <= 2.0 ** -44 * np.abs(cols).sum(axis=1))
+
+
+@pytest.mark.parametrize("shape,dims", SLICED)
+def test_sliced_columns_with_and_without_workspace(ops, shape, dims):
+    """With ds_reduce_workspace_size bytes the reduced dimension is sliced
+    across blocks; with none the one-stage kernel runs.  The two fold in
+    different orders: integer-valued sums (exact in both) agree bit for bit,
+    general inputs agree within the DS bound."""
+    from ds_b200 import _lib as L
+    import ctypes
+    rng = np.random.default_rng(47)
+    xi = rng.integers(-2 ** 20, 2 ** 20, shape).astype(np.float64)
+    bx, kx = L.make_buffer(0, shape)
+    cd = (ctypes.c_int64 * len(dims))(*dims)
+    need = int(L.lib().ds_reduce_workspace_size(ctypes.byref(bx), cd, len(dims)))
+    assert need > 0  # these shapes are sliced
+    d = cu(xi)
+    a, b = _reduce_f64_capi(d, dims, "add", need), _reduce_f64_capi(d, dims, "add", 0)
+    assert np.array_equal(a.view(np.uint64), b.view(np.uint64))
+    assert np.array_equal(a.ravel(), _columns(xi, dims).sum(axis=1))
+    xf = rng.uniform(-1, 1, shape) * 1e6 + rng.uniform(0, 1, shape) * 1e-6
+    d = cu(xf)
+    a, b = _reduce_f64_capi(d, dims, "add", need), _reduce_f64_capi(d, dims, "add", 0)
+    cols = _columns(xf, dims)
+    want = np.array([exact.exact_sum(c) for c in cols])
+    bound = 2.0 ** -44 * np.abs(cols).sum(axis=1)
+    assert np.all(np.abs(a.ravel() - want) <= bound) and np.all(np.abs(b.ravel() - want) <= bound)

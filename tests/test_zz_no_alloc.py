@@ -52,3 +52,11 @@ def test_noalloc_matches_workspace_entry():
     want = ops.ds_reduce_f64(y, dimensions=(1,))
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+    # Reductions over a leading dimension with few columns slice it across
+    # blocks; their slice partials live in the same static array.
+    for shape in ((1 << 18, 8), (20000, 3, 5)):
+        z = torch.from_numpy(rng.uniform(-1, 1, shape) * 1e6).to(dev)
+        got = _noalloc_sum(L, z, (0,))
+        want = ops.ds_reduce_f64(z, dimensions=(0,))
+        torch.cuda.synchronize()
+        assert got.cpu().numpy().tobytes() == want.cpu().numpy().tobytes()
