@@ -253,9 +253,23 @@ def ds_matmul_f64_row_sharded(A_local: torch.Tensor, B: torch.Tensor,
 
 
 def gather_rows(C_local: torch.Tensor, group=None) -> torch.Tensor:
-    """Concatenate every rank's row block (equal row counts) on every rank."""
+    """Concatenate every rank's row block, in rank order, on every rank.  The
+    blocks may differ in length (shard_range gives the first n mod world
+    ranks one row more): each is padded to the longest for one all-gather,
+    and the padding is dropped."""
     world, _ = _world(group)
-    out = torch.empty((world * C_local.shape[0],) + tuple(C_local.shape[1:]),
-                      dtype=C_local.dtype, device=C_local.device)
-    dist.all_gather_into_tensor(out, C_local.contiguous(), group=group)
-    return out
+    rows = torch.tensor([C_local.shape[0]], dtype=torch.int64, device=C_local.device)
+    counts = torch.empty(world, dtype=torch.int64, device=C_local.device)
+    dist.all_gather_into_tensor(counts, rows, group=group)
+    counts = [int(c) for c in counts.tolist()]
+    most = max(counts)
+    tail = tuple(C_local.shape[1:])
+    block = C_local.contiguous()
+    if C_local.shape[0] < most:
+        block = torch.cat([block, torch.zeros((most - C_local.shape[0],) + tail,
+                                              dtype=C_local.dtype, device=C_local.device)])
+    out = torch.empty((world * most,) + tail, dtype=C_local.dtype, device=C_local.device)
+    dist.all_gather_into_tensor(out, block, group=group)
+    if all(c == most for c in counts):
+        return out
+    return torch.cat([out[r * most:r * most + c] for r, c in enumerate(counts)])

@@ -218,3 +218,65 @@ def test_peer_exchange_host_logic(world):
         assert failed == "raised"
         assert bad_log[-1] == ("free", 1000 + rank)  # own buffer released on failure
         assert "timed out" in checked
+
+
+def _gemm_worker(rank, world, port, q):
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from ds_b200 import dist as dsd
+        from oracle import ds_pass_ref
+        M, K, N = 101, 64, 48  # 101 rows: the shards differ in length
+        rng = np.random.default_rng(8)
+        A = rng.integers(-64, 64, (M, K)).astype(np.float64)
+        B = torch.from_numpy(rng.integers(-64, 64, (K, N)).astype(np.float64)) if rank == 0 \
+            else torch.zeros((K, N), dtype=torch.float64)
+        dsd.replicate(B, src=0)
+        r0, r1 = dsd.shard_range(M, rank, world)
+        # the per-rank product stood in for by the oracle's restatement of the
+        # reference pass (exact here: small integers)
+        C_local = torch.from_numpy(ds_pass_ref.dot_general_f64(A[r0:r1], B.numpy()))
+        C = dsd.gather_rows(C_local)
+        q.put((rank, C.numpy(), (r0, r1), B.numpy()))
+    except Exception as e:
+        q.put((rank, None, repr(e), None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_row_sharded_gemm_gloo(world):
+    """The GEMM's multi-GPU partitioning with CPU ranks: rows of A split by
+    shard_range, B replicated from rank 0, every rank's block reassembled by
+    gather_rows in rank order, equal on every rank to the single-process
+    product."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gemm_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] is not None for r in results), results
+    assert all(p.exitcode == 0 for p in procs)
+    from oracle import ds_pass_ref
+    rng = np.random.default_rng(8)
+    A = rng.integers(-64, 64, (101, 64)).astype(np.float64)
+    B = rng.integers(-64, 64, (64, 48)).astype(np.float64)
+    want = ds_pass_ref.dot_general_f64(A, B)
+    assert np.array_equal(want, A @ B)
+    for _, C, _, Bg in results:
+        assert np.array_equal(Bg, B)
+        assert np.array_equal(C, want)
+    spans = [r[2] for r in results]
+    assert spans[0][0] == 0 and spans[-1][1] == 101
+    assert len({s[1] - s[0] for s in spans}) == 2  # ragged shards exercised
