@@ -136,6 +136,15 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # workloads
 
+def gemm_config(world, algo):
+    """The headline workload's config: the same dict in both arms."""
+    return {"workload": "ds_dot_general_f64 4096x4096x4096 (A, B f64 U[-1,1] seed 2; "
+                        "per-rank 4096-row A block, B replicated)",
+            "M": GEMM_DIM * world, "N": GEMM_DIM, "K": GEMM_DIM,
+            "algorithm": algo, "parallelism": f"rows{world}",
+            "l2": "inputs 256 MiB + output 128 MiB per step exceed the 126 MB L2"}
+
+
 def gemm_inputs(rank):
     """Rank 0: exactly the 4096^3 config (default_rng(2), A then B).  Rank r > 0
     multiplies its own A block (default_rng((2, r))) by the same B."""
@@ -242,7 +251,7 @@ def run_ours(args):
     k_ms, k_n = _lib.profile_read(fam)
     launches = {}
     for f in ("ozaki_split", "ozaki_split_rows", "ozaki_colmax", "ozaki_split_rows_colmax",
-              "ozaki_split_cols", "ozaki_gemm", "ozaki_crt", "ozaki_fix",
+              "ozaki_split_cols", "ozaki_gemm", "ozaki_crt", "ozaki_fix", "ozaki_fix",
               "dot_simt", "dot_vec", "elementwise",
               "reduce", "recurrence"):
         t, n = _lib.profile_read(f)
@@ -364,7 +373,11 @@ def run_ours(args):
         if world == 1:
             result["cpu_baseline"] = cpu_baseline_gemm(A, B)
             if not args.no_secondary:
-                result["secondary"] = secondary_metrics(dev)
+                result["configs"] = every_config(dev, clk, roofline.get("kernel_ms_per_step"))
+    if world > 1 and not args.no_secondary:
+        sc = config5_strong(dev, rank, world, barrier, max_over_ranks)
+        if rank == 0:
+            result["config5_strong_scaling"] = sc
 
     if world > 1:
         dist.destroy_process_group()
@@ -375,11 +388,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (numpy default_rng(2) U[-1,1] f64, as the config)",
-        "config": {"workload": "ds_dot_general_f64 4096x4096x4096 (A, B f64 U[-1,1] seed 2; "
-                               "per-rank 4096-row A block, B replicated)",
-                   "M": GEMM_DIM * world, "N": GEMM_DIM, "K": GEMM_DIM,
-                   "algorithm": algo, "parallelism": f"rows{world}",
-                   "l2": "inputs 256 MiB + output 128 MiB per step exceed the 126 MB L2"},
+        "config": gemm_config(world, algo),
         "e2e": e2e, "roofline": roofline, "gpu_launches": gpu_launches,
         "kernel_launches": launches, "clocks": clk,
     }
@@ -400,46 +409,400 @@ def cpu_baseline_gemm(A, B, reps=1):
                       "float32 numpy matmuls (f32 accumulation), two_sum, recombine"}
 
 
-def secondary_metrics(dev):
-    """Short HBM-bound checks: fused (a+b)*c and the DS sum at 2^26 elements."""
+# ---------------------------------------------------------------------------
+# every configuration in the default line (N = 1)
+
+# f32 operations per iteration of x <- x*a + b with the reference's Dekker
+# two_prod (a's split precomputed): ds_mul 25 (two_prod 13, cross 3, two_sum
+# 6, low word 3) + ds_add 20.
+REC_F32_OPS = 45
+FP32_LANES_PER_SM = 128
+SMS = 148
+
+
+def _events():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _time_calls(fn, steps, warmup=3, families=()):
+    """Device time per call of fn (CUDA events on the current stream, ms),
+    and the named kernel families' device time per call (ms): the family
+    events are taken in a second pass, so they do not disturb the first."""
+    import torch
+    from ds_b200 import _lib
+    stream = torch.cuda.current_stream()
+    out = None
+    for _ in range(warmup):
+        out = fn()
+    torch.cuda.synchronize()
+    e0, e1 = _events()
+    e0.record(stream)
+    for _ in range(steps):
+        out = fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    fam = {}
+    if families:
+        _lib.profile_reset()
+        _lib.profile_enable(True)
+        for _ in range(steps):
+            fn()
+        torch.cuda.synchronize()
+        _lib.profile_enable(False)
+        for f in families:
+            t, n = _lib.profile_read(f)
+            fam[f] = t / steps if n else None
+    return ms, fam, out
+
+
+def _hbm_roofline(bytes_per_call, kernel_ms, family, peaks, peak_src, workload):
+    ach = bytes_per_call / (kernel_ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": family, "achieved": round(ach, 1),
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4),
+            "traffic": ncu_traffic(family, workload), "peak_source": f"{peak_src} hbm_gbs",
+            "kernel_ms": round(kernel_ms, 4)}
+
+
+def _cpu_rate(fn, work, reps=1):
+    fn()
+    t = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return work * reps / (time.perf_counter() - t) / 1e9
+
+
+def config1_lines(dev, peaks, peak_src):
+    """Config 1: y = (a + b) * c on f64 inputs (U[-1,1], seed 0) through the
+    DS chain, recombined to f64; at the config's 2^20 (32 MiB, L2-resident:
+    no flush) and at 2^26 (2 GiB per call, above L2)."""
     import torch
     from ds_b200 import ops
-    from oracle import exact
+    from oracle import dso
     out = {}
-    n = 1 << 26
-    rng = np.random.default_rng(0)
-    a = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
-    b = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
-    c = torch.from_numpy(rng.uniform(-1, 1, n)).to(dev)
-    for _ in range(3):
-        y = ops.ds_fused_add_mul3_to_f64(a, b, c)
+    for lg in (20, 26):
+        n = 1 << lg
+        rng = np.random.default_rng(0)
+        a, b, c = (rng.uniform(-1, 1, n) for _ in range(3))
+        da, db, dc = (torch.from_numpy(v).to(dev) for v in (a, b, c))
+        fn = lambda: ops.ds_fused_add_mul3_to_f64(da, db, dc)  # noqa: E731
+        ms, fam, y = _time_calls(fn, 50 if lg == 20 else 20, families=("elementwise",))
+        got = y.cpu().numpy()
+        m = min(n, 1 << 22)
+        want = dso.ds_fused_add_mul3_to_f64(a[:m], b[:m], c[:m], dso.max_threads())
+        line = {"n": n, "ms": round(ms, 4), "GB/s": round(32.0 * n / (ms * 1e-3) / 1e9, 1),
+                "bytes_per_elem": 32,
+                "l2": "fits in L2 (no flush: the config's size)" if lg == 20
+                      else "inputs and output exceed the 126 MB L2",
+                "roofline": _hbm_roofline(32.0 * n, fam["elementwise"], "elementwise", peaks,
+                                          peak_src, f"fused_add_mul{n}"),
+                "bit_exact_vs_oracle": bool(np.array_equal(got[:m].view(np.uint64),
+                                                           want.view(np.uint64))),
+                "bit_exact_checked": m,
+                "max_abs_err_vs_numpy_f64": float(np.max(np.abs(got - (a + b) * c)))}
+        # e2e through the public op: pinned inputs copied in, the result out
+        ha, hb, hc = (torch.from_numpy(v).pin_memory() for v in (a, b, c))
+        hy = torch.empty(n, dtype=torch.float64).pin_memory()
+
+        def e2e():
+            da.copy_(ha, non_blocking=True)
+            db.copy_(hb, non_blocking=True)
+            dc.copy_(hc, non_blocking=True)
+            hy.copy_(ops.ds_fused_add_mul3_to_f64(da, db, dc), non_blocking=True)
+        ems, _, _ = _time_calls(e2e, 5 if lg == 26 else 20)
+        line["e2e"] = {"GB/s": round(32.0 * n / (ems * 1e-3) / 1e9, 1), "ms": round(ems, 4),
+                       "h2d_bytes_per_step": 24 * n, "d2h_bytes_per_step": 8 * n}
+        ms_ = min(n, 1 << 24)
+        one = _cpu_rate(lambda: dso.ds_fused_add_mul3_to_f64(a[:ms_], b[:ms_], c[:ms_], 1),
+                        32.0 * ms_)
+        th = dso.max_threads()
+        allc = _cpu_rate(lambda: dso.ds_fused_add_mul3_to_f64(a[:ms_], b[:ms_], c[:ms_], th),
+                         32.0 * ms_, reps=3)
+        line["cpu_baseline"] = {"value": round(allc, 3), "unit": "GB/s", "cores": th,
+                                "kind": "port", "single_thread_GB/s": round(one, 3),
+                                "sample": f"{ms_} elements of (a+b)*c through the C "
+                                          "restatement of the reference ops"}
+        out[f"n_2^{lg}"] = line
+        del da, db, dc, y, ha, hb, hc, hy
+    return out
+
+
+def config2_lines(dev, peaks, peak_src):
+    """Config 2: DS sum of x_i = s_i 1e8 + u_i 1e-3 (s alternating, u ~ U[0,1),
+    seed 1) at N = 10^4 (launch-bound) and 2^26 (512 MiB)."""
+    import torch
+    from ds_b200 import ops
+    from oracle import dso, exact
+    out = {}
+    for n in (10_000, 1 << 26):
+        s = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)
+        x = s * 1e8 + np.random.default_rng(1).uniform(0, 1, n) * 1e-3
+        dx = torch.from_numpy(x).to(dev)
+        fn = lambda: ops.ds_sum_f64(dx)  # noqa: E731
+        steps = 200 if n == 10_000 else 20
+        ms, fam, r = _time_calls(fn, steps, families=("reduce",))
+        truth = exact.exact_sum(x)
+        h, l = dso.ds_reduce_f64_seq(x)
+        err = abs(float(r.item()) - truth)
+        ref_err = abs(float(h) + float(l) - truth)
+        line = {"n": n, "ms": round(ms, 5), "GB/s": round(8.0 * n / (ms * 1e-3) / 1e9, 1),
+                "bytes_per_elem": 8, "abs_err_vs_fsum": err,
+                "reference_ds_seq_abs_err": ref_err, "err_le_reference": err <= ref_err,
+                "f32_abs_err": abs(float(np.sum(x.astype(np.float32), dtype=np.float32)) - truth)}
+        if n == 10_000:
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            for _ in range(steps):
+                fn()
+            host_us = (time.perf_counter() - t) / steps * 1e6
+            torch.cuda.synchronize()
+            kus = fam["reduce"] * 1e3
+            line.update({"us_per_call": round(ms * 1e3, 2), "kernel_us": round(kus, 2),
+                         "host_us_per_call": round(host_us, 2),
+                         "bound": "launch: the two kernels (block partials, their fold) run "
+                                  f"{kus:.1f} us; back-to-back calls cost "
+                                  f"{ms * 1e3:.1f} us each on the device and {host_us:.1f} us "
+                                  "of host time (Python op, argument checks, launches)"})
+        else:
+            line["roofline"] = _hbm_roofline(8.0 * n, fam["reduce"], "reduce", peaks, peak_src,
+                                             f"reduce{n}")
+        m = min(n, 1 << 24)
+        rate = _cpu_rate(lambda: dso.ds_reduce_f64_seq(x[:m]), 8.0 * m)
+        line["cpu_baseline"] = {"value": round(rate, 3), "unit": "GB/s", "cores": 1,
+                                "kind": "port",
+                                "sample": f"sequential DS fold of {m} elements (the reference "
+                                          "reduce body in index order; one thread, as the "
+                                          "order is sequential)"}
+        out["n_10^4" if n == 10_000 else "n_2^26"] = line
+        del dx
+    return out
+
+
+def config4_lines(dev, peaks, clock_mhz):
+    """Config 4: x <- x*a + b, k = 1 .. 1024 times, 2^24 elements (seed 3)."""
+    import torch
+    from ds_b200 import ops
+    from oracle import dso
+    n = 1 << 24
+    rng = np.random.default_rng(3)
+    x0 = rng.uniform(-1, 1, n)
+    a = rng.uniform(0.999, 1.001, n)
+    b = rng.uniform(-1e-3, 1e-3, n)
+    dx, da, db = (torch.from_numpy(v).to(dev) for v in (x0, a, b))
+    pipe = SMS * FP32_LANES_PER_SM * clock_mhz * 1e6  # f32 ops/s of the FP32 pipe
+    sweep = []
+    y = None
+    for k in REC_KS:
+        fn = lambda k=k: ops.ds_recurrence_mul_add_to_f64(dx, da, db, k)  # noqa: E731
+        steps = max(2, min(20, int(2000 / k)))
+        ms, fam, y = _time_calls(fn, steps, families=("recurrence",))
+        kms = fam["recurrence"]
+        ops_s = REC_F32_OPS * n * k / (kms * 1e-3)
+        sweep.append({"k": k, "ms": round(ms, 4), "GB/s": round(32.0 * n / (ms * 1e-3) / 1e9, 1),
+                      "Gelem_iter_per_s": round(n * k / (ms * 1e-3) / 1e9, 2),
+                      "fp32_pipe_frac": round(ops_s / pipe, 4),
+                      "hbm_frac": round(32.0 * n / (kms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)})
+    m = 1 << 16
+    got = y[:m].cpu().numpy()
+    want = dso.ds_recurrence_mul_add_to_f64(x0[:m], a[:m], b[:m], REC_KS[-1], dso.max_threads())
+    # the reference's own form, z <- (z + y) * y (x0 as z, a as y)
+    ref_ms, _, _ = _time_calls(lambda: ops.ds_recurrence_add_mul_to_f64_cuda(dx, da, 1024), 2)
+    th = dso.max_threads()
+    mm = 1 << 18
+    rate = _cpu_rate(lambda: dso.ds_recurrence_mul_add_to_f64(x0[:mm], a[:mm], b[:mm], 1024, th),
+                     float(mm) * 1024)
+    out = {"n": n, "sweep": sweep, "f32_ops_per_iteration": REC_F32_OPS,
+           "fp32_pipe_peak": f"{SMS} SMs x {FP32_LANES_PER_SM} lanes x {clock_mhz:.0f} MHz",
+           "bit_exact_vs_oracle_k1024": bool(np.array_equal(got.view(np.uint64),
+                                                            want.view(np.uint64))),
+           "bit_exact_checked": m,
+           "reference_form_(z+y)*y_k1024": {
+               "ms": round(ref_ms, 4),
+               "Gelem_iter_per_s": round(n * 1024 / (ref_ms * 1e-3) / 1e9, 2)},
+           "cpu_baseline": {"value": round(rate, 3), "unit": "Gelem-iter/s", "cores": th,
+                            "kind": "port", "sample": f"{mm} elements, k=1024, C restatement"}}
+    del dx, da, db, y
+    return out
+
+
+def config5_lines(dev, peaks, peak_src):
+    """Config 5 on one GPU: the 65536 x 8192 x 8192 product and the batched
+    dot (4096 x 65536), entries 1 + 1e-7 u (seed 4, drawn A, B, X, Y)."""
+    import torch
+    from ds_b200 import _lib, ops
+    from oracle import ds_pass_ref, exact
+    out = {}
+    A, B, _ = large_inputs("gemm_large", 0, 1)
+    dA, dB = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+    ms, fam, C = _time_calls(lambda: ops.ds_matmul_f64(dA, dB), 3, warmup=1,
+                             families=("ozaki_gemm",))
+    info = _lib.gemm_info(LARGE_M, LARGE_N, LARGE_K)
+    ach = info["tensor_ops_per_launch"] / (fam["ozaki_gemm"] * 1e-3) / 1e12
+    peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    rows, cols = exact.sample_indices(LARGE_M, LARGE_N, 64, seed=5)
+    Ch = C.cpu().numpy()
+    truth = exact.exact_gemm_entries(A, B, rows, cols)
+    err = np.abs(Ch[rows, cols] - truth)
+    ref_err = reference_gemm_error(A, B, rows, cols, truth)
+    sub = A[:256]
+    rate = _cpu_rate(lambda: ds_pass_ref.dot_general_f64(sub, B), 2.0 * 256 * LARGE_N * LARGE_K)
+    out["gemm"] = {
+        "M": LARGE_M, "N": LARGE_N, "K": LARGE_K, "ms": round(ms, 3),
+        "GFLOP/s": round(2.0 * LARGE_M * LARGE_N * LARGE_K / (ms * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "tensor", "kernel": "ozaki_gemm", "achieved": round(ach, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4),
+                     "traffic": None, "kernel_ms": round(fam["ozaki_gemm"], 3),
+                     "peak_source": f"2 x {peak_src} bf16_tflops_sustained (a ~45 ms kernel "
+                                    "run back to back)"},
+        "accuracy": {"max_abs_err_vs_exact": float(err.max()),
+                     "reference_ds_path_max_abs_err": ref_err,
+                     "err_le_reference": bool(np.all(err <= ref_err)),
+                     "sampled_entries": int(len(rows))},
+        "cpu_baseline": {"value": round(rate, 2), "unit": "GFLOP/s", "cores": host_cores(),
+                         "kind": "port", "sample": "256 rows of A times B: the DS pass in NumPy"}}
+    del dA, dB, C, Ch, A, B
+    torch.cuda.empty_cache()
+    X, Y, _ = large_inputs("batched_dot", 0, 1)
+    dX, dY = torch.from_numpy(X).to(dev), torch.from_numpy(Y).to(dev)
+    fn = lambda: ops.ds_dot_general_f64(dX, dY, lhs_contracting=1, rhs_contracting=1,  # noqa
+                                        lhs_batch=(0,), rhs_batch=(0,))
+    ms, fam, d = _time_calls(fn, 10, families=("dot_vec",))
+    nbytes = 2.0 * BATCH_DOTS * DOT_LEN * 8
+    got = d.cpu().numpy()
+    idx = np.arange(0, BATCH_DOTS, BATCH_DOTS // 16)
+    truth = np.array([exact.exact_dot(X[i], Y[i]) for i in idx])
+    ah, al = ds_pass_ref.from_float(X[idx])
+    bh, bl = ds_pass_ref.from_float(Y[idx])
+    p = np.einsum("ik,ik->i", ah, bh)
+    e = (np.einsum("ik,ik->i", ah, bl) + np.einsum("ik,ik->i", al, bh)) + \
+        np.einsum("ik,ik->i", al, bl)
+    ref = ds_pass_ref.to_float(*ds_pass_ref.two_sum(p, e))
+    derr = np.abs(got[idx] - truth)
+    rerr = np.abs(ref - truth)
+
+    def host_dots():
+        h1, l1 = ds_pass_ref.from_float(X[:256])
+        h2, l2 = ds_pass_ref.from_float(Y[:256])
+        return ds_pass_ref.two_sum(np.einsum("ik,ik->i", h1, h2),
+                                   (np.einsum("ik,ik->i", h1, l2) +
+                                    np.einsum("ik,ik->i", l1, h2)) + np.einsum("ik,ik->i", l1, l2))
+    rate = _cpu_rate(host_dots, 2.0 * 256 * DOT_LEN * 8)
+    out["batched_dot"] = {
+        "batch": BATCH_DOTS, "length": DOT_LEN, "ms": round(ms, 3),
+        "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes_per_mac": 16,
+        "roofline": _hbm_roofline(nbytes, fam["dot_vec"], "dot_vec", peaks, peak_src,
+                                  "batched_dot"),
+        "accuracy": {"max_abs_err_vs_exact": float(derr.max()),
+                     "reference_ds_path_max_abs_err": float(rerr.max()),
+                     "err_le_reference": bool(np.all(derr <= rerr)), "sampled_dots": len(idx)},
+        "cpu_baseline": {"value": round(rate, 2), "unit": "GB/s", "cores": host_cores(),
+                         "kind": "port", "sample": "256 of the dot products: the DS pass in NumPy"}}
+    del dX, dY, d, X, Y
+    torch.cuda.empty_cache()
+    return out
+
+
+def config5_strong(dev, rank, world, barrier, max_over_ranks):
+    """Config 5's product strong-scaled over the N ranks: the 65536 rows of A
+    split across them, B drawn on rank 0 and broadcast before timing.  T1,
+    the whole product on rank 0 alone, is measured in the same run while the
+    other ranks wait, so the efficiency T1 / (N T_N) needs no other run.  e2e
+    adds each rank's pinned A block copied in and C block copied out."""
+    import torch
+    from ds_b200 import ops
+    from ds_b200 import dist as dsd
+    if rank == 0:
+        B = torch.from_numpy(large_draw(LARGE_M * LARGE_K, (LARGE_K, LARGE_N))).to(dev)
+    else:
+        B = torch.empty((LARGE_K, LARGE_N), dtype=torch.float64, device=dev)
+    dsd.replicate(B, src=0)
+    r0, r1 = shard_rows(LARGE_M, rank, world)
+    hA = torch.from_numpy(large_draw(r0 * LARGE_K, (r1 - r0, LARGE_K))).pin_memory()
+    dA = hA.to(dev)
+    t1 = None
+    if rank == 0:
+        full = torch.from_numpy(large_draw(0, (LARGE_M, LARGE_K))).to(dev)
+        t1, _, c = _time_calls(lambda: ops.ds_matmul_f64(full, B), 2, warmup=1)
+        del full, c
+        torch.cuda.empty_cache()
+    stream = torch.cuda.current_stream()
+    C = None
+    for _ in range(2):
+        C = ops.ds_matmul_f64(dA, B)
+    barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    e0.record()
-    for _ in range(reps):
-        y = ops.ds_fused_add_mul3_to_f64(a, b, c)
-    e1.record()
+    steps = 3
+    e0, e1 = _events()
+    e0.record(stream)
+    for _ in range(steps):
+        C = ops.ds_matmul_f64(dA, B)
+    e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    out["fused_add_mul3_2p26"] = {"GB/s": round(32.0 * n / (ms * 1e-3) / 1e9, 1),
-                                  "ms": round(ms, 4), "bytes_per_elem": 32}
-    del a, b, c, y
-    s = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)
-    x = s * 1e8 + np.random.default_rng(1).uniform(0, 1, n) * 1e-3
-    dx = torch.from_numpy(x).to(dev)
-    for _ in range(3):
-        r = ops.ds_sum_f64(dx)
+    barrier()
+    tn = max_over_ranks(e0.elapsed_time(e1) / steps)
+    hC = torch.empty(C.shape, dtype=torch.float64).pin_memory()
+    barrier()
     torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        r = ops.ds_sum_f64(dx)
-    e1.record()
+    e0.record(stream)
+    for _ in range(steps):
+        dA.copy_(hA, non_blocking=True)
+        C = ops.ds_matmul_f64(dA, B)
+        hC.copy_(C, non_blocking=True)
+    e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    truth = exact.exact_sum(x)
-    out["ds_sum_2p26"] = {"GB/s": round(8.0 * n / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
-                          "abs_err_vs_fsum": abs(float(r.item()) - truth)}
+    barrier()
+    te = max_over_ranks(e0.elapsed_time(e1) / steps)
+    del dA, B, C
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    flops = 2.0 * LARGE_M * LARGE_N * LARGE_K
+    return {"what": "65536x8192x8192 DS GEMM, rows of A split over the ranks, B replicated "
+                    "(broadcast before timing); value is the whole job",
+            "n_gpus": world, "rows_per_rank": int(r1 - r0),
+            "ms_per_step": round(tn, 3), "GFLOP/s": round(flops / (tn * 1e-3) / 1e9, 1),
+            "single_gpu_ms_same_run": round(t1, 3),
+            "efficiency_vs_single_gpu": round(t1 / (world * tn), 4),
+            "e2e": {"ms_per_step": round(te, 3), "GFLOP/s": round(flops / (te * 1e-3) / 1e9, 1),
+                    "h2d_bytes_per_step_per_rank": int(hA.numel() * 8),
+                    "d2h_bytes_per_step_per_rank": int(hC.numel() * 8),
+                    "note": "each rank's copies cross its own PCIe link"}}
+
+
+def int8_library_line(dev, ours_kernel_ms):
+    """cuBLASLt's int8 GEMM (torch._int_mm, s8 x s8 -> s32) at 4096^3 and
+    8192^3 on the same GPU, beside the product's own int8 GEMM kernel (14
+    residue GEMMs of 4096^3 per launch)."""
+    import torch
+    out = {}
+    for n in (4096, 8192):
+        a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev)
+        b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev)
+        ms, _, _ = _time_calls(lambda: torch._int_mm(a, b), 20 if n == 4096 else 10)
+        out[f"cublaslt_int8_{n}^3_TOPS"] = round(2.0 * n ** 3 / (ms * 1e-3) / 1e12, 1)
+        del a, b
+    if ours_kernel_ms:
+        ours = 14 * 2.0 * 4096 ** 3 / (ours_kernel_ms * 1e-3) / 1e12
+        out["ozaki_gemm_4096^3_TOPS"] = round(ours, 1)
+        out["ozaki_gemm_over_cublaslt_4096"] = round(ours / out["cublaslt_int8_4096^3_TOPS"], 3)
+    return out
+
+
+def every_config(dev, clk, ours_kernel_ms):
+    """The other configurations, each with its roofline, CPU baseline and
+    exactness flag (rank 0, N = 1)."""
+    peaks, peak_src = measured_peaks()
+    mhz = (clk or {}).get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    out = {}
+    for name, fn in (("config1_fused_add_mul", lambda: config1_lines(dev, peaks, peak_src)),
+                     ("config2_ds_sum", lambda: config2_lines(dev, peaks, peak_src)),
+                     ("config4_recurrence", lambda: config4_lines(dev, peaks, mhz)),
+                     ("config5", lambda: config5_lines(dev, peaks, peak_src)),
+                     ("int8_library_gemm", lambda: int8_library_line(dev, ours_kernel_ms))):
+        t = time.perf_counter()
+        out[name] = fn()
+        out[name]["host_seconds"] = round(time.perf_counter() - t, 1)
     return out
 
 
@@ -686,39 +1049,35 @@ def cpu_baseline_stream(wl, host_in, threads=None):
             "sample": sample}
 
 
-REF_ROWS = 1024  # rows of A per reference step (a quarter of the GEMM)
-
-
 def run_reference(args):
-    """Each step multiplies one 1024-row block of A (cycling over the four
-    blocks) by B through the NumPy restatement of the reference DS pass, so a
-    step is about 0.3 s of host work; GFLOP/s counts that block's 2*m*N*K."""
+    """Each step is one full 4096^3 product (one rank's block of the weak-scaled
+    job; at N > 1 rank 0 runs it for the whole job, value being a rate)
+    through the NumPy restatement of the reference DS pass on all host cores:
+    split, four float32 matmuls with f32 accumulation, two_sum, recombine.
+    The reference itself needs JAX/XLA, absent in this image."""
     rank, world, _ = env_rank()
     if rank != 0:
         return None
     A, B = gemm_inputs(0)
     from oracle import ds_pass_ref
-    blocks = [A[i:i + REF_ROWS] for i in range(0, GEMM_DIM, REF_ROWS)]
-    for i in range(args.warmup):
-        ds_pass_ref.dot_general_f64(blocks[i % len(blocks)], B)
+    for _ in range(args.warmup):
+        ds_pass_ref.dot_general_f64(A, B)
     t = time.perf_counter()
-    for i in range(args.steps):
-        ds_pass_ref.dot_general_f64(blocks[i % len(blocks)], B)
+    for _ in range(args.steps):
+        ds_pass_ref.dot_general_f64(A, B)
     dt = (time.perf_counter() - t) / args.steps
-    value = 2.0 * REF_ROWS * GEMM_DIM * GEMM_DIM / dt / 1e9
+    value = 2.0 * GEMM_DIM ** 3 / dt / 1e9
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "GFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32x2 (DS)", "data": "synthetic (default_rng(2))",
-        "config": {"workload": "ds_dot_general_f64 4096x4096x4096 (A, B f64 U[-1,1] seed 2)",
-                   "M": GEMM_DIM, "N": GEMM_DIM, "K": GEMM_DIM},
+        "config": gemm_config(world, args.algorithm),
         "cpu_baseline": {"value": round(value, 2), "unit": "GFLOP/s", "cores": host_cores(),
                          "kind": "port",
-                         "sample": f"per step a {REF_ROWS}x4096 block of A times B (4096^2): "
-                                   "the DS pass restated in NumPy (split, 4 float32 matmuls, "
-                                   "two_sum, recombine) with BLAS on all host cores; the "
-                                   "reference needs JAX/XLA, absent in this image"},
+                         "sample": "one full 4096^3 DS GEMM per step: the DS pass restated in "
+                                   "NumPy (split, 4 float32 matmuls, two_sum, recombine) with "
+                                   "BLAS on all host cores"},
         "e2e": {"value": round(value, 2), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -37,6 +37,8 @@ def test_reference_arm_gemm_line():
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["metric"] == bench.METRIC
+    # the same workload dict as the GPU arm's line, one full 4096^3 per step
+    assert line["config"] == bench.gemm_config(1, "tensor")
 
 
 def test_reference_arm_stream_line():
