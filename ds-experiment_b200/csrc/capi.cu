@@ -2,6 +2,7 @@
 // the reference handlers' messages, then the launchers in kernels.h.
 #include <cstring>
 #include <mutex>
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -151,88 +152,211 @@ int reduce_geometry(const char* op, const ds_buffer* in, const int64_t* dims, in
   return DS_OK;
 }
 
-struct DotGeom {
-  int64_t batch = 1, M = 1, N = 1, K = 0;
-  int64_t a_sb = 0, a_sr = 0, a_sk = 1;
-  int64_t b_sb = 0, b_sr = 0, b_sk = 1;
+// One operand of dot_general as the products read it: its dimensions
+// grouped into batch (in the order of the batching list), free (ascending:
+// the result's order) and contracting (in the order of the contracting
+// list, which pairs them with the other operand's).  Each group is one
+// index, (batch, rows, K), with one element stride when the group's
+// dimensions nest (each outer stride = inner stride x inner size, unit
+// dimensions ignored); otherwise the operand is first copied to a
+// contiguous [batch][rows][K] buffer in the workspace.
+struct DotSide {
+  int64_t batch = 1, rows = 1, K = 1;
+  int64_t s_b = 0, s_r = 0, s_k = 0;
+  bool nested = true;
+  int nd = 0;                       // the copy: dimensions in group order ...
+  int64_t size[DS_DOT_MAX_DIMS];    // ... their sizes
+  int64_t stride[DS_DOT_MAX_DIMS];  // ... and strides in the operand
 };
 
-// Operand view of one dot_general side: [batch..., free?, K] in any order of
-// the last two dims.
-int dot_side(const ds_buffer* x, int64_t nb, int64_t contracting, int64_t& rows, int64_t& K,
-             int64_t& s_b, int64_t& s_r, int64_t& s_k) {
-  const int64_t r = x->rank;
-  if (r != nb + 1 && r != nb + 2) return invalid("dot_general: each operand must have one free dimension at most");
-  if (contracting < nb || contracting >= r) return invalid("dot_general: contracting dimension must follow the batch dimensions");
-  int64_t inner = 1;
-  for (int64_t i = nb; i < r; ++i) inner *= x->dims[i];
-  s_b = inner;
-  K = x->dims[contracting];
-  if (r == nb + 1) {
-    rows = 1;
-    s_r = 0;
-    s_k = 1;
-  } else if (contracting == r - 1) {
-    rows = x->dims[r - 2];
-    s_r = K;
-    s_k = 1;
-  } else {
-    rows = x->dims[r - 1];
-    s_r = 1;
-    s_k = rows;
+struct DotGeom {
+  int64_t batch = 1, M = 1, N = 1, K = 1;
+  DotSide a, b;
+};
+
+// Sizes and strides of `idx` (n dimensions of x) nested into one index.
+bool nest(const int64_t* dims, const int64_t* strides, const int64_t* idx, int64_t n,
+          int64_t& size, int64_t& stride) {
+  size = 1;
+  stride = 0;
+  bool ok = true;
+  for (int64_t t = n - 1; t >= 0; --t) {
+    const int64_t len = dims[idx[t]];
+    if (len == 1) continue;
+    if (size == 1) {
+      stride = strides[idx[t]];
+    } else if (strides[idx[t]] != stride * size) {
+      ok = false;
+    }
+    size *= len;
   }
+  return ok;
+}
+
+int dot_side(const ds_buffer* x, const int64_t* batch, int64_t nb, const int64_t* contracting,
+             int64_t nc, DotSide& d, std::vector<int64_t>& free_dims) {
+  const int64_t r = x->rank;
+  if (r > DS_DOT_MAX_DIMS)
+    return invalid("dot_general: operands of rank above " + std::to_string(DS_DOT_MAX_DIMS) +
+                   " are not supported");
+  int64_t strides[DS_DOT_MAX_DIMS];
+  for (int64_t i = r - 1, s = 1; i >= 0; --i) {
+    strides[i] = s;
+    s *= x->dims[i];
+  }
+  int role[DS_DOT_MAX_DIMS] = {0};  // 0 free, 1 batch, 2 contracting
+  for (int64_t i = 0; i < nb; ++i) {
+    if (batch[i] < 0 || batch[i] >= r || role[batch[i]])
+      return invalid("dot_general: batching dimensions out of range or repeated");
+    role[batch[i]] = 1;
+  }
+  for (int64_t i = 0; i < nc; ++i) {
+    if (contracting[i] < 0 || contracting[i] >= r || role[contracting[i]])
+      return invalid("dot_general: contracting dimensions out of range or repeated");
+    role[contracting[i]] = 2;
+  }
+  free_dims.clear();
+  for (int64_t i = 0; i < r; ++i)
+    if (role[i] == 0) free_dims.push_back(i);
+  bool ok = nest(x->dims, strides, batch, nb, d.batch, d.s_b);
+  ok = nest(x->dims, strides, free_dims.data(), static_cast<int64_t>(free_dims.size()), d.rows,
+            d.s_r) && ok;
+  ok = nest(x->dims, strides, contracting, nc, d.K, d.s_k) && ok;
+  d.nested = ok;
+  d.nd = 0;
+  auto add = [&](int64_t dim) {
+    d.size[d.nd] = x->dims[dim];
+    d.stride[d.nd] = strides[dim];
+    ++d.nd;
+  };
+  for (int64_t i = 0; i < nb; ++i) add(batch[i]);
+  for (int64_t dim : free_dims) add(dim);
+  for (int64_t i = 0; i < nc; ++i) add(contracting[i]);
   return DS_OK;
 }
 
 int dot_geometry(const ds_buffer* lhs, const ds_buffer* rhs, const ds_dot_dims* dd,
                  const ds_buffer* out, DotGeom& g) {
   if (dd == nullptr) return invalid("dot_general: missing dimension numbers");
-  const int64_t nb = dd->n_batch;
-  if (nb < 0 || nb > 4) return invalid("dot_general: at most 4 batch dimensions");
-  g.batch = 1;
-  for (int64_t i = 0; i < nb; ++i) {
-    if (dd->lhs_batch[i] != i || dd->rhs_batch[i] != i)
-      return invalid("dot_general: batch dimensions must be the leading dimensions");
-    if (i >= lhs->rank || i >= rhs->rank || lhs->dims[i] != rhs->dims[i])
-      return invalid("dot_general: batch dimensions must match");
-    g.batch *= lhs->dims[i];
+  const int64_t nb = dd->n_batch, nc = dd->n_contracting;
+  if (nb < 0 || nb > DS_DOT_MAX_DIMS || nc < 0 || nc > DS_DOT_MAX_DIMS)
+    return invalid("dot_general: bad count of batching or contracting dimensions");
+  std::vector<int64_t> lfree, rfree;
+  if (int st = dot_side(lhs, dd->lhs_batch, nb, dd->lhs_contracting, nc, g.a, lfree)) return st;
+  if (int st = dot_side(rhs, dd->rhs_batch, nb, dd->rhs_contracting, nc, g.b, rfree)) return st;
+  // The contracting pairs may be taken in any order (the sum does not
+  // depend on it): of the given order and the pairs sorted by the lhs or the
+  // rhs dimension, the one whose operands nest best (fewest copies) is used.
+  if (nc > 1 && !(g.a.nested && g.b.nested)) {
+    auto copies = [](const DotSide& a, const DotSide& b) {
+      return (a.nested ? 0 : a.batch * a.rows * a.K) + (b.nested ? 0 : b.batch * b.rows * b.K);
+    };
+    int64_t best = copies(g.a, g.b);
+    for (int by = 0; by < 2; ++by) {
+      std::vector<int64_t> order(nc);
+      for (int64_t i = 0; i < nc; ++i) order[i] = i;
+      const int64_t* key = by == 0 ? dd->lhs_contracting : dd->rhs_contracting;
+      std::sort(order.begin(), order.end(), [key](int64_t x, int64_t y) { return key[x] < key[y]; });
+      int64_t lc[DS_DOT_MAX_DIMS], rc[DS_DOT_MAX_DIMS];
+      for (int64_t i = 0; i < nc; ++i) {
+        lc[i] = dd->lhs_contracting[order[i]];
+        rc[i] = dd->rhs_contracting[order[i]];
+      }
+      DotSide a, b;
+      std::vector<int64_t> f1, f2;
+      dot_side(lhs, dd->lhs_batch, nb, lc, nc, a, f1);
+      dot_side(rhs, dd->rhs_batch, nb, rc, nc, b, f2);
+      if (copies(a, b) < best) {
+        best = copies(a, b);
+        g.a = a;
+        g.b = b;
+      }
+    }
   }
-  int64_t Ka = 0, Kb = 0;
-  if (int st = dot_side(lhs, nb, dd->lhs_contracting, g.M, Ka, g.a_sb, g.a_sr, g.a_sk)) return st;
-  if (int st = dot_side(rhs, nb, dd->rhs_contracting, g.N, Kb, g.b_sb, g.b_sr, g.b_sk)) return st;
-  if (Ka != Kb) return invalid("dot_general: contracting dimensions must match");
-  g.K = Ka;
-  // Result: [batch..., lhs free?, rhs free?].
-  std::vector<int64_t> want(lhs->dims, lhs->dims + nb);
-  if (lhs->rank == nb + 2) want.push_back(g.M);
-  if (rhs->rank == nb + 2) want.push_back(g.N);
+  for (int64_t i = 0; i < nb; ++i)
+    if (lhs->dims[dd->lhs_batch[i]] != rhs->dims[dd->rhs_batch[i]])
+      return invalid("dot_general: batch dimensions must match");
+  for (int64_t i = 0; i < nc; ++i)
+    if (lhs->dims[dd->lhs_contracting[i]] != rhs->dims[dd->rhs_contracting[i]])
+      return invalid("dot_general: contracting dimensions must match");
+  g.batch = g.a.batch;
+  g.M = g.a.rows;
+  g.N = g.b.rows;
+  g.K = g.a.K;
+  // Result: [batch (lhs order)..., lhs free..., rhs free...], row-major.
+  std::vector<int64_t> want;
+  for (int64_t i = 0; i < nb; ++i) want.push_back(lhs->dims[dd->lhs_batch[i]]);
+  for (int64_t d : lfree) want.push_back(lhs->dims[d]);
+  for (int64_t d : rfree) want.push_back(rhs->dims[d]);
   if (out->rank != static_cast<int64_t>(want.size())) return invalid("dot_general: output shape mismatch");
   for (size_t i = 0; i < want.size(); ++i)
     if (out->dims[i] != want[i]) return invalid("dot_general: output shape mismatch");
   return DS_OK;
 }
 
+// Bytes of the contiguous copy of a side that does not nest (8 per element:
+// one f64, or an f32 hi and an f32 lo), 256-byte aligned.
+size_t side_copy_bytes(const DotSide& d, int64_t rows) {
+  if (d.nested) return 0;
+  const size_t n = static_cast<size_t>(d.batch) * rows * d.K;
+  return (n * 8 + 255) / 256 * 256;
+}
+
 size_t dot_workspace(const DotGeom& g, int32_t algorithm) {
-  if (g.M == 1 && g.N == 1) return dot_vec_workspace_bytes(g.batch, g.K);
+  const size_t copies = side_copy_bytes(g.a, g.M) + side_copy_bytes(g.b, g.N);
+  if (g.M == 1 && g.N == 1) return copies + dot_vec_workspace_bytes(g.batch, g.K);
   if (algorithm == DS_DOT_TENSOR_INT8 && dot_ozaki_supported(g.M, g.N, g.K))
-    return dot_ozaki_workspace_bytes(g.batch, g.M, g.N, g.K);
-  return 0;
+    return copies + dot_ozaki_workspace_bytes(g.batch, g.M, g.N, g.K);
+  return copies;
+}
+
+// Copy a side that does not nest into [batch][rows][K] at `at`, and point
+// the operand there.
+int place_side(const DotSide& d, int64_t rows, DotOperand& o, uint8_t*& at, cudaStream_t s) {
+  if (d.nested) {
+    o.s_b = d.s_b;
+    o.s_r = d.s_r;
+    o.s_k = d.s_k;
+    return DS_OK;
+  }
+  const size_t n = static_cast<size_t>(d.batch) * rows * d.K;
+  if (o.f64) {
+    double* dst = reinterpret_cast<double*>(at);
+    if (int st = gather_strided(o.f64, dst, 8, d.size, d.stride, d.nd, s)) return st;
+    o.f64 = dst;
+  } else {
+    float* hi = reinterpret_cast<float*>(at);
+    float* lo = hi + n;
+    if (int st = gather_strided(o.hi, hi, 4, d.size, d.stride, d.nd, s)) return st;
+    if (int st = gather_strided(o.lo, lo, 4, d.size, d.stride, d.nd, s)) return st;
+    o.hi = hi;
+    o.lo = lo;
+  }
+  o.s_b = rows * d.K;
+  o.s_r = d.K;
+  o.s_k = 1;
+  at += side_copy_bytes(d, rows);
+  return DS_OK;
 }
 
 int dot_run(const DotGeom& g, DotProblem& p, int32_t algorithm, void* ws, size_t ws_bytes,
             cudaStream_t s) {
+  if (algorithm != DS_DOT_TENSOR_INT8 && algorithm != DS_DOT_CUDA_CORE)
+    return invalid("dot_general: unknown algorithm");
   p.batch = g.batch;
   p.M = g.M;
   p.N = g.N;
   p.K = g.K;
-  p.a.s_b = g.a_sb;
-  p.a.s_r = g.a_sr;
-  p.a.s_k = g.a_sk;
-  p.b.s_b = g.b_sb;
-  p.b.s_r = g.b_sr;
-  p.b.s_k = g.b_sk;
-  if (algorithm != DS_DOT_TENSOR_INT8 && algorithm != DS_DOT_CUDA_CORE)
-    return invalid("dot_general: unknown algorithm");
+  if (g.batch * g.M * g.N == 0) return ok();
+  const size_t copies = side_copy_bytes(g.a, g.M) + side_copy_bytes(g.b, g.N);
+  if (copies > ws_bytes || (copies && !aligned(ws, 256)))
+    return invalid("dot_general: workspace too small (need " +
+                   std::to_string(dot_workspace(g, algorithm)) + " bytes, 256-byte aligned)");
+  uint8_t* at = static_cast<uint8_t*>(ws);
+  if (int st = place_side(g.a, g.M, p.a, at, s)) return st;
+  if (int st = place_side(g.b, g.N, p.b, at, s)) return st;
+  ws = at;
+  ws_bytes -= copies;
   if (g.M == 1 && g.N == 1) return dot_batched_vec(p, ws, ws_bytes, s);
   if (algorithm == DS_DOT_TENSOR_INT8 && dot_ozaki_supported(g.M, g.N, g.K))
     return dot_ozaki(p, ws, ws_bytes, s);
@@ -576,18 +700,24 @@ int ds_reduce_f64_noalloc(const ds_buffer* in, const ds_buffer* init,
 
 size_t ds_dot_general_workspace_size(const ds_buffer* lhs, const ds_buffer* rhs,
                                      const ds_dot_dims* dims, int32_t algorithm) {
-  if (!valid_buffer(lhs) || !valid_buffer(rhs) || bad_dims(lhs) || bad_dims(rhs)) return 0;
-  DotGeom g;
-  // Build the expected output descriptor from the operands to reuse the checks.
-  std::vector<int64_t> od;
-  if (dims == nullptr || dims->n_batch < 0 || dims->n_batch > 4) return 0;
-  for (int64_t i = 0; i < dims->n_batch && i < lhs->rank; ++i) od.push_back(lhs->dims[i]);
-  const int64_t nb = dims->n_batch;
-  if (lhs->rank == nb + 2) od.push_back(lhs->dims[dims->lhs_contracting == nb + 1 ? nb : nb + 1]);
-  if (rhs->rank == nb + 2) od.push_back(rhs->dims[dims->rhs_contracting == nb ? nb + 1 : nb]);
-  ds_buffer out{nullptr, od.data(), static_cast<int64_t>(od.size())};
+  if (!valid_buffer(lhs) || !valid_buffer(rhs) || bad_dims(lhs) || bad_dims(rhs) ||
+      dims == nullptr)
+    return 0;
+  // The output descriptor the dimension numbers imply, to reuse the checks.
   const std::string saved = g_last_error;
-  const int st = dot_geometry(lhs, rhs, dims, &out, g);
+  DotGeom g;
+  std::vector<int64_t> lfree, rfree, od;
+  const int64_t nb = dims->n_batch, nc = dims->n_contracting;
+  int st = (nb < 0 || nb > DS_DOT_MAX_DIMS || nc < 0 || nc > DS_DOT_MAX_DIMS) ? DS_INVALID_ARGUMENT
+           : dot_side(lhs, dims->lhs_batch, nb, dims->lhs_contracting, nc, g.a, lfree);
+  if (st == DS_OK) st = dot_side(rhs, dims->rhs_batch, nb, dims->rhs_contracting, nc, g.b, rfree);
+  if (st == DS_OK) {
+    for (int64_t i = 0; i < nb; ++i) od.push_back(lhs->dims[dims->lhs_batch[i]]);
+    for (int64_t d : lfree) od.push_back(lhs->dims[d]);
+    for (int64_t d : rfree) od.push_back(rhs->dims[d]);
+    ds_buffer out{nullptr, od.data(), static_cast<int64_t>(od.size())};
+    st = dot_geometry(lhs, rhs, dims, &out, g);
+  }
   g_last_error = saved;
   if (st != DS_OK) return 0;
   return dot_workspace(g, algorithm);

@@ -28,6 +28,13 @@ int ew_recurrence_add_mul(const double* x, const double* y, double* out, int64_t
 int ew_recurrence_mul_add(const double* x, const double* a, const double* b, double* out,
                           int64_t n, int32_t k, cudaStream_t s);
 
+// layout.cu: dst (contiguous, row-major over size[0..nd)) = src at offsets
+// sum_d index_d * stride[d] (elements of elem_bytes = 4 or 8); unit sizes
+// are skipped, at most kGatherMaxDims others.
+constexpr int kGatherMaxDims = 8;
+int gather_strided(const void* src, void* dst, int elem_bytes, const int64_t* size,
+                   const int64_t* stride, int nd, cudaStream_t s);
+
 // reduce.cu
 struct ReduceArgs {
   const double* in_f64 = nullptr;  // either f64 input ...

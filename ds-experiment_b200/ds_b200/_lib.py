@@ -40,12 +40,16 @@ class DsBuffer(ctypes.Structure):
                 ("rank", ctypes.c_int64)]
 
 
+DS_DOT_MAX_DIMS = 8
+
+
 class DsDotDims(ctypes.Structure):
     _fields_ = [("n_batch", ctypes.c_int64),
-                ("lhs_batch", ctypes.c_int64 * 4),
-                ("rhs_batch", ctypes.c_int64 * 4),
-                ("lhs_contracting", ctypes.c_int64),
-                ("rhs_contracting", ctypes.c_int64)]
+                ("lhs_batch", ctypes.c_int64 * DS_DOT_MAX_DIMS),
+                ("rhs_batch", ctypes.c_int64 * DS_DOT_MAX_DIMS),
+                ("n_contracting", ctypes.c_int64),
+                ("lhs_contracting", ctypes.c_int64 * DS_DOT_MAX_DIMS),
+                ("rhs_contracting", ctypes.c_int64 * DS_DOT_MAX_DIMS)]
 
 
 class DsFusedOp(ctypes.Structure):
@@ -231,12 +235,27 @@ def make_buffer(ptr: int, shape) -> tuple:
     return DsBuffer(ptr, dims, n), dims
 
 
-def make_dot_dims(n_batch=0, lhs_contracting=1, rhs_contracting=0) -> DsDotDims:
+def make_dot_dims(n_batch=0, lhs_contracting=1, rhs_contracting=0, lhs_batch=None,
+                  rhs_batch=None) -> DsDotDims:
+    """stablehlo dot_general dimension numbers.  Contracting dimensions are an
+    int or a sequence (paired in order); batching dimensions default to the
+    leading n_batch of each operand."""
+    lb = tuple(range(n_batch)) if lhs_batch is None else tuple(lhs_batch)
+    rb = tuple(range(n_batch)) if rhs_batch is None else tuple(rhs_batch)
+    lc = (lhs_contracting,) if isinstance(lhs_contracting, int) else tuple(lhs_contracting)
+    rc = (rhs_contracting,) if isinstance(rhs_contracting, int) else tuple(rhs_contracting)
+    if len(lb) != len(rb) or len(lc) != len(rc):
+        raise ValueError("dot_general: lhs and rhs dimension lists differ in length")
+    if len(lb) > DS_DOT_MAX_DIMS or len(lc) > DS_DOT_MAX_DIMS:
+        raise ValueError(f"dot_general: at most {DS_DOT_MAX_DIMS} batching or contracting "
+                         "dimensions")
     d = DsDotDims()
-    d.n_batch = n_batch
-    for i in range(n_batch):
-        d.lhs_batch[i] = i
-        d.rhs_batch[i] = i
-    d.lhs_contracting = lhs_contracting
-    d.rhs_contracting = rhs_contracting
+    d.n_batch = len(lb)
+    for i, (x, y) in enumerate(zip(lb, rb)):
+        d.lhs_batch[i] = int(x)
+        d.rhs_batch[i] = int(y)
+    d.n_contracting = len(lc)
+    for i, (x, y) in enumerate(zip(lc, rc)):
+        d.lhs_contracting[i] = int(x)
+        d.rhs_contracting[i] = int(y)
     return d

@@ -285,17 +285,5 @@ def _dot_dims(attrs, lhs_rank) -> _lib.DsDotDims:
     rb = tuple(attrs.get("rhs_batching_dimensions", ()))
     lc = tuple(attrs.get("lhs_contracting_dimensions", (lhs_rank - 1,)))
     rc = tuple(attrs.get("rhs_contracting_dimensions", (len(rb),)))
-    if len(lb) != len(rb):
-        raise ValueError("dot_general: lhs and rhs batching dimensions differ in count")
-    if len(lc) != 1 or len(rc) != 1:
-        raise ValueError("dot_general: exactly one contracting dimension per operand is supported")
-    if len(lb) > 4:
-        raise ValueError("dot_general: at most 4 batch dimensions")
-    d = _lib.DsDotDims()
-    d.n_batch = len(lb)
-    for i, (x, y) in enumerate(zip(lb, rb)):
-        d.lhs_batch[i] = int(x)
-        d.rhs_batch[i] = int(y)
-    d.lhs_contracting = int(lc[0])
-    d.rhs_contracting = int(rc[0])
-    return d
+    return _lib.make_dot_dims(lhs_contracting=lc, rhs_contracting=rc, lhs_batch=lb,
+                              rhs_batch=rb)

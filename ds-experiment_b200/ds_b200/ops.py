@@ -223,38 +223,47 @@ def ds_sum_f64(x: torch.Tensor, dimensions=None) -> torch.Tensor:
 
 # ---- dot_general -------------------------------------------------------------------
 
-def _dot_out_shape(ls, rs, lb, lc, rc):
-    nb = len(lb)
-    out = list(ls[:nb])
-    out += [d for i, d in enumerate(ls) if i >= nb and i != lc]
-    out += [d for i, d in enumerate(rs) if i >= nb and i != rc]
+def _dims(x, default):
+    if x is None:
+        return default
+    return (int(x),) if isinstance(x, int) else tuple(int(v) for v in x)
+
+
+def _dot_out_shape(ls, rs, lb, rb, lc, rc):
+    """stablehlo.dot_general's result: batch (lhs order), lhs free, rhs free."""
+    out = [ls[i] for i in lb]
+    out += [d for i, d in enumerate(ls) if i not in lb and i not in lc]
+    out += [d for i, d in enumerate(rs) if i not in rb and i not in rc]
     return tuple(out)
 
 
 def ds_dot_general(lhs_hi, lhs_lo, rhs_hi, rhs_lo, lhs_contracting=None, rhs_contracting=None,
                    lhs_batch=(), rhs_batch=(), algorithm: str = "tensor"):
-    """DS dot_general on SoA operands -> (hi, lo).  Defaults: A[..., M, K] @ B[..., K, N]."""
-    nb = len(lhs_batch)
-    lc = lhs_hi.dim() - 1 if lhs_contracting is None else int(lhs_contracting)
-    rc = nb if rhs_contracting is None else int(rhs_contracting)
-    out = _sds(_dot_out_shape(lhs_hi.shape, rhs_hi.shape, lhs_batch, lc, rc), F32)
+    """DS dot_general on SoA operands -> (hi, lo), with stablehlo dimension
+    numbers: contracting dimensions an int or a sequence (paired in order),
+    batching dimensions anywhere.  Defaults: A[..., M, K] @ B[..., K, N]."""
+    lb, rb = tuple(lhs_batch), tuple(rhs_batch)
+    lc = _dims(lhs_contracting, (lhs_hi.dim() - 1,))
+    rc = _dims(rhs_contracting, (len(rb),))
+    out = _sds(_dot_out_shape(lhs_hi.shape, rhs_hi.shape, lb, rb, lc, rc), F32)
     return ffi_call("ds_dot_general", (out, out))(
-        lhs_hi, lhs_lo, rhs_hi, rhs_lo, lhs_batching_dimensions=tuple(lhs_batch),
-        rhs_batching_dimensions=tuple(rhs_batch), lhs_contracting_dimensions=(lc,),
-        rhs_contracting_dimensions=(rc,), algorithm=_ALGOS[algorithm])
+        lhs_hi, lhs_lo, rhs_hi, rhs_lo, lhs_batching_dimensions=lb,
+        rhs_batching_dimensions=rb, lhs_contracting_dimensions=lc,
+        rhs_contracting_dimensions=rc, algorithm=_ALGOS[algorithm])
 
 
 def ds_dot_general_f64(lhs, rhs, lhs_contracting=None, rhs_contracting=None, lhs_batch=(),
                        rhs_batch=(), algorithm: str = "tensor"):
-    """DS dot_general of f64 operands (split and recombine fused) -> f64."""
-    nb = len(lhs_batch)
-    lc = lhs.dim() - 1 if lhs_contracting is None else int(lhs_contracting)
-    rc = nb if rhs_contracting is None else int(rhs_contracting)
-    out = _sds(_dot_out_shape(lhs.shape, rhs.shape, lhs_batch, lc, rc), F64)
+    """DS dot_general of f64 operands (split and recombine fused) -> f64,
+    with the dimension numbers of ds_dot_general."""
+    lb, rb = tuple(lhs_batch), tuple(rhs_batch)
+    lc = _dims(lhs_contracting, (lhs.dim() - 1,))
+    rc = _dims(rhs_contracting, (len(rb),))
+    out = _sds(_dot_out_shape(lhs.shape, rhs.shape, lb, rb, lc, rc), F64)
     return ffi_call("ds_dot_general_f64", out)(
-        lhs, rhs, lhs_batching_dimensions=tuple(lhs_batch),
-        rhs_batching_dimensions=tuple(rhs_batch), lhs_contracting_dimensions=(lc,),
-        rhs_contracting_dimensions=(rc,), algorithm=_ALGOS[algorithm])
+        lhs, rhs, lhs_batching_dimensions=lb,
+        rhs_batching_dimensions=rb, lhs_contracting_dimensions=lc,
+        rhs_contracting_dimensions=rc, algorithm=_ALGOS[algorithm])
 
 
 def ds_matmul_f64(A, B, algorithm: str = "tensor"):

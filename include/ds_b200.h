@@ -69,14 +69,21 @@ enum {
   DS_DOT_CUDA_CORE = 1
 };
 
-/* dot_general dimension numbers (stablehlo.dot_general).  One contracting
-   dimension per operand; batch dimensions must be the leading ones, in order. */
+/* dot_general dimension numbers, as stablehlo.dot_general's
+   DotDimensionNumbers (lhs/rhs_batching_dimensions, lhs/rhs_contracting_
+   dimensions): any batching dimensions, in any position, paired in list
+   order; any number of contracting dimensions (none: an outer product),
+   paired in list order; every other dimension is free.  The result is
+   [batch (lhs order)..., lhs free (ascending)..., rhs free (ascending)...].
+   Operands of rank up to DS_DOT_MAX_DIMS. */
+#define DS_DOT_MAX_DIMS 8
 typedef struct ds_dot_dims {
   int64_t n_batch;
-  int64_t lhs_batch[4];
-  int64_t rhs_batch[4];
-  int64_t lhs_contracting;
-  int64_t rhs_contracting;
+  int64_t lhs_batch[DS_DOT_MAX_DIMS];
+  int64_t rhs_batch[DS_DOT_MAX_DIMS];
+  int64_t n_contracting;
+  int64_t lhs_contracting[DS_DOT_MAX_DIMS];
+  int64_t rhs_contracting[DS_DOT_MAX_DIMS];
 } ds_dot_dims;
 
 /* Message of the calling thread's last failing call ("" if none). */
@@ -296,10 +303,16 @@ DS_API int ds_reduce_f64_sharded(const ds_buffer* in, const ds_buffer* init, int
 /* ---- dot_general (DsTransformPass.cpp:337-370) --------------------------- */
 
 /* DS dot_general of SoA operands (lhs_hi, lhs_lo), (rhs_hi, rhs_lo) f32 with
-   stablehlo dimension numbers; result (out_hi, out_lo) f32 of shape
-   [batch..., lhs free, rhs free].  The reference lowers this to four f32
-   dots (f32 accumulation) and a two_sum; here the product is computed from
-   the exact DS values (see algorithm). */
+   stablehlo dimension numbers (any batching, contracting and free
+   dimensions, as the reference's handler clones them,
+   DsTransformPass.cpp:345-356); result (out_hi, out_lo) f32 of shape
+   [batch..., lhs free..., rhs free...].  The reference lowers this to four
+   f32 dots (f32 accumulation) and a two_sum; here the product is computed
+   from the exact DS values (see algorithm).  An operand whose batch, free or
+   contracting dimensions do not nest into one stride each is first copied
+   (one gather) into the workspace, which ds_dot_general_workspace_size
+   counts; the contracting pairs are taken in whichever of their given
+   order or the lhs or rhs dimension order needs the fewest copies. */
 DS_API size_t ds_dot_general_workspace_size(const ds_buffer* lhs, const ds_buffer* rhs,
                                      const ds_dot_dims* dims, int32_t algorithm);
 DS_API int ds_dot_general(const ds_buffer* lhs_hi, const ds_buffer* lhs_lo,

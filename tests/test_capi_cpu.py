@@ -233,3 +233,47 @@ def test_fused_reduce_rows_argument_errors(L):
     null, _5 = _b(L, (), ptr=0)
     st, msg = call(init=null)
     assert st == L.DS_INVALID_ARGUMENT and "null" in msg
+
+
+def test_dot_general_workspace_counts_the_gather_copy(L):
+    """An operand whose free dimensions do not nest into one stride ([F1, K,
+    F2], contracting over K) is copied to [F1 * F2, K] first: the workspace
+    query adds exactly that copy (8 bytes per element, 256-byte aligned) to
+    what the nested [54, 64] x [64, 30] product needs; nested layouts, non-
+    leading batch dimensions and several contracting dimensions add nothing."""
+    import ctypes
+    r = ctypes.byref
+    A3, _a = _b(L, (6, 64, 9))
+    A2, _b2 = _b(L, (54, 64))
+    B, _c = _b(L, (64, 30))
+    nested = L.lib().ds_dot_general_workspace_size(r(A2), r(B), r(L.make_dot_dims(0, 1, 0)), 0)
+    copied = L.lib().ds_dot_general_workspace_size(r(A3), r(B), r(L.make_dot_dims(0, 1, 0)), 0)
+    assert nested > 0 and copied == nested + (54 * 64 * 8 + 255) // 256 * 256
+    S, _d = _b(L, (40, 3, 64))
+    T, _e = _b(L, (64, 3, 36))
+    dd = L.make_dot_dims(lhs_contracting=2, rhs_contracting=0, lhs_batch=(1,), rhs_batch=(1,))
+    Sb, _f = _b(L, (3, 40, 64))
+    Tb, _g = _b(L, (3, 64, 36))
+    lead = L.make_dot_dims(1, 2, 1)
+    assert L.lib().ds_dot_general_workspace_size(r(S), r(T), r(dd), 0) == \
+        L.lib().ds_dot_general_workspace_size(r(Sb), r(Tb), r(lead), 0)
+    M3, _h = _b(L, (64, 12, 20))
+    N3, _i = _b(L, (12, 20, 48))
+    two = L.make_dot_dims(lhs_contracting=(1, 2), rhs_contracting=(0, 1))
+    M2, _j = _b(L, (64, 240))
+    N2, _k = _b(L, (240, 48))
+    flat = L.lib().ds_dot_general_workspace_size(r(M2), r(N2), r(L.make_dot_dims(0, 1, 0)), 0)
+    assert L.lib().ds_dot_general_workspace_size(r(M3), r(N3), r(two), 0) == flat
+    # contracting pairs listed out of memory order are taken in memory order
+    # (the sum does not depend on it): no copy ...
+    swapped = L.make_dot_dims(lhs_contracting=(2, 1), rhs_contracting=(1, 0))
+    assert L.lib().ds_dot_general_workspace_size(r(M3), r(N3), r(swapped), 0) == flat
+    # ... unless no order suits both operands: A[m, a, b] x B[b, a, n] copies one
+    # (the smaller, B)
+    Bx, _l = _b(L, (20, 12, 48))
+    crossed = L.make_dot_dims(lhs_contracting=(2, 1), rhs_contracting=(0, 1))
+    assert L.lib().ds_dot_general_workspace_size(r(M3), r(Bx), r(crossed), 0) == \
+        flat + (240 * 48 * 8 + 255) // 256 * 256
+    # mismatched sizes get no workspace (the call itself reports why)
+    bad = L.make_dot_dims(lhs_contracting=(1, 2), rhs_contracting=(1, 0))
+    assert L.lib().ds_dot_general_workspace_size(r(M3), r(N3), r(bad), 0) == 0

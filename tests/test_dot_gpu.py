@@ -326,3 +326,75 @@ def test_many_uncertified_outputs_take_the_tiled_recompute(ops):
     again = host(ops.ds_matmul_f64(dA, dB))
     assert np.array_equal(got.view(np.uint64), again.view(np.uint64))
     assert_no_worse_than_reference(got, A, B, samples=400)
+
+
+def test_dot_general_dimension_numbers(ops):
+    """stablehlo dot_general dimension numbers beyond [batch..., M, K] x
+    [batch..., K, N] (the reference's handler clones any of them,
+    DsTransformPass.cpp:345-356).  Where the dimensions nest into single
+    strides the product reads the operands in place and gives the same bits
+    as the 2-D product of the reshaped operands; otherwise one gather copy
+    runs first and the result is checked against exact sampled entries."""
+    rng = np.random.default_rng(60)
+    u = lambda *s: rng.uniform(-1, 1, s)  # noqa: E731
+    mm = lambda A, B: host(ops.ds_matmul_f64(cu(A), cu(B)))  # noqa: E731
+
+    def same_bits(got, want):
+        assert got.shape == want.shape
+        assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+
+    # [B, S, D] x [D, E], no batch dimensions: [B, S, E]
+    A, B = u(3, 70, 96), u(96, 50)
+    got = host(ops.ds_dot_general_f64(cu(A), cu(B), lhs_contracting=2, rhs_contracting=0))
+    same_bits(got, mm(A.reshape(-1, 96), B).reshape(3, 70, 50))
+    # contracting over two dimensions: [M, K1, K2] x [K1, K2, N]
+    A, B = u(64, 12, 20), u(12, 20, 48)
+    got = host(ops.ds_dot_general_f64(cu(A), cu(B), lhs_contracting=(1, 2),
+                                      rhs_contracting=(0, 1)))
+    same_bits(got, mm(A.reshape(64, 240), B.reshape(240, 48)))
+    # batch dimensions that are not leading: [S, B, K] x [K, B, N] -> [B, S, N]
+    A, B = u(40, 3, 64), u(64, 3, 36)
+    got = host(ops.ds_dot_general_f64(cu(A), cu(B), lhs_contracting=2, rhs_contracting=0,
+                                      lhs_batch=(1,), rhs_batch=(1,)))
+    for b in range(3):
+        same_bits(got[b], mm(np.ascontiguousarray(A[:, b, :]), np.ascontiguousarray(B[:, b, :])))
+    # free dimensions on both sides of a contracting one, and contracting
+    # dimensions paired across the operands' orders: these take the gather copy
+    A, B = u(6, 64, 9), u(64, 30)            # [F1, K, F2] x [K, N] -> [F1, F2, N]
+    got = host(ops.ds_dot_general_f64(cu(A), cu(B), lhs_contracting=1, rhs_contracting=0))
+    A2 = A.transpose(0, 2, 1).reshape(54, 64)
+    assert got.shape == (6, 9, 30)
+    check_gemm(got.reshape(54, 30), A2, B, samples=300, ref=ds_pass_ref.dot_general_f64(A2, B))
+    A, B = u(50, 10, 14), u(14, 10, 40)      # A[m, a, b] B[b, a, n], pairs (2, 0), (1, 1)
+    got = host(ops.ds_dot_general_f64(cu(A), cu(B), lhs_contracting=(2, 1),
+                                      rhs_contracting=(0, 1)))
+    A2 = A.transpose(0, 2, 1).reshape(50, 140)
+    B2 = B.reshape(140, 40)
+    check_gemm(got, A2, B2, samples=300, ref=ds_pass_ref.dot_general_f64(A2, B2))
+    # the same through the SoA DS entry
+    ah, al = ds_pass_ref.from_float(A)
+    bh, bl = ds_pass_ref.from_float(B)
+    hi, lo = ops.ds_dot_general(cu(ah), cu(al), cu(bh), cu(bl), lhs_contracting=(2, 1),
+                                rhs_contracting=(0, 1))
+    got_ds = host(hi).astype(np.float64) + host(lo).astype(np.float64)
+    check_gemm(got_ds, ds_of(A2), ds_of(B2), samples=200)
+    # no contracting dimension: an outer product [M] x [N] -> [M, N]
+    a, b = u(300), u(200)
+    got = host(ops.ds_dot_general_f64(cu(a), cu(b), lhs_contracting=(), rhs_contracting=()))
+    assert got.shape == (300, 200)
+    assert_no_worse_than_reference(got, a[:, None], b[None, :], samples=400)
+
+
+def test_dot_general_dimension_errors(ops):
+    """Mismatched or repeated dimensions are rejected before any launch."""
+    import torch
+    from ds_b200 import _lib
+    A = torch.zeros((4, 5, 6), dtype=torch.float64, device="cuda")
+    B = torch.zeros((6, 5, 7), dtype=torch.float64, device="cuda")
+    with pytest.raises(_lib.DsInvalidArgument, match="contracting dimensions must match"):
+        ops.ds_dot_general_f64(A, B, lhs_contracting=(2, 1), rhs_contracting=(1, 0))
+    with pytest.raises(_lib.DsInvalidArgument, match="out of range or repeated"):
+        ops.ds_dot_general_f64(A, B, lhs_contracting=(2, 2), rhs_contracting=(0, 0))
+    with pytest.raises(_lib.DsInvalidArgument, match="batch dimensions must match"):
+        ops.ds_dot_general_f64(A, B, lhs_contracting=2, rhs_contracting=0, lhs_batch=(0,),
+                               rhs_batch=(2,))
