@@ -412,10 +412,11 @@ def cpu_baseline_gemm(A, B, reps=1):
 # ---------------------------------------------------------------------------
 # every configuration in the default line (N = 1)
 
-# f32 operations per iteration of x <- x*a + b with the reference's Dekker
-# two_prod (a's split precomputed): ds_mul 25 (two_prod 13, cross 3, two_sum
-# 6, low word 3) + ds_add 20.
-REC_F32_OPS = 45
+# f32 operations per iteration of x <- x*a + b: ds_mul 14 (the product and
+# its FMA error term 2, cross 3, two_sum 6, low word 3) + ds_add 20 + the
+# range test that keeps Dekker's bits (about 2 per element: one min, one
+# max and a compare for four chains, one vote).
+REC_F32_OPS = 36
 FP32_LANES_PER_SM = 128
 SMS = 148
 

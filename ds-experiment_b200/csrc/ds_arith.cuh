@@ -61,6 +61,32 @@ __device__ __forceinline__ void two_prod_bsplit(float a, float b, float bh,
   e = __fadd_rn(t, __fmul_rn(al, bl));
 }
 
+// Dekker's error term of p = a * b with b's split (bh, bl) known: the error
+// half of two_prod_bsplit.
+__device__ __forceinline__ float dekker_err_bsplit(float a, float bh, float bl, float p) {
+  float ah, al;
+  split(a, ah, al);
+  float t = __fsub_rn(__fmul_rn(ah, bh), p);
+  t = __fadd_rn(t, __fmul_rn(ah, bl));
+  t = __fadd_rn(t, __fmul_rn(al, bh));
+  return __fadd_rn(t, __fmul_rn(al, bl));
+}
+
+// Where an FMA gives Dekker's bits.  For |a|, |b| < 2^115 and
+// 2^-90 <= |p| <= 2^120 neither split overflows and every partial product
+// of Dekker's algorithm is exact (their lowest bits lie at or above 2^-138,
+// on the subnormal grid), so Dekker's e is the exact error a*b - p, which
+// is what __fmaf_rn(a, b, -p) returns.  With |b| in [2^-5, 2^115) (checked
+// once per loop-invariant b), |p| in [2^-90, 2^110] implies |a| < 2^115.
+__device__ __forceinline__ bool fma_b_range(float b) {
+  const float ab = fabsf(b);
+  return ab >= 0x1p-5f && ab < 0x1p115f;
+}
+__device__ __forceinline__ bool fma_p_range(float p) {
+  const float ap = fabsf(p);
+  return ap >= 0x1p-90f && ap <= 0x1p110f;
+}
+
 // f64 -> DS: hi = f32(x), lo = f32(x - f64(hi)).
 __device__ __forceinline__ ds2 from_f64(double x) {
   ds2 r;
@@ -105,6 +131,15 @@ __device__ __forceinline__ ds2 mul(ds2 a, ds2 b) {
 __device__ __forceinline__ ds2 mul_bsplit(ds2 a, ds2 b, float bh, float bl) {
   float p1, e1, s, e2;
   two_prod_bsplit(a.hi, b.hi, bh, bl, p1, e1);
+  const float cross = __fadd_rn(__fmul_rn(a.hi, b.lo), __fmul_rn(a.lo, b.hi));
+  two_sum(p1, cross, s, e2);
+  return ds2{s, __fadd_rn(__fadd_rn(e1, e2), __fmul_rn(a.lo, b.lo))};
+}
+
+// ds_mul after its head product: p1 = a.hi * b.hi and its exact error e1
+// given, the rest of mul() in the same order (the same bits).
+__device__ __forceinline__ ds2 mul_finish(ds2 a, ds2 b, float p1, float e1) {
+  float s, e2;
   const float cross = __fadd_rn(__fmul_rn(a.hi, b.lo), __fmul_rn(a.lo, b.hi));
   two_sum(p1, cross, s, e2);
   return ds2{s, __fadd_rn(__fadd_rn(e1, e2), __fmul_rn(a.lo, b.lo))};

@@ -211,20 +211,55 @@ int launch_ew(const void* a, const void* b, const void* c, void* out, int64_t n,
 //
 // Each thread owns kChains elements and advances all of them one iteration at
 // a time, so kChains independent DS dependency chains interleave in the
-// pipeline.  The Veltkamp split of the loop-invariant multiplier is hoisted
-// (mul_bsplit), which leaves the rounded results unchanged.
+// pipeline.  The Veltkamp split of the loop-invariant multiplier is hoisted.
+// The product's error term comes from one FMA wherever that equals Dekker's
+// (fma_b_range / fma_p_range): one vote per iteration checks the warp's
+// kChains products at once, so the common case is one straight-line block of
+// about 36 f32 operations per element-iteration (ds_mul 14, ds_add 20, the
+// range test about 2) instead of 45; a warp with any product out of range
+// takes Dekker for those lanes.  The bits are Dekker's everywhere.  The outer
+// loop is warp-uniform (lanes past n compute on zeros) so the vote sees the
+// whole warp.
 
 constexpr int kChains = 4;
+
+// p = a.hi * b.hi for every chain and their exact errors, into p[] and e[].
+__device__ __forceinline__ void head_products(const ds2 (&a)[kChains], const ds2 (&b)[kChains],
+                                              const float (&bh)[kChains],
+                                              const float (&bl)[kChains], bool b_ok,
+                                              float (&p)[kChains], float (&e)[kChains]) {
+  float lo = 0x1p127f, hi = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kChains; ++u) {
+    p[u] = __fmul_rn(a[u].hi, b[u].hi);
+    lo = fminf(lo, fabsf(p[u]));
+    hi = fmaxf(hi, fabsf(p[u]));
+  }
+  // fminf/fmaxf drop a NaN operand: a NaN product (a NaN a.hi; b_ok excludes
+  // a NaN or infinite b) takes the FMA, whose error term is NaN as Dekker's is
+  const bool ok = b_ok && lo >= 0x1p-90f && hi <= 0x1p110f;
+  if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+    for (int u = 0; u < kChains; ++u) e[u] = __fmaf_rn(a[u].hi, b[u].hi, -p[u]);
+  } else {
+#pragma unroll
+    for (int u = 0; u < kChains; ++u)
+      e[u] = (b_ok && fma_p_range(p[u])) ? __fmaf_rn(a[u].hi, b[u].hi, -p[u])
+                                         : dekker_err_bsplit(a[u].hi, bh[u], bl[u], p[u]);
+  }
+}
 
 // z <- (z + y) * y, k times (cpp/ds_recurrence_add_mul_to_f64_cuda.cu:69-93).
 __global__ void __launch_bounds__(kThreads)
 recurrence_add_mul_kernel(const double* __restrict__ x, const double* __restrict__ y,
                           double* __restrict__ out, int64_t n, int32_t k) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       base < n; base += stride * kChains) {
+       base - lane < n; base += stride * kChains) {
     ds2 z[kChains], Y[kChains];
     float yh[kChains], yl[kChains];
+    bool y_ok = true;
 #pragma unroll
     for (int u = 0; u < kChains; ++u) {
       const int64_t i = base + u * stride;
@@ -232,10 +267,16 @@ recurrence_add_mul_kernel(const double* __restrict__ x, const double* __restrict
       z[u] = from_f64(in ? x[i] : 0.0);
       Y[u] = from_f64(in ? y[i] : 0.0);
       split(Y[u].hi, yh[u], yl[u]);
+      y_ok = y_ok && fma_b_range(Y[u].hi);
     }
     for (int32_t it = 0; it < k; ++it) {
+      ds2 w[kChains];
+      float p[kChains], e[kChains];
 #pragma unroll
-      for (int u = 0; u < kChains; ++u) z[u] = mul_bsplit(add(z[u], Y[u]), Y[u], yh[u], yl[u]);
+      for (int u = 0; u < kChains; ++u) w[u] = add(z[u], Y[u]);
+      head_products(w, Y, yh, yl, y_ok, p, e);
+#pragma unroll
+      for (int u = 0; u < kChains; ++u) z[u] = mul_finish(w[u], Y[u], p[u], e[u]);
     }
 #pragma unroll
     for (int u = 0; u < kChains; ++u) {
@@ -251,10 +292,12 @@ recurrence_mul_add_kernel(const double* __restrict__ x, const double* __restrict
                           const double* __restrict__ b, double* __restrict__ out,
                           int64_t n, int32_t k) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       base < n; base += stride * kChains) {
+       base - lane < n; base += stride * kChains) {
     ds2 z[kChains], A[kChains], B[kChains];
     float ah[kChains], al[kChains];
+    bool a_ok = true;
 #pragma unroll
     for (int u = 0; u < kChains; ++u) {
       const int64_t i = base + u * stride;
@@ -263,10 +306,13 @@ recurrence_mul_add_kernel(const double* __restrict__ x, const double* __restrict
       A[u] = from_f64(in ? a[i] : 0.0);
       B[u] = from_f64(in ? b[i] : 0.0);
       split(A[u].hi, ah[u], al[u]);
+      a_ok = a_ok && fma_b_range(A[u].hi);
     }
     for (int32_t it = 0; it < k; ++it) {
+      float p[kChains], e[kChains];
+      head_products(z, A, ah, al, a_ok, p, e);
 #pragma unroll
-      for (int u = 0; u < kChains; ++u) z[u] = add(mul_bsplit(z[u], A[u], ah[u], al[u]), B[u]);
+      for (int u = 0; u < kChains; ++u) z[u] = add(mul_finish(z[u], A[u], p[u], e[u]), B[u]);
     }
 #pragma unroll
     for (int u = 0; u < kChains; ++u) {

@@ -104,7 +104,8 @@ def test_fused_vs_oracle(ops, dso, n):
                       dso.ds_fused_add_mul3_to_f64(x, y, c, 8), "add_mul3")
 
 
-@pytest.mark.parametrize("n,k", [(0, 3), (1, 0), (7, 1), (4099, 4), (65537, 16), (1 << 16, 64)])
+@pytest.mark.parametrize("n,k", [(0, 3), (1, 0), (7, 1), (4099, 4), (65537, 16), (1 << 16, 64),
+                                 (4097, 1024)])
 def test_recurrences_vs_oracle(ops, dso, n, k):
     rng = np.random.default_rng(400 + n + k)
     x = rng.uniform(-1, 1, n)
@@ -115,6 +116,35 @@ def test_recurrences_vs_oracle(ops, dso, n, k):
                       dso.ds_recurrence_mul_add_to_f64(x, a, b, k, 8), f"mul_add k={k}")
     assert_bits_equal(host(ops.ds_recurrence_add_mul_to_f64_cuda(cu(x), cu(y), k)),
                       dso.ds_recurrence_add_mul_to_f64(x, y, k, 8), f"add_mul k={k}")
+
+
+def test_recurrences_edge_magnitudes(ops, dso):
+    """The recurrences take the product's error term from an FMA only where
+    it equals Dekker's; operands and products over the whole f32 range
+    (Veltkamp-split overflow near 8.3e34, products near the subnormal range,
+    zeros, Inf, NaN) give the oracle's (Dekker's) bits at every k.  The
+    edge values sit at the start of the array, so whole warps see them."""
+    rng = np.random.default_rng(77)
+    n = (1 << 16) + 7
+    sign = lambda: np.where(rng.integers(0, 2, n) == 0, 1.0, -1.0)  # noqa: E731
+    x = sign() * 2.0 ** rng.uniform(-148, 127, n)
+    a = sign() * 2.0 ** rng.uniform(-80, 80, n)
+    b = sign() * 2.0 ** rng.uniform(-148, 127, n)
+    y = sign() * 2.0 ** rng.uniform(-75, 64, n)
+    edges = [0.0, -0.0, np.inf, -np.inf, np.nan, 8.4e34, -8.3e34, 1e-45, 2.0 ** -90,
+             2.0 ** 115, 2.0 ** 120, 2.0 ** -126, 2.0 ** -5, 2.0 ** 110]
+    for v in (x, a, b, y):
+        v[:len(edges)] = edges
+        v[len(edges):2 * len(edges)] = edges[::-1]
+    # a stretch of ordinary values, where whole warps take the FMA path
+    x[4096:8192] = rng.uniform(-1, 1, 4096)
+    a[4096:8192] = rng.uniform(0.999, 1.001, 4096)
+    y[4096:8192] = rng.uniform(-1, 1, 4096)
+    for k in (1, 2, 5, 33):
+        assert_bits_equal(host(ops.ds_recurrence_mul_add_to_f64(cu(x), cu(a), cu(b), k)),
+                          dso.ds_recurrence_mul_add_to_f64(x, a, b, k, 8), f"mul_add k={k}")
+        assert_bits_equal(host(ops.ds_recurrence_add_mul_to_f64_cuda(cu(x), cu(y), k)),
+                          dso.ds_recurrence_add_mul_to_f64(x, y, k, 8), f"add_mul k={k}")
 
 
 def test_unaligned_views(ops, dso):
