@@ -55,6 +55,29 @@ def host_cores():
         return os.cpu_count() or 1
 
 
+class all_host_threads:
+    """BLAS on every host core for the CPU arms (torchrun sets
+    OMP_NUM_THREADS=1 in every rank, which would leave numpy's BLAS on one
+    thread); `.threads` is the count the BLAS libraries report inside."""
+
+    def __enter__(self):
+        try:
+            from threadpoolctl import threadpool_info, threadpool_limits
+        except ImportError:
+            self._ctl, self.threads = None, host_cores()
+            return self
+        self._ctl = threadpool_limits(limits=host_cores(), user_api="blas")
+        self._ctl.__enter__()
+        counts = [i["num_threads"] for i in threadpool_info() if i["user_api"] == "blas"]
+        self.threads = max(counts) if counts else host_cores()
+        return self
+
+    def __exit__(self, *exc):
+        if self._ctl is not None:
+            self._ctl.__exit__(*exc)
+        return False
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -399,12 +422,13 @@ def run_ours(args):
 def cpu_baseline_gemm(A, B, reps=1):
     """The reference DS path on the host (NumPy restatement, BLAS on all cores)."""
     from oracle import ds_pass_ref
-    t = time.perf_counter()
-    for _ in range(reps):
-        ds_pass_ref.dot_general_f64(A, B)
-    dt = (time.perf_counter() - t) / reps
+    with all_host_threads() as pool:
+        t = time.perf_counter()
+        for _ in range(reps):
+            ds_pass_ref.dot_general_f64(A, B)
+        dt = (time.perf_counter() - t) / reps
     return {"value": round(2.0 * A.shape[0] * A.shape[1] * B.shape[1] / dt / 1e9, 2),
-            "unit": "GFLOP/s", "cores": host_cores(), "kind": "port",
+            "unit": "GFLOP/s", "cores": pool.threads, "kind": "port",
             "sample": f"one full {A.shape[0]}x{A.shape[1]}x{B.shape[1]} DS GEMM: split, four "
                       "float32 numpy matmuls (f32 accumulation), two_sum, recombine"}
 
@@ -650,7 +674,9 @@ def config5_lines(dev, peaks, peak_src):
     err = np.abs(Ch[rows, cols] - truth)
     ref_err = reference_gemm_error(A, B, rows, cols, truth)
     sub = A[:256]
-    rate = _cpu_rate(lambda: ds_pass_ref.dot_general_f64(sub, B), 2.0 * 256 * LARGE_N * LARGE_K)
+    with all_host_threads() as pool:
+        rate = _cpu_rate(lambda: ds_pass_ref.dot_general_f64(sub, B),
+                         2.0 * 256 * LARGE_N * LARGE_K)
     out["gemm"] = {
         "M": LARGE_M, "N": LARGE_N, "K": LARGE_K, "ms": round(ms, 3),
         "GFLOP/s": round(2.0 * LARGE_M * LARGE_N * LARGE_K / (ms * 1e-3) / 1e9, 1),
@@ -663,7 +689,7 @@ def config5_lines(dev, peaks, peak_src):
                      "reference_ds_path_max_abs_err": ref_err,
                      "err_le_reference": bool(np.all(err <= ref_err)),
                      "sampled_entries": int(len(rows))},
-        "cpu_baseline": {"value": round(rate, 2), "unit": "GFLOP/s", "cores": host_cores(),
+        "cpu_baseline": {"value": round(rate, 2), "unit": "GFLOP/s", "cores": pool.threads,
                          "kind": "port", "sample": "256 rows of A times B: the DS pass in NumPy"}}
     del dA, dB, C, Ch, A, B
     torch.cuda.empty_cache()
@@ -691,7 +717,8 @@ def config5_lines(dev, peaks, peak_src):
         return ds_pass_ref.two_sum(np.einsum("ik,ik->i", h1, h2),
                                    (np.einsum("ik,ik->i", h1, l2) +
                                     np.einsum("ik,ik->i", l1, h2)) + np.einsum("ik,ik->i", l1, l2))
-    rate = _cpu_rate(host_dots, 2.0 * 256 * DOT_LEN * 8)
+    with all_host_threads() as pool:
+        rate = _cpu_rate(host_dots, 2.0 * 256 * DOT_LEN * 8)
     out["batched_dot"] = {
         "batch": BATCH_DOTS, "length": DOT_LEN, "ms": round(ms, 3),
         "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes_per_mac": 16,
@@ -700,7 +727,7 @@ def config5_lines(dev, peaks, peak_src):
         "accuracy": {"max_abs_err_vs_exact": float(derr.max()),
                      "reference_ds_path_max_abs_err": float(rerr.max()),
                      "err_le_reference": bool(np.all(derr <= rerr)), "sampled_dots": len(idx)},
-        "cpu_baseline": {"value": round(rate, 2), "unit": "GB/s", "cores": host_cores(),
+        "cpu_baseline": {"value": round(rate, 2), "unit": "GB/s", "cores": pool.threads,
                          "kind": "port", "sample": "256 of the dot products: the DS pass in NumPy"}}
     del dX, dY, d, X, Y
     torch.cuda.empty_cache()
@@ -727,7 +754,7 @@ def config5_strong(dev, rank, world, barrier, max_over_ranks):
     t1 = None
     if rank == 0:
         full = torch.from_numpy(large_draw(0, (LARGE_M, LARGE_K))).to(dev)
-        t1, _, c = _time_calls(lambda: ops.ds_matmul_f64(full, B), 2, warmup=2)
+        t1, _, c = _time_calls(lambda: ops.ds_matmul_f64(full, B), 3, warmup=2)
         del full, c
         torch.cuda.empty_cache()
     stream = torch.cuda.current_stream()
@@ -1064,12 +1091,13 @@ def run_reference(args):
         return None
     A, B = gemm_inputs(0)
     from oracle import ds_pass_ref
-    for _ in range(args.warmup):
-        ds_pass_ref.dot_general_f64(A, B)
-    t = time.perf_counter()
-    for _ in range(args.steps):
-        ds_pass_ref.dot_general_f64(A, B)
-    dt = (time.perf_counter() - t) / args.steps
+    with all_host_threads() as pool:
+        for _ in range(args.warmup):
+            ds_pass_ref.dot_general_f64(A, B)
+        t = time.perf_counter()
+        for _ in range(args.steps):
+            ds_pass_ref.dot_general_f64(A, B)
+        dt = (time.perf_counter() - t) / args.steps
     value = 2.0 * GEMM_DIM ** 3 / dt / 1e9
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "GFLOP/s",
@@ -1077,7 +1105,7 @@ def run_reference(args):
         "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32x2 (DS)", "data": "synthetic (default_rng(2))",
         "config": gemm_config(world, args.algorithm),
-        "cpu_baseline": {"value": round(value, 2), "unit": "GFLOP/s", "cores": host_cores(),
+        "cpu_baseline": {"value": round(value, 2), "unit": "GFLOP/s", "cores": pool.threads,
                          "kind": "port",
                          "sample": "one full 4096^3 DS GEMM per step: the DS pass restated in "
                                    "NumPy (split, 4 float32 matmuls, two_sum, recombine) with "
@@ -1310,16 +1338,17 @@ def run_reference_large(args):
             return ds_pass_ref.to_float(*ds_pass_ref.two_sum(p, e))
         work, unit = 2.0 * m * DOT_LEN * 8, "GB/s"
         sample = f"{m} of the 4096 dot products per step"
-    for _ in range(min(args.warmup, 1)):
-        fn()
     steps = max(1, min(args.steps, 5))
-    t = time.perf_counter()
-    for _ in range(steps):
-        fn()
-    dt = (time.perf_counter() - t) / steps
+    with all_host_threads() as pool:
+        for _ in range(min(args.warmup, 1)):
+            fn()
+        t = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        dt = (time.perf_counter() - t) / steps
     value = round(work / dt / 1e9, 2)
     metric, _ = LARGE_METRICS[wl]
-    cb = {"value": value, "unit": unit, "cores": host_cores(), "kind": "port",
+    cb = {"value": value, "unit": unit, "cores": pool.threads, "kind": "port",
           "sample": sample + ": the DS pass restated in NumPy (split, four float32 products "
                              "with f32 accumulation, two_sum, recombine)"}
     return {"impl": "reference", "metric": metric, "value": value, "unit": unit,

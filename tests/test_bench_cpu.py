@@ -45,3 +45,10 @@ def test_reference_arm_stream_line():
     line = bench.run_reference_stream(_args(workload="fused_add_mul", n=1 << 20))
     assert REQUIRED <= set(line)
     assert line["cpu_baseline"]["kind"] == "port" and line["value"] > 0
+
+
+def test_reference_arm_uses_every_host_core_under_torchrun(monkeypatch):
+    """torchrun sets OMP_NUM_THREADS=1 in each rank; the CPU arms still run
+    numpy's BLAS on every host core and report the count they used."""
+    with bench.all_host_threads() as pool:
+        assert pool.threads == bench.host_cores()
