@@ -1,0 +1,55 @@
+"""The header-gated adapters (ds-experiment_b200/adapters/) agree with each
+other and with the boundary, read as text: they cannot be compiled in this
+image (no XLA-FFI or MLIR headers), so this keeps them from drifting.
+
+- every XLA-FFI handler symbol the reference defines (cpp/*.cpp, cpp/*.cu)
+  has a replacement in ds_b200_ffi.cc;
+- every custom-call target the retargeted pass emits has a handler, and the
+  attribute names the pass writes are the ones the handler binds;
+- every C-ABI function the handlers call is declared in include/ds_b200.h.
+"""
+import os
+import re
+
+from conftest import ROOT
+
+ADAPTERS = os.path.join(ROOT, "ds-experiment_b200", "adapters")
+FFI = open(os.path.join(ADAPTERS, "ds_b200_ffi.cc")).read()
+PASS = open(os.path.join(ADAPTERS, "DsTransformPassB200.cpp")).read()
+HEADER = open(os.path.join(ROOT, "include", "ds_b200.h")).read()
+
+REFERENCE_HANDLERS = ["DsFromF64", "DsToF64", "DsFromF32", "DsToF32", "DsAdd", "DsSub", "DsMul",
+                      "DsFusedAddMul", "DsFusedAddMulToF64", "DsFusedAxpy",
+                      "DsFusedAddMulToF64Cuda", "DsFusedAddSubToF64Cuda",
+                      "DsRecurrenceAddMulToF64Cuda"]
+
+
+def handler_symbols():
+    direct = re.findall(r"XLA_FFI_DEFINE_HANDLER_SYMBOL\((\w+),", FFI)
+    macro = re.findall(r"DS_(?:PACKED|CHAIN)_HANDLER\((\w+),", FFI)
+    return set(direct) | set(macro)
+
+
+def camel(target):
+    return "".join(p[:1].upper() + p[1:] for p in target.split("_"))
+
+
+def test_every_reference_handler_is_replaced():
+    assert set(REFERENCE_HANDLERS) <= handler_symbols() - {"Symbol"}
+
+
+def test_pass_targets_have_handlers_with_the_same_attributes():
+    targets = set(re.findall(r'customCall\(b, loc, "(\w+)"', PASS))
+    assert targets == {"ds_dot_general_f64", "ds_reduce_f64", "ds_fused"}
+    symbols = handler_symbols()
+    for t in targets:
+        assert camel(t) in symbols, t
+    written = set(re.findall(r'getNamedAttr\("(\w+)"', PASS))
+    bound = set(re.findall(r'\.Attr<[^>]*>+\("(\w+)"\)', FFI))
+    assert written <= bound, written - bound
+
+
+def test_handlers_call_declared_entry_points():
+    called = set(re.findall(r"\b(ds_[a-z0-9_]+)\(", FFI)) - {"ds_last_error"}
+    declared = set(re.findall(r"DS_API\s+[\w\s\*]+?\b(ds_[a-z0-9_]+)\(", HEADER))
+    assert called and called <= declared, called - declared
