@@ -72,6 +72,12 @@ __host__ __device__ constexpr int mod_of(int l) {
        : l == 10 ? 223 : l == 11 ? 217 : l == 12 ? 211 : 199;
 }
 
+// Moduli whose split residue is taken on the FP64 pipe (three FP64
+// instructions) rather than the integer pipes (two byte dot products and a
+// multiply-high reduction, all on the FMA-heavy pipe): ten of the thirteen
+// were fastest in both split kernels (7: +3%, 13: +6 to 18%).
+__host__ __device__ constexpr bool residue_fp64(int l) { return l >= 1 && l <= 10; }
+
 // ---------------------------------------------------------------------------
 // Host-side constants: P from K, and the CRT weights in 40-bit limbs.
 
@@ -194,17 +200,18 @@ __device__ __forceinline__ uint64_t quantise(double v, int shift) {
 }
 
 // t = hi * 2^32 + lo (hi < 2^20): the seven bytes of t in two words, and
-// the unbiased integer t - 2^51 as an f64 (exact: |t - 2^51| <= 2^50).
+// x - 128 as an f64 for the unbiased integer x = t - 2^51 (exact:
+// |x| <= 2^50).
 struct Limbs {
   uint32_t lo, hi;
-  double xd;
+  double xs;
 };
 
 __device__ __forceinline__ Limbs limbs_of(uint64_t t) {
   // t is the mantissa of 1.5 * 2^52 + x_int, a double in [2^52, 2^53)
   const double y = __longlong_as_double(static_cast<long long>(0x4330000000000000ull | t));
   return Limbs{static_cast<uint32_t>(t), static_cast<uint32_t>(t >> 32),
-               __dsub_rn(y, 6755399441055744.0)};
+               __dsub_rn(y, kMagic + 128.0)};
 }
 
 // 2^e mod m, for the byte weights below.
@@ -246,18 +253,14 @@ __constant__ SplitConsts c_split[kL] = {
     split_consts(mod_of(9)),  split_consts(mod_of(10)), split_consts(mod_of(11)),
     split_consts(mod_of(12)), split_consts(mod_of(13))};
 
-// The same residue on the FP64 pipe, for half of the moduli, so that the
-// integer and FP64 pipes share the work.  q = rint(x / m) from one FMA with
-// 1.5 * 2^52 (x / m is known to 2^-10, so q is within one of the nearest
-// integer); r = x - q m is exact, |r| < m; adding 2^52 + m exactly leaves
-// m + r in (0, 2m) as the low word; one unsigned min folds it into [0, m).
+// Constants of the residue on the FP64 pipe: 1 / m rounded, which gives
+// (x - 128) / m to 2^-10 for |x| <= 2^50, and m.
 struct SplitF64 {
-  double inv, m, two52_plus_m;
+  double inv, m;
 };
 
 __host__ __device__ constexpr SplitF64 split_f64(uint32_t m) {
-  return SplitF64{1.0 / static_cast<double>(m), static_cast<double>(m),
-                  4503599627370496.0 + static_cast<double>(m)};
+  return SplitF64{1.0 / static_cast<double>(m), static_cast<double>(m)};
 }
 
 __constant__ SplitF64 c_split_f64[kL] = {
@@ -267,10 +270,31 @@ __constant__ SplitF64 c_split_f64[kL] = {
     split_f64(mod_of(9)),  split_f64(mod_of(10)), split_f64(mod_of(11)),
     split_f64(mod_of(12)), split_f64(mod_of(13))};
 
-// With kMixed, moduli 1..7 take the FP64 path and 8..13 the integer one;
-// otherwise all take the integer path.  0 (256) is a mask.
+// With kMixed, the moduli of residue_fp64 take the FP64 path and the others
+// the integer one; otherwise all take the integer path.  0 (256) is a mask.
 template <bool kMixed>
-constexpr bool residue_on_fp64(int l) { return kMixed && l >= 1 && l <= 7; }
+constexpr bool residue_on_fp64(int l) { return kMixed && residue_fp64(l); }
+
+// Residue on the FP64 pipe, three instructions: q = rint((x - 128) / m)
+// (x.xs = x - 128; the rounded 1 / m puts q within one of the nearest
+// integer), so x - q m = 128 + ((x - 128) - q m) lies in
+// [128 - m / 2 - m 2^-10, 128 + m / 2 + m 2^-10], inside [0, 255] for
+// m <= 255; and y - q m = 1.5 * 2^52 + (x - q m), exact, has x - q m as its
+// low word.  y = 1.5 * 2^52 + x is the quantised double itself.  The value
+// is a residue of x in [0, 256) but not always below m; the GEMM only needs
+// an unsigned byte of the right class.
+__device__ __forceinline__ uint32_t residue_fp64_path(const Limbs& x, int l) {
+  const SplitF64& c = c_split_f64[l];
+  const double q = __dsub_rn(__fma_rn(x.xs, c.inv, kMagic), kMagic);
+  const double y = __hiloint2double(static_cast<int>(0x43300000u | x.hi), static_cast<int>(x.lo));
+  return static_cast<uint32_t>(__double2loint(__fma_rn(-q, c.m, y)));
+}
+
+// Residue in [0, m) on the integer pipes.
+__device__ __forceinline__ uint32_t residue_int(const Limbs& x, const SplitConsts& c, uint32_t m) {
+  const uint32_t s = __dp4a(x.lo, c.w_lo, __dp4a(x.hi, c.w_hi, c.unbias));
+  return s - __umulhi(s, c.magic) * m;
+}
 
 template <int l, bool kMixed>
 __device__ __forceinline__ uint32_t residue(const Limbs& x) {
@@ -278,14 +302,9 @@ __device__ __forceinline__ uint32_t residue(const Limbs& x) {
   if constexpr (m == 256u) {
     return x.lo & 0xFFu;
   } else if constexpr (residue_on_fp64<kMixed>(l)) {
-    const SplitF64& c = c_split_f64[l];
-    const double q = __dsub_rn(__fma_rn(x.xd, c.inv, 6755399441055744.0), 6755399441055744.0);
-    const double r = __fma_rn(-q, c.m, x.xd);
-    const uint32_t v = static_cast<uint32_t>(__double2loint(__dadd_rn(r, c.two52_plus_m)));
-    return min(v, v - m);
+    return residue_fp64_path(x, l);
   } else {
-    const uint32_t s = __dp4a(x.lo, c_split[l].w_lo, __dp4a(x.hi, c_split[l].w_hi, c_split[l].unbias));
-    return s - __umulhi(s, c_split[l].magic) * m;
+    return residue_int(x, c_split[l], m);
   }
 }
 
@@ -317,9 +336,9 @@ __device__ __forceinline__ void store_planes_n(const Limbs (&x)[N], uint8_t* bas
   }
 }
 
-// The integer-path residue with the modulus picked at run time: the same
-// arithmetic as residue<l, false>, its constants read from the constant
-// bank by index (m = 256 works too: its weights select byte 0 and its
+// The residue with the modulus picked at run time: the same arithmetic as
+// residue<l, true>, its constants read from the constant bank by index
+// (m = 256 works on the integer path too: its weights select byte 0 and its
 // magic is 0).  A loop over the moduli built from it is a fourteenth of the
 // unrolled code, which keeps the column split's instruction stream in cache.
 __constant__ uint32_t c_mod_rt[kL] = {mod_of(0), mod_of(1), mod_of(2),  mod_of(3),  mod_of(4),
@@ -327,9 +346,8 @@ __constant__ uint32_t c_mod_rt[kL] = {mod_of(0), mod_of(1), mod_of(2),  mod_of(3
                                       mod_of(10), mod_of(11), mod_of(12), mod_of(13)};
 
 __device__ __forceinline__ uint32_t residue_rt(const Limbs& x, int l) {
-  const SplitConsts c = c_split[l];
-  const uint32_t s = __dp4a(x.lo, c.w_lo, __dp4a(x.hi, c.w_hi, c.unbias));
-  return s - __umulhi(s, c.magic) * c_mod_rt[l];
+  if (residue_fp64(l)) return residue_fp64_path(x, l);
+  return residue_int(x, c_split[l], c_mod_rt[l]);
 }
 
 // Residues of 16 consecutive values -> one 16-byte store per modulus plane,
@@ -654,6 +672,62 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
                      plane_stride);
 }
 
+// Pass 2 for an operand whose rows are contiguous (s_r == 1) into
+// row-contiguous planes [l][batch][Kp][rows_pad] (the GEMM reads them as an
+// MN-major operand, so nothing is transposed): one block per (1024 rows,
+// kMnSlab k), each thread four consecutive rows over the slab.  A warp
+// reads 1 KB of one k and writes 128 contiguous bytes per modulus.  The
+// slab is unrolled: a loop would keep the moduli's constants in registers
+// across iterations and spill.
+constexpr int kMnRows = 1024, kMnSlab = 2;
+
+__global__ void __launch_bounds__(256, 4)
+split_mn_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
+                int64_t batch, int P, const int* __restrict__ codes,
+                uint8_t* __restrict__ planes, int* __restrict__ shifts) {
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kMnRows + threadIdx.x * 4;
+  if (r0 >= rows_pad) return;  // rows_pad is a multiple of 4
+  int sh[4];
+  bool z[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t r = r0 + j;
+    const int s = r < rows ? shift_from_code(codes[b * rows_pad + r], P) : 0;
+    if (blockIdx.y == 0) shifts[b * rows_pad + r] = s;
+    z[j] = r >= rows || s == kShiftNonFinite || s == kShiftZero;
+    sh[j] = z[j] ? 0 : s;
+  }
+  const bool vec = o.f64 && o.s_r == 1 && r0 + 4 <= rows && (o.s_k & 1) == 0 &&
+                   (o.s_b & 1) == 0 && (reinterpret_cast<uintptr_t>(o.f64) & 15) == 0;
+  const size_t plane_stride = static_cast<size_t>(batch) * Kp * rows_pad;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * kMnSlab;
+#pragma unroll
+  for (int64_t k = k0; k < k0 + kMnSlab && k < Kp; ++k) {
+    double w[4] = {0.0, 0.0, 0.0, 0.0};
+    if (k < K) {
+      const int64_t off = b * o.s_b + r0 * o.s_r + k * o.s_k;
+      if (vec) {
+        const double2* p = reinterpret_cast<const double2*>(o.f64 + off);
+        const double2 v01 = __ldcs(p), v23 = __ldcs(p + 1);
+        w[0] = v01.x;
+        w[1] = v01.y;
+        w[2] = v23.x;
+        w[3] = v23.y;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (r0 + j < rows) w[j] = op_value(o, off + j * o.s_r);
+      }
+    }
+    Limbs x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(z[j] ? 0.0 : w[j], sh[j]));
+    store_planes_n<4, true>(x, planes + (static_cast<size_t>(b) * Kp + k) * rows_pad + r0,
+                            plane_stride);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Step 2: tcgen05 int8 GEMM.
 
@@ -737,6 +811,20 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   return d;
 }
 
+// MN-major operand tile with 128-byte swizzle, 128 bytes (one swizzle atom)
+// of M or N per CTA: rows of 128 B along MN, one per k; 8-k atoms of 1024 B
+// (stride byte offset).  The leading byte offset steps between 128-byte MN
+// atoms, of which a CTA's tile has one, so it is never applied.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;          // leading byte offset (unused here): 16 B
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: 8 k of 128 B
+  d |= static_cast<uint64_t>(1) << 46;          // version
+  d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
+  return d;
+}
+
 // kind::i8, D = s32, A = B = unsigned 8-bit (residues in [0, m)), both
 // K-major, N = 256, M = 128.
 constexpr uint32_t kIdesc = (2u << 4) | (0u << 7) | (0u << 10) |
@@ -744,12 +832,12 @@ constexpr uint32_t kIdesc = (2u << 4) | (0u << 7) | (0u << 10) |
                             (static_cast<uint32_t>(kTileM >> 4) << 24);
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t accumulate) {
+                                       uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -915,7 +1003,7 @@ ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const uint32_t b0 = smem_u32(smem_b + stage * kStageB);
 #pragma unroll
           for (int k = 0; k < kTileK / 32; ++k) {
-            mma_i8(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32), (kb | k) != 0 ? 1u : 0u);
+            mma_i8(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == kStages) {
@@ -1000,6 +1088,7 @@ constexpr int kSub2 = 2;  // 128-byte K sub-tiles per stage
 constexpr int kStage2 = kTileM * kTileK;  // 16 KB: A rows, or half of the B tile
 constexpr uint32_t kIdesc2 = (2u << 4) | (0u << 7) | (0u << 10) | ((256u >> 3) << 17) |
                              ((256u >> 4) << 24);
+constexpr uint32_t kIdescBMajorMN = 1u << 16;  // B MN-major
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -1066,13 +1155,22 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 int z, uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(mbar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                            uint32_t accumulate) {
+                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate));
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive (when the prior MMAs complete) on the barrier at this address in
@@ -1093,6 +1191,10 @@ __device__ __forceinline__ void mma_commit_pair_self(uint64_t* bar) {
       : "memory");
 }
 
+// kBMn: B's planes are [l][batch][Kp][Np] (N contiguous, from split_mn_kernel)
+// and load as MN-major tiles through a 3-D tensor map {Np, Kp, planes};
+// otherwise [l][batch][Np][Kp] like A's.
+template <bool kBMn>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
@@ -1149,6 +1251,8 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                         static_cast<int64_t>(w.tm) * 256 + rank * 128);
         const int yb = static_cast<int>((static_cast<int64_t>(w.l) * p.batch + w.b) * p.Np +
                                         static_cast<int64_t>(w.tn) * 256 + rank * 128);
+        const int xb = w.tn * 256 + static_cast<int>(rank) * 128;
+        const int zb = w.l * p.batch + w.b;
         for (int kb = 0; kb < (p.kblocks + kSub2 - 1) / kSub2; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 11)) {
             ok = false;
@@ -1160,7 +1264,10 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
           for (int sub = 0; sub < kSub2; ++sub) {
             const int x = (kb * kSub2 + sub) * kTileK;
             tma_load_2d_pair(smem_a + (stage * kSub2 + sub) * kStage2, &tmap_a, x, ya, full0);
-            tma_load_2d_pair(smem_b + (stage * kSub2 + sub) * kStage2, &tmap_b, x, yb, full0);
+            if constexpr (kBMn)
+              tma_load_3d_pair(smem_b + (stage * kSub2 + sub) * kStage2, &tmap_b, xb, x, zb, full0);
+            else
+              tma_load_2d_pair(smem_b + (stage * kSub2 + sub) * kStage2, &tmap_b, x, yb, full0);
           }
           if (++stage == kStages2) {
             stage = 0;
@@ -1186,6 +1293,7 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.err, 12)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc * 256);
+        constexpr uint32_t idesc = kBMn ? kIdesc2 | kIdescBMajorMN : kIdesc2;
         for (int kb = 0; kb < (p.kblocks + kSub2 - 1) / kSub2; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, 13)) {
             ok = false;
@@ -1198,8 +1306,10 @@ ozaki_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t b0 = smem_u32(smem_b + (stage * kSub2 + sub) * kStage2);
 #pragma unroll
             for (int k = 0; k < kTileK / 32; ++k) {
-              mma_i8_pair(d, sdesc(a0 + k * 32), sdesc(b0 + k * 32),
-                          (kb | sub | k) != 0 ? 1u : 0u);
+              // 32 k per instruction: 32 bytes along a K-major row, or 32
+              // rows of 128 bytes of an MN-major tile
+              const uint64_t bdesc = kBMn ? sdesc_mn(b0 + k * 32 * 128) : sdesc(b0 + k * 32);
+              mma_i8_pair(d, sdesc(a0 + k * 32), bdesc, idesc, (kb | sub | k) != 0 ? 1u : 0u);
             }
           }
           mma_commit_pair(&empty[stage]);
@@ -1643,6 +1753,24 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t Kp, int64_t rows, int 
   return DS_OK;
 }
 
+// Row-contiguous planes [planes][Kp][Np] (MN-major B): boxes of 128 rows
+// (128 bytes) x 128 k of one plane.  k past Kp reads as zero.
+int make_tmap_mn(CUtensorMap* map, const void* base, int64_t Np, int64_t Kp, int64_t planes) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(DS_INTERNAL, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Np), static_cast<cuuint64_t>(Kp),
+                              static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Np), static_cast<cuuint64_t>(Np * Kp)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTileN / 2), static_cast<cuuint32_t>(kTileK),
+                             1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DS_INTERNAL, "cuTensorMapEncodeTiled failed");
+  return DS_OK;
+}
+
 size_t gemm_smem_bytes() {
   return 1024 + kStages * (kStageA + kStageB) + (2 * kStages + 5) * sizeof(uint64_t) + 16;
 }
@@ -1674,7 +1802,11 @@ const GemmSetup& gemm_setup() {
     g.err = cudaFuncSetAttribute(ozaki_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(gemm_smem_bytes()));
     if (g.err == cudaSuccess)
-      g.err = cudaFuncSetAttribute(ozaki_gemm2_kernel,
+      g.err = cudaFuncSetAttribute(ozaki_gemm2_kernel<false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(gemm2_smem_bytes()));
+    if (g.err == cudaSuccess)
+      g.err = cudaFuncSetAttribute(ozaki_gemm2_kernel<true>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(gemm2_smem_bytes()));
     const char* one = std::getenv("DS_B200_GEMM_1CTA");
@@ -1691,7 +1823,8 @@ const GemmSetup& gemm_setup() {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      const cudaError_t qe = cudaOccupancyMaxActiveClusters(&n, ozaki_gemm2_kernel, &cfg);
+      // both instantiations have the same resources
+      const cudaError_t qe = cudaOccupancyMaxActiveClusters(&n, ozaki_gemm2_kernel<false>, &cfg);
       if (qe == cudaSuccess) {
         g.pair_clusters = n;
       } else {
@@ -1710,9 +1843,26 @@ const GemmSetup& gemm_setup() {
 // max and the tiled column split over all rows.
 bool split_by_rows(const DotOperand& o, int64_t rows) { return o.s_k == 1 || rows == 1; }
 
+// Pass 2 of a column split: K-major planes (split_cols_kernel), or with mn
+// row-contiguous ones (split_mn_kernel).
+void launch_split_cols(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad,
+                       int64_t K, int64_t Kp, int P, const int* codes, uint8_t* planes,
+                       int* shifts, bool mn, cudaStream_t s) {
+  ProfileScope prof("ozaki_split_cols", s);
+  if (mn) {
+    dim3 g(static_cast<unsigned>((rows_pad + kMnRows - 1) / kMnRows),
+           static_cast<unsigned>((Kp + kMnSlab - 1) / kMnSlab), static_cast<unsigned>(batch));
+    split_mn_kernel<<<g, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
+  } else {
+    dim3 g(static_cast<unsigned>(rows_pad / kColTileR), static_cast<unsigned>(Kp / kColTileK),
+           static_cast<unsigned>(batch));
+    split_cols_kernel<<<g, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
+  }
+}
+
 int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
                  int64_t Kp, int P, uint8_t* planes, int* shifts, int* codes, cudaStream_t s,
-                 int64_t row0 = 0, int64_t row1 = -1) {
+                 bool mn = false, int64_t row0 = 0, int64_t row1 = -1) {
   if (split_by_rows(o, rows)) {
     if (row1 < 0) row1 = rows_pad;
     ProfileScope prof("ozaki_split_rows", s);
@@ -1728,10 +1878,7 @@ int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_
       ProfileScope prof("ozaki_colmax", s);
       colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
     }
-    ProfileScope prof("ozaki_split_cols", s);
-    dim3 g2(static_cast<unsigned>(rows_pad / kColTileR), static_cast<unsigned>(Kp / kColTileK),
-            static_cast<unsigned>(batch));
-    split_cols_kernel<<<g2, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
+    launch_split_cols(o, batch, rows, rows_pad, K, Kp, P, codes, planes, shifts, mn, s);
   }
   return launch_status();
 }
@@ -1848,11 +1995,18 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
   int* err = reinterpret_cast<int*>(ws + g.off_err);
   const int P = bits_for_k(p.K);
 
+  // B split by columns with its rows contiguous (a row-major [K, N] B) is
+  // written N-contiguous and read by the pair kernel as an MN-major operand.
+  const bool b_mn = pair && !split_by_rows(p.b, p.N) && p.b.s_r == 1;
   CUtensorMap ta, tb;
   if (int st = make_tmap(&ta, planes_a, g.Kp, kL * p.batch * g.Mp, kTileM)) return st;
   // The pair kernel loads half of each 256-row B tile per CTA.
-  if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np, pair ? kTileN / 2 : kTileN))
+  if (b_mn) {
+    if (int st = make_tmap_mn(&tb, planes_b, g.Np, g.Kp, kL * p.batch)) return st;
+  } else if (int st = make_tmap(&tb, planes_b, g.Kp, kL * p.batch * g.Np,
+                                pair ? kTileN / 2 : kTileN)) {
     return st;
+  }
   const int tile_rows = pair ? 2 * kTileM : kTileM;
   GemmParams gp{};
   gp.batch = static_cast<int>(p.batch);
@@ -1909,7 +2063,10 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
       cfg.stream = st;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel, ta, tb, q));
+      if (b_mn)
+        DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel<true>, ta, tb, q));
+      else
+        DSB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ozaki_gemm2_kernel<false>, ta, tb, q));
     } else {
       const int grid = static_cast<int>(q.units < sm_count() ? q.units : sm_count());
       ozaki_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), st>>>(ta, tb, q);
@@ -1959,16 +2116,14 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
           p.a, p.M, g.Mp, p.b, p.N, g.Np, p.K, g.Kp, P, planes_a, sa, cb, nc, cgx, cgy);
       if (int st = launch_status()) return st;
     }
-    ProfileScope prof3("ozaki_split_cols", s);
-    dim3 g2(static_cast<unsigned>(g.Np / kColTileR), static_cast<unsigned>(g.Kp / kColTileK), 1);
-    split_cols_kernel<<<g2, 256, 0, s>>>(p.b, p.N, p.K, g.Np, g.Kp, 1, P, cb, planes_b, sb);
+    launch_split_cols(p.b, 1, p.N, g.Np, p.K, g.Kp, P, cb, planes_b, sb, b_mn, s);
     if (int st = launch_status()) return st;
   } else {
     DSB_CUDA_TRY(cudaMemsetAsync(err, 0, clear_end - reinterpret_cast<uint8_t*>(err), s));
     ProfileScope prof("ozaki_split", s);
     if (int st = launch_split(p.a, p.batch, p.M, g.Mp, p.K, g.Kp, P, planes_a, sa, ca, s))
       return st;
-    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, cb, s))
+    if (int st = launch_split(p.b, p.batch, p.N, g.Np, p.K, g.Kp, P, planes_b, sb, cb, s, b_mn))
       return st;
   }
   if (int st = launch_gemm(0, static_cast<int>(g.Mp / tile_rows), s)) return st;

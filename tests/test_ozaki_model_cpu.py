@@ -5,17 +5,22 @@ row to a P-bit integer, multiplies residues modulo 14 coprime moduli exactly,
 and rebuilds the product by the Chinese remainder theorem in two f64 limbs
 (the weights split at bit 70).  This restates those steps in NumPy/Python
 integers at small sizes: the byte-dot-product residues of the biased
-quantised integers, the unsigned residue GEMM, and the two-limb
-reconstruction, whose only rounding is far below the quantisation error.
+quantised integers (in [0, m)), the FP64-pipe residues of half of the
+moduli (in [0, 255], not always below m), the unsigned residue GEMM with the
+epilogue's reduction, and the two-limb reconstruction, whose only rounding
+is far below the quantisation error.
 """
 import math
+from fractions import Fraction
 
 import numpy as np
 
 from oracle import exact
 
 MODULI = [256, 255, 253, 251, 247, 241, 239, 233, 229, 227, 223, 217, 211, 199]
+FP64_PATH = set(range(1, 11))  # indices of the moduli split on the FP64 pipe
 SPLIT = 70  # W = W_hi * 2^70 + W_lo
+MAGIC = 1.5 * 2.0 ** 52
 
 
 def consts():
@@ -71,6 +76,54 @@ def byte_residue(x_int, m):
     assert s < 2 ** 19
     magic = (2 ** 32 - 1) // m + 1
     return s - ((s * magic) >> 32) * m
+
+
+def rint_even(f):
+    """Round a Fraction to the nearest integer, ties to even."""
+    fl = math.floor(f)
+    d = f - fl
+    if d > Fraction(1, 2) or (d == Fraction(1, 2) and fl % 2 == 1):
+        return fl + 1
+    return fl
+
+
+def fp64_residue(x_int, m):
+    """The split kernel's FP64-pipe residue: q = fma(x - 128, RN(1/m),
+    1.5 * 2^52) - 1.5 * 2^52 ((x - 128) * RN(1/m) rounded to an integer,
+    ties to even), then fma(-q, m, 1.5 * 2^52 + x), exact, whose low word is
+    x - q m."""
+    inv = Fraction(1.0 / m)  # the double nearest 1/m, exactly
+    q = rint_even(Fraction(x_int - 128) * inv)
+    y = Fraction(MAGIC) + x_int - q * m  # the fma's exact result ...
+    assert y == int(y) and 2 ** 52 <= y < 2 ** 53  # ... is a double: no rounding
+    return x_int - q * m
+
+
+def residue(x_int, l):
+    """The residue of modulus index l as the split writes it (a byte)."""
+    m = MODULI[l]
+    return fp64_residue(x_int, m) if l in FP64_PATH else byte_residue(x_int, m)
+
+
+def test_fp64_residues():
+    """x - q m is in [0, 255] for |x| <= 2^50, including x next to the
+    points where (x - 128) / m is a half-integer and the rounded quotient
+    may pick either neighbour."""
+    rng = np.random.default_rng(4)
+    for l in FP64_PATH:
+        m = MODULI[l]
+        vals = [0, 1, -1, 127, 128, 129, 2 ** 50, -(2 ** 50), 2 ** 50 - 1]
+        vals += [int(v) for v in rng.integers(-(2 ** 50), 2 ** 50, 4000)]
+        for k in [int(v) for v in rng.integers(-(2 ** 50) // m, 2 ** 50 // m, 400)]:
+            for d in (-1, 0, 1):
+                vals.append(128 + k * m + m // 2 + d)
+                vals.append(128 + k * m - m // 2 + d)
+        for x in vals:
+            if abs(x) > 2 ** 50:
+                continue
+            r = fp64_residue(x, m)
+            assert 0 <= r <= 255
+            assert (x - r) % m == 0
 
 
 def test_byte_residues():
@@ -140,8 +193,8 @@ def model_gemm(A, B):
             # per-modulus GEMM on unsigned residues (u8 x u8 -> s32), as the
             # tensor cores do; the epilogue keeps the sum mod m
             res = []
-            for m in MODULI:
-                acc = sum(byte_residue(x, m) * byte_residue(y, m) for x, y in zip(ai[i], bi[j]))
+            for l, m in enumerate(MODULI):
+                acc = sum(residue(x, l) * residue(y, l) for x, y in zip(ai[i], bi[j]))
                 assert 0 <= acc < 2 ** 31
                 res.append(acc % m)
             got, _ = crt_limbs(res)
