@@ -1412,7 +1412,7 @@ __device__ __forceinline__ void put_result(const DotResult& c, int64_t idx, doub
 }
 
 constexpr int kCrtThreads = 128;
-constexpr int kCrtCols = 4;  // consecutive outputs per thread
+constexpr int kCrtCols = 4;  // consecutive outputs per thread (4 or 8)
 
 // Byte q of `word` as an f64: the bits of 2^52 + byte, minus 2^52 -- one
 // add on the FP64 pipe instead of a quarter-rate integer conversion.
@@ -1439,18 +1439,68 @@ __device__ __forceinline__ double pow2_normal(int e) {
 // Such outputs are recomputed with a compensated dot product (fix_kernel).
 constexpr int kCertifyBits = 24;
 
-// blockIdx.x * 512 is the first column of the block; blockIdx.y strides over
-// the batch*M output rows, so each thread rebuilds 4 consecutive outputs of
-// several rows (one 4-byte load per residue plane and row) with its
-// columns' scale exponents loaded once per batch entry.
-__global__ void __launch_bounds__(kCrtThreads, 8)
+__device__ __forceinline__ bool shift_ordinary(int s) {
+  return s != kShiftNonFinite && s != kShiftZero;
+}
+
+// One output of the CRT from its two limbs: non-finite operands, zero rows
+// and columns, and uncertified outputs (listed for fix_kernel) included.
+__device__ __forceinline__ void crt_finish(const CrtParams& p, bool failed, int64_t row,
+                                           int64_t b, int64_t i, int64_t j, int sa, int sb,
+                                           double s_hi, double s_lo) {
+  double out;
+  if (failed) {
+    out = __longlong_as_double(0x7ff8000000000000LL);
+  } else if (sa == kShiftNonFinite || sb == kShiftNonFinite) {
+    // A non-finite operand: the IEEE sum of the products carries NaN/Inf
+    // as a float GEMM would.
+    double s = 0.0;
+    for (int64_t k = 0; k < p.K; ++k)
+      s += op_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
+           op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
+    out = s;
+  } else if (sa == kShiftZero || sb == kShiftZero) {
+    out = 0.0;  // a row or column of zeros
+  } else {
+    // C = S - round(S / Mprod) * Mprod: the quotient is exact (S / Mprod
+    // lies within 0.22 of an integer), the high limb difference is an
+    // exact integer below 2^53, and the low limb carries the only
+    // rounding (below 2^34 units of C_int).
+    const double approx = __fma_rn(s_hi, 0x1p70, s_lo);
+    const double qt = rint(approx * p.inv_m);
+    const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi);
+    const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo);
+    const double c = __fma_rn(t_hi, 0x1p70, t_lo);
+    if (!(fabs(c) >= p.certify_below)) {
+      // uncertified: listed for fix_kernel, which writes this output
+      const int slot = atomicAdd(p.fix_count, 1);
+      if (slot < p.fix_cap) p.fix_list[slot] = static_cast<uint64_t>(row * p.N + j);
+      return;
+    }
+    // scale by 2^-(sa + sb): one exact multiply when 2^-(sa+sb) is normal
+    const int e = -(sa + sb);
+    out = (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sb);
+  }
+  put_result(p.c, row * p.N + j, out);
+}
+
+// blockIdx.x * kCrtThreads * kCols is the first column of the block;
+// blockIdx.y strides over the batch*M output rows, so each thread rebuilds
+// kCols consecutive outputs of several rows (one kCols-byte load per
+// residue plane and row) with its columns' scale exponents loaded once per
+// batch entry.  Rows and columns with ordinary shifts (the common case) take
+// a path without per-output tests of the special codes.
+template <int kCols>
+__global__ void __launch_bounds__(kCrtThreads, kCols == 4 ? 8 : 6)
 crt_kernel(CrtParams p) {
+  static_assert(kCols == 4 || kCols == 8, "one or two residue words per plane");
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
-  const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCrtCols;
+  const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCols;
   if (j0 >= p.N) return;
   int64_t cur_b = -1;
-  int sbv[kCrtCols];
+  int sbv[kCols];
+  bool cols_ordinary = false;  // all kCols columns exist and have ordinary shifts
   // (b, i) of the flattened row, advanced without a 64-bit division per row
   int64_t b = (p.row_begin + blockIdx.y) / p.M;
   int64_t i = (p.row_begin + blockIdx.y) - b * p.M;
@@ -1462,65 +1512,61 @@ crt_kernel(CrtParams p) {
     }
     if (b != cur_b) {
       cur_b = b;
+      cols_ordinary = !failed && j0 + kCols <= p.N;
 #pragma unroll
-      for (int q = 0; q < kCrtCols; ++q)
+      for (int q = 0; q < kCols; ++q) {
         sbv[q] = j0 + q < p.N ? p.sb[b * p.Np + j0 + q] : 0;
+        cols_ordinary &= shift_ordinary(sbv[q]);
+      }
     }
     const int sa = p.sa[b * p.Mp + i];
-    const size_t at = (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
-    double s_hi[kCrtCols], s_lo[kCrtCols];
+    const uint8_t* src = p.cres + (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
+    double s_hi[kCols], s_lo[kCols];
 #pragma unroll
-    for (int q = 0; q < kCrtCols; ++q) s_hi[q] = s_lo[q] = 0.0;
+    for (int q = 0; q < kCols; ++q) s_hi[q] = s_lo[q] = 0.0;
 #pragma unroll
     for (int l = 0; l < kL; ++l) {
-      const uint32_t word = __ldcs(reinterpret_cast<const unsigned int*>(p.cres + l * plane + at));
+      uint32_t words[kCols / 4];
+      if constexpr (kCols == 4) {
+        words[0] = __ldcs(reinterpret_cast<const unsigned int*>(src + l * plane));
+      } else {
+        const uint2 w2 = __ldcs(reinterpret_cast<const uint2*>(src + l * plane));
+        words[0] = w2.x;
+        words[1] = w2.y;
+      }
       const double w_hi = p.w[l][0], w_lo = p.w[l][1];
 #pragma unroll
-      for (int q = 0; q < kCrtCols; ++q) {
-        const double r = byte_to_f64(word, q);
+      for (int q = 0; q < kCols; ++q) {
+        const double r = byte_to_f64(words[q / 4], q % 4);
         s_hi[q] = __fma_rn(r, w_hi, s_hi[q]);  // exact
         s_lo[q] = __fma_rn(r, w_lo, s_lo[q]);
       }
     }
+    if (cols_ordinary && shift_ordinary(sa)) {
 #pragma unroll
-    for (int q = 0; q < kCrtCols; ++q) {
-      const int64_t j = j0 + q;
-      if (j >= p.N) break;
-      const int sb = sbv[q];
-      double out;
-      if (failed) {
-        out = __longlong_as_double(0x7ff8000000000000LL);
-      } else if (sa == kShiftNonFinite || sb == kShiftNonFinite) {
-        // A non-finite operand: the IEEE sum of the products carries NaN/Inf
-        // as a float GEMM would.
-        double s = 0.0;
-        for (int64_t k = 0; k < p.K; ++k)
-          s += op_value(p.a, b * p.a.s_b + i * p.a.s_r + k * p.a.s_k) *
-               op_value(p.b, b * p.b.s_b + j * p.b.s_r + k * p.b.s_k);
-        out = s;
-      } else if (sa == kShiftZero || sb == kShiftZero) {
-        out = 0.0;  // a row or column of zeros
-      } else {
-        // C = S - round(S / Mprod) * Mprod: the quotient is exact (S / Mprod
-        // lies within 0.22 of an integer), the high limb difference is an
-        // exact integer below 2^53, and the low limb carries the only
-        // rounding (below 2^34 units of C_int).
+      for (int q = 0; q < kCols; ++q) {
         const double approx = __fma_rn(s_hi[q], 0x1p70, s_lo[q]);
         const double qt = rint(approx * p.inv_m);
         const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi[q]);
         const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo[q]);
         const double c = __fma_rn(t_hi, 0x1p70, t_lo);
+        const int64_t j = j0 + q;
         if (!(fabs(c) >= p.certify_below)) {
-          // uncertified: listed for fix_kernel, which writes this output
           const int slot = atomicAdd(p.fix_count, 1);
           if (slot < p.fix_cap) p.fix_list[slot] = static_cast<uint64_t>(row * p.N + j);
           continue;
         }
-        // scale by 2^-(sa + sb): one exact multiply when 2^-(sa+sb) is normal
-        const int e = -(sa + sb);
-        out = (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sb);
+        const int e = -(sa + sbv[q]);
+        const double out =
+            (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sbv[q]);
+        put_result(p.c, row * p.N + j, out);
       }
-      put_result(p.c, row * p.N + j, out);
+    } else {
+#pragma unroll
+      for (int q = 0; q < kCols; ++q) {
+        if (j0 + q >= p.N) break;
+        crt_finish(p, failed, row, b, i, j0 + q, sa, sbv[q], s_hi[q], s_lo[q]);
+      }
     }
   }
 }
@@ -2088,7 +2134,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
     if (gy > n) gy = n;
     if (gy > 65535) gy = 65535;
     dim3 cg(static_cast<unsigned>(gx), static_cast<unsigned>(gy < 1 ? 1 : gy));
-    crt_kernel<<<cg, kCrtThreads, 0, st>>>(q);
+    crt_kernel<kCrtCols><<<cg, kCrtThreads, 0, st>>>(q);
     return launch_status();
   };
 
