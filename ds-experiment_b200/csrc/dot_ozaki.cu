@@ -674,57 +674,61 @@ split_cols_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64
 
 // Pass 2 for an operand whose rows are contiguous (s_r == 1) into
 // row-contiguous planes [l][batch][Kp][rows_pad] (the GEMM reads them as an
-// MN-major operand, so nothing is transposed): one block per (1024 rows,
-// kMnSlab k), each thread four consecutive rows over the slab.  A warp
-// reads 1 KB of one k and writes 128 contiguous bytes per modulus.  The
-// slab is unrolled: a loop would keep the moduli's constants in registers
-// across iterations and spill.
-constexpr int kMnRows = 1024, kMnSlab = 2;
+// MN-major operand, so nothing is transposed): one block per (kMnRows rows,
+// kMnSlab k), each thread kMnCols consecutive rows over the slab.  A warp
+// reads 32 * kMnCols values of one k and writes 32 * kMnCols contiguous
+// bytes per modulus.  The slab is unrolled: a loop would keep the moduli's
+// constants in registers across iterations and spill.  (Two rows per thread,
+// 40 registers and half again as many warps, was 15% slower.)
+constexpr int kMnCols = 4, kMnRows = 256 * kMnCols, kMnSlab = 2;
 
 __global__ void __launch_bounds__(256, 4)
 split_mn_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, int64_t Kp,
                 int64_t batch, int P, const int* __restrict__ codes,
                 uint8_t* __restrict__ planes, int* __restrict__ shifts) {
   const int64_t b = blockIdx.z;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kMnRows + threadIdx.x * 4;
-  if (r0 >= rows_pad) return;  // rows_pad is a multiple of 4
-  int sh[4];
-  bool z[4];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kMnRows + threadIdx.x * kMnCols;
+  if (r0 >= rows_pad) return;  // rows_pad is a multiple of kMnCols
+  int sh[kMnCols];
+  bool z[kMnCols];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < kMnCols; ++j) {
     const int64_t r = r0 + j;
     const int s = r < rows ? shift_from_code(codes[b * rows_pad + r], P) : 0;
     if (blockIdx.y == 0) shifts[b * rows_pad + r] = s;
     z[j] = r >= rows || s == kShiftNonFinite || s == kShiftZero;
     sh[j] = z[j] ? 0 : s;
   }
-  const bool vec = o.f64 && o.s_r == 1 && r0 + 4 <= rows && (o.s_k & 1) == 0 &&
+  const bool vec = o.f64 && o.s_r == 1 && r0 + kMnCols <= rows && (o.s_k & 1) == 0 &&
                    (o.s_b & 1) == 0 && (reinterpret_cast<uintptr_t>(o.f64) & 15) == 0;
   const size_t plane_stride = static_cast<size_t>(batch) * Kp * rows_pad;
   const int64_t k0 = static_cast<int64_t>(blockIdx.y) * kMnSlab;
 #pragma unroll
   for (int64_t k = k0; k < k0 + kMnSlab && k < Kp; ++k) {
-    double w[4] = {0.0, 0.0, 0.0, 0.0};
+    double w[kMnCols];
+#pragma unroll
+    for (int j = 0; j < kMnCols; ++j) w[j] = 0.0;
     if (k < K) {
       const int64_t off = b * o.s_b + r0 * o.s_r + k * o.s_k;
       if (vec) {
         const double2* p = reinterpret_cast<const double2*>(o.f64 + off);
-        const double2 v01 = __ldcs(p), v23 = __ldcs(p + 1);
-        w[0] = v01.x;
-        w[1] = v01.y;
-        w[2] = v23.x;
-        w[3] = v23.y;
+#pragma unroll
+        for (int h = 0; h < kMnCols / 2; ++h) {
+          const double2 v = __ldcs(p + h);
+          w[2 * h] = v.x;
+          w[2 * h + 1] = v.y;
+        }
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < kMnCols; ++j)
           if (r0 + j < rows) w[j] = op_value(o, off + j * o.s_r);
       }
     }
-    Limbs x[4];
+    Limbs x[kMnCols];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = limbs_of(quantise(z[j] ? 0.0 : w[j], sh[j]));
-    store_planes_n<4, true>(x, planes + (static_cast<size_t>(b) * Kp + k) * rows_pad + r0,
-                            plane_stride);
+    for (int j = 0; j < kMnCols; ++j) x[j] = limbs_of(quantise(z[j] ? 0.0 : w[j], sh[j]));
+    store_planes_n<kMnCols, true>(x, planes + (static_cast<size_t>(b) * Kp + k) * rows_pad + r0,
+                                  plane_stride);
   }
 }
 
@@ -1412,7 +1416,7 @@ __device__ __forceinline__ void put_result(const DotResult& c, int64_t idx, doub
 }
 
 constexpr int kCrtThreads = 128;
-constexpr int kCrtCols = 4;  // consecutive outputs per thread (4 or 8)
+constexpr int kCrtCols = 4;  // consecutive outputs per thread: one residue word per plane
 
 // Byte q of `word` as an f64: the bits of 2^52 + byte, minus 2^52 -- one
 // add on the FP64 pipe instead of a quarter-rate integer conversion.
@@ -1484,32 +1488,49 @@ __device__ __forceinline__ void crt_finish(const CrtParams& p, bool failed, int6
   put_result(p.c, row * p.N + j, out);
 }
 
-// blockIdx.x * kCrtThreads * kCols is the first column of the block;
+// The 14 residue words (4 outputs each) of one row of a thread.
+__device__ __forceinline__ void crt_load(uint32_t (&w)[kL], const uint8_t* src, size_t plane) {
+#pragma unroll
+  for (int l = 0; l < kL; ++l) w[l] = __ldcs(reinterpret_cast<const unsigned int*>(src + l * plane));
+}
+
+// blockIdx.x * kCrtThreads * kCrtCols is the first column of the block;
 // blockIdx.y strides over the batch*M output rows, so each thread rebuilds
-// kCols consecutive outputs of several rows (one kCols-byte load per
-// residue plane and row) with its columns' scale exponents loaded once per
-// batch entry.  Rows and columns with ordinary shifts (the common case) take
-// a path without per-output tests of the special codes.
-template <int kCols>
-__global__ void __launch_bounds__(kCrtThreads, kCols == 4 ? 8 : 6)
+// kCrtCols consecutive outputs of several rows (one 4-byte load per residue
+// plane and row) with its columns' scale exponents loaded once per batch
+// entry.  Rows and columns with ordinary shifts (the common case) take a
+// path without per-output tests of the special codes, and store their four
+// outputs as two 16-byte words when all four are certified.  Occupancy
+// decides its speed: issuing the next row's loads before this row's
+// arithmetic (80 registers) or capping the registers at 48 or 40 (spills)
+// were 7 to 10% slower than 64 registers and 8 blocks per SM.
+__global__ void __launch_bounds__(kCrtThreads, 8)
 crt_kernel(CrtParams p) {
-  static_assert(kCols == 4 || kCols == 8, "one or two residue words per plane");
+  constexpr int kCols = kCrtCols;
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
   const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCols;
-  if (j0 >= p.N) return;
+  int64_t row = p.row_begin + blockIdx.y;
+  if (j0 >= p.N || row >= p.row_end) return;
   int64_t cur_b = -1;
   int sbv[kCols];
   bool cols_ordinary = false;  // all kCols columns exist and have ordinary shifts
   // (b, i) of the flattened row, advanced without a 64-bit division per row
-  int64_t b = (p.row_begin + blockIdx.y) / p.M;
-  int64_t i = (p.row_begin + blockIdx.y) - b * p.M;
-  for (int64_t row = p.row_begin + blockIdx.y; row < p.row_end;
-       row += gridDim.y, i += gridDim.y) {
-    while (i >= p.M) {
-      i -= p.M;
-      ++b;
+  int64_t b = row / p.M;
+  int64_t i = row - b * p.M;
+  auto src_of = [&](int64_t bb, int64_t ii) {
+    return p.cres + (static_cast<size_t>(bb) * p.Mp + ii) * p.Np + j0;
+  };
+  uint32_t cur[kL];
+  crt_load(cur, src_of(b, i), plane);
+  for (;;) {
+    const int64_t next = row + gridDim.y;
+    int64_t nb = b, ni = i + gridDim.y;
+    while (ni >= p.M) {
+      ni -= p.M;
+      ++nb;
     }
+    const bool more = next < p.row_end;
     if (b != cur_b) {
       cur_b = b;
       cols_ordinary = !failed && j0 + kCols <= p.N;
@@ -1520,29 +1541,23 @@ crt_kernel(CrtParams p) {
       }
     }
     const int sa = p.sa[b * p.Mp + i];
-    const uint8_t* src = p.cres + (static_cast<size_t>(b) * p.Mp + i) * p.Np + j0;
     double s_hi[kCols], s_lo[kCols];
 #pragma unroll
     for (int q = 0; q < kCols; ++q) s_hi[q] = s_lo[q] = 0.0;
 #pragma unroll
     for (int l = 0; l < kL; ++l) {
-      uint32_t words[kCols / 4];
-      if constexpr (kCols == 4) {
-        words[0] = __ldcs(reinterpret_cast<const unsigned int*>(src + l * plane));
-      } else {
-        const uint2 w2 = __ldcs(reinterpret_cast<const uint2*>(src + l * plane));
-        words[0] = w2.x;
-        words[1] = w2.y;
-      }
       const double w_hi = p.w[l][0], w_lo = p.w[l][1];
 #pragma unroll
       for (int q = 0; q < kCols; ++q) {
-        const double r = byte_to_f64(words[q / 4], q % 4);
+        const double r = byte_to_f64(cur[l], q);
         s_hi[q] = __fma_rn(r, w_hi, s_hi[q]);  // exact
         s_lo[q] = __fma_rn(r, w_lo, s_lo[q]);
       }
     }
     if (cols_ordinary && shift_ordinary(sa)) {
+      double out[kCols];
+      bool cert[kCols];
+      bool all = true;
 #pragma unroll
       for (int q = 0; q < kCols; ++q) {
         const double approx = __fma_rn(s_hi[q], 0x1p70, s_lo[q]);
@@ -1550,16 +1565,24 @@ crt_kernel(CrtParams p) {
         const double t_hi = __fma_rn(-qt, p.mlimb[0], s_hi[q]);
         const double t_lo = __fma_rn(-qt, p.mlimb[1], s_lo[q]);
         const double c = __fma_rn(t_hi, 0x1p70, t_lo);
-        const int64_t j = j0 + q;
-        if (!(fabs(c) >= p.certify_below)) {
+        cert[q] = fabs(c) >= p.certify_below;
+        all &= cert[q];
+        if (!cert[q]) {
+          // uncertified: listed for fix_kernel, which writes this output
           const int slot = atomicAdd(p.fix_count, 1);
-          if (slot < p.fix_cap) p.fix_list[slot] = static_cast<uint64_t>(row * p.N + j);
-          continue;
+          if (slot < p.fix_cap) p.fix_list[slot] = static_cast<uint64_t>(row * p.N + j0 + q);
         }
         const int e = -(sa + sbv[q]);
-        const double out =
-            (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sbv[q]);
-        put_result(p.c, row * p.N + j, out);
+        out[q] = (e >= -1022 && e <= 1023) ? c * pow2_normal(e) : scale2(scale2(c, -sa), -sbv[q]);
+      }
+      double* dst = p.c.f64 ? p.c.f64 + row * p.N + j0 : nullptr;
+      if (all && dst && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<double2*>(dst)[0] = make_double2(out[0], out[1]);
+        reinterpret_cast<double2*>(dst)[1] = make_double2(out[2], out[3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kCols; ++q)
+          if (cert[q]) put_result(p.c, row * p.N + j0 + q, out[q]);
       }
     } else {
 #pragma unroll
@@ -1568,6 +1591,11 @@ crt_kernel(CrtParams p) {
         crt_finish(p, failed, row, b, i, j0 + q, sa, sbv[q], s_hi[q], s_lo[q]);
       }
     }
+    if (!more) break;
+    row = next;
+    b = nb;
+    i = ni;
+    crt_load(cur, src_of(b, i), plane);
   }
 }
 
@@ -2134,7 +2162,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
     if (gy > n) gy = n;
     if (gy > 65535) gy = 65535;
     dim3 cg(static_cast<unsigned>(gx), static_cast<unsigned>(gy < 1 ? 1 : gy));
-    crt_kernel<kCrtCols><<<cg, kCrtThreads, 0, st>>>(q);
+    crt_kernel<<<cg, kCrtThreads, 0, st>>>(q);
     return launch_status();
   };
 
