@@ -72,10 +72,11 @@ __host__ __device__ constexpr int mod_of(int l) {
        : l == 10 ? 223 : l == 11 ? 217 : l == 12 ? 211 : 199;
 }
 
-// Moduli whose split residue is taken on the FP64 pipe (three FP64
-// instructions) rather than the integer pipes (two byte dot products and a
-// multiply-high reduction, all on the FMA-heavy pipe): ten of the thirteen
-// were fastest in both split kernels (7: +3%, 13: +6 to 18%).
+// Moduli whose split residue is taken from the FP64 pipe (one FMA and one
+// integer multiply-add) rather than the integer pipes (two byte dot
+// products and a multiply-high reduction).  Ten of the thirteen were
+// fastest: with all thirteen the row split spills (its group loop keeps
+// every 1 / m in a register), with seven both splits are 4 to 6% slower.
 __host__ __device__ constexpr bool residue_fp64(int l) { return l >= 1 && l <= 10; }
 
 // ---------------------------------------------------------------------------
@@ -253,41 +254,30 @@ __constant__ SplitConsts c_split[kL] = {
     split_consts(mod_of(9)),  split_consts(mod_of(10)), split_consts(mod_of(11)),
     split_consts(mod_of(12)), split_consts(mod_of(13))};
 
-// Constants of the residue on the FP64 pipe: 1 / m rounded, which gives
-// (x - 128) / m to 2^-10 for |x| <= 2^50, and m.
-struct SplitF64 {
-  double inv, m;
-};
-
-__host__ __device__ constexpr SplitF64 split_f64(uint32_t m) {
-  return SplitF64{1.0 / static_cast<double>(m), static_cast<double>(m)};
-}
-
-__constant__ SplitF64 c_split_f64[kL] = {
-    split_f64(mod_of(0)),  split_f64(mod_of(1)),  split_f64(mod_of(2)),
-    split_f64(mod_of(3)),  split_f64(mod_of(4)),  split_f64(mod_of(5)),
-    split_f64(mod_of(6)),  split_f64(mod_of(7)),  split_f64(mod_of(8)),
-    split_f64(mod_of(9)),  split_f64(mod_of(10)), split_f64(mod_of(11)),
-    split_f64(mod_of(12)), split_f64(mod_of(13))};
+// 1 / m rounded, for the residue from the FP64 pipe: (x - 128) / m to
+// 2^-10 for |x| <= 2^50.
+__constant__ double c_inv_m[kL] = {
+    1.0 / mod_of(0),  1.0 / mod_of(1),  1.0 / mod_of(2),  1.0 / mod_of(3),  1.0 / mod_of(4),
+    1.0 / mod_of(5),  1.0 / mod_of(6),  1.0 / mod_of(7),  1.0 / mod_of(8),  1.0 / mod_of(9),
+    1.0 / mod_of(10), 1.0 / mod_of(11), 1.0 / mod_of(12), 1.0 / mod_of(13)};
 
 // With kMixed, the moduli of residue_fp64 take the FP64 path and the others
 // the integer one; otherwise all take the integer path.  0 (256) is a mask.
 template <bool kMixed>
 constexpr bool residue_on_fp64(int l) { return kMixed && residue_fp64(l); }
 
-// Residue on the FP64 pipe, three instructions: q = rint((x - 128) / m)
-// (x.xs = x - 128; the rounded 1 / m puts q within one of the nearest
-// integer), so x - q m = 128 + ((x - 128) - q m) lies in
-// [128 - m / 2 - m 2^-10, 128 + m / 2 + m 2^-10], inside [0, 255] for
-// m <= 255; and y - q m = 1.5 * 2^52 + (x - q m), exact, has x - q m as its
-// low word.  y = 1.5 * 2^52 + x is the quantised double itself.  The value
-// is a residue of x in [0, 256) but not always below m; the GEMM only needs
-// an unsigned byte of the right class.
-__device__ __forceinline__ uint32_t residue_fp64_path(const Limbs& x, int l) {
-  const SplitF64& c = c_split_f64[l];
-  const double q = __dsub_rn(__fma_rn(x.xs, c.inv, kMagic), kMagic);
-  const double y = __hiloint2double(static_cast<int>(0x43300000u | x.hi), static_cast<int>(x.lo));
-  return static_cast<uint32_t>(__double2loint(__fma_rn(-q, c.m, y)));
+// Residue from the FP64 pipe, two instructions: one FMA gives
+// 1.5 * 2^52 + q with q = rint((x - 128) / m) (x.xs = x - 128; the rounded
+// 1 / m puts q within one of the nearest integer), so r = x - q m =
+// 128 + ((x - 128) - q m) lies in [128 - m / 2 - m 2^-10,
+// 128 + m / 2 + m 2^-10], inside [0, 255] for m <= 255.  r is then exact in
+// 32-bit integer arithmetic from the low words: x mod 2^32 is x.lo (2^51 is
+// 0 mod 2^32) and q mod 2^32 is the low word of the FMA's result, so one
+// multiply-add x.lo - q m gives r.  r is a residue of x in [0, 256) but not
+// always below m; the GEMM only needs an unsigned byte of the right class.
+__device__ __forceinline__ uint32_t residue_fp64_path(const Limbs& x, double inv, uint32_t m) {
+  const double qd = __fma_rn(x.xs, inv, kMagic);
+  return x.lo - static_cast<uint32_t>(__double2loint(qd)) * m;
 }
 
 // Residue in [0, m) on the integer pipes.
@@ -302,7 +292,7 @@ __device__ __forceinline__ uint32_t residue(const Limbs& x) {
   if constexpr (m == 256u) {
     return x.lo & 0xFFu;
   } else if constexpr (residue_on_fp64<kMixed>(l)) {
-    return residue_fp64_path(x, l);
+    return residue_fp64_path(x, c_inv_m[l], m);
   } else {
     return residue_int(x, c_split[l], m);
   }
@@ -346,7 +336,7 @@ __constant__ uint32_t c_mod_rt[kL] = {mod_of(0), mod_of(1), mod_of(2),  mod_of(3
                                       mod_of(10), mod_of(11), mod_of(12), mod_of(13)};
 
 __device__ __forceinline__ uint32_t residue_rt(const Limbs& x, int l) {
-  if (residue_fp64(l)) return residue_fp64_path(x, l);
+  if (residue_fp64(l)) return residue_fp64_path(x, c_inv_m[l], c_mod_rt[l]);
   return residue_int(x, c_split[l], c_mod_rt[l]);
 }
 

@@ -88,15 +88,18 @@ def rint_even(f):
 
 
 def fp64_residue(x_int, m):
-    """The split kernel's FP64-pipe residue: q = fma(x - 128, RN(1/m),
-    1.5 * 2^52) - 1.5 * 2^52 ((x - 128) * RN(1/m) rounded to an integer,
-    ties to even), then fma(-q, m, 1.5 * 2^52 + x), exact, whose low word is
-    x - q m."""
+    """The split kernel's FP64-pipe residue: fma(x - 128, RN(1/m), 1.5 * 2^52)
+    = 1.5 * 2^52 + q ((x - 128) * RN(1/m) rounded to an integer, ties to
+    even), then x.lo - (low word of that) * m in 32-bit arithmetic, which is
+    x - q m when x - q m lies in [0, 2^32)."""
     inv = Fraction(1.0 / m)  # the double nearest 1/m, exactly
     q = rint_even(Fraction(x_int - 128) * inv)
-    y = Fraction(MAGIC) + x_int - q * m  # the fma's exact result ...
-    assert y == int(y) and 2 ** 52 <= y < 2 ** 53  # ... is a double: no rounding
-    return x_int - q * m
+    qd = Fraction(MAGIC) + q  # the fma's result, exact: a double with ulp 1
+    assert qd == int(qd) and 2 ** 52 <= qd < 2 ** 53
+    t = x_int + 2 ** 51  # the split's biased integer; its low word is x.lo
+    r32 = ((t & 0xFFFFFFFF) - (int(qd) & 0xFFFFFFFF) * m) & 0xFFFFFFFF
+    assert r32 == x_int - q * m
+    return r32
 
 
 def residue(x_int, l):
