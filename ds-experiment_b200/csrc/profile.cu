@@ -5,6 +5,7 @@
 #include <atomic>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -20,6 +21,7 @@ struct Span {
 
 std::atomic<bool> g_enabled{false};
 std::mutex g_mu;
+std::set<std::string> g_only;  // families recorded while enabled; empty: all
 std::map<std::string, std::vector<Span>> g_spans;
 std::vector<cudaEvent_t> g_free;
 
@@ -39,6 +41,7 @@ cudaEvent_t take_event() {
 ProfileScope::ProfileScope(const char* name, cudaStream_t s) : name_(name), stream_(s) {
   if (!g_enabled.load(std::memory_order_relaxed)) return;
   std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_only.empty() && !g_only.count(name)) return;
   start_ = take_event();
   if (start_ && cudaEventRecord(start_, s) != cudaSuccess) {
     g_free.push_back(start_);
@@ -65,6 +68,21 @@ using namespace dsb;
 extern "C" {
 
 void ds_profile_enable(int on) { g_enabled.store(on != 0); }
+
+void ds_profile_select(const char* names) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  g_only.clear();
+  if (!names) return;
+  const std::string all(names);
+  size_t at = 0;
+  while (at <= all.size()) {
+    const size_t end = all.find(',', at);
+    const std::string one = all.substr(at, end == std::string::npos ? std::string::npos : end - at);
+    if (!one.empty()) g_only.insert(one);
+    if (end == std::string::npos) break;
+    at = end + 1;
+  }
+}
 
 void ds_profile_reset(void) {
   std::lock_guard<std::mutex> lock(g_mu);

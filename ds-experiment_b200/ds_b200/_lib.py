@@ -131,6 +131,7 @@ SIGNATURES = {
     "ds_dot_tensor_plan": ([_I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_dot_tensor_kernel_info": ([ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "ds_profile_enable": ([ctypes.c_int], None),
+    "ds_profile_select": ([ctypes.c_char_p], None),
     "ds_profile_reset": ([], None),
     "ds_profile_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), _I64P], ctypes.c_int),
 }
@@ -176,6 +177,12 @@ def current_stream_ptr(device=None) -> int:
 
 def profile_enable(on: bool = True) -> None:
     lib().ds_profile_enable(1 if on else 0)
+
+
+def profile_select(names=None) -> None:
+    """Record only the kernel families in `names` (an iterable of names);
+    None records all."""
+    lib().ds_profile_select(",".join(names).encode() if names else None)
 
 
 def profile_reset() -> None:

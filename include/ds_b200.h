@@ -419,9 +419,13 @@ DS_API int ds_fused_reduce_rows_compile_check(const ds_fused_op* ops, int32_t n_
 /* Per-kernel GPU time.  While enabled, each op brackets its main kernel with
    CUDA events on the launch stream under a family name ("elementwise",
    "recurrence", "reduce", "dot_simt", "dot_vec", "ozaki_split" (with its
-   parts "ozaki_split_rows" and "ozaki_split_cols"), "ozaki_gemm",
-   "ozaki_crt").  ds_profile_read waits for the recorded
-   events and returns the summed milliseconds and the launch count. */
+   parts "ozaki_split_rows", "ozaki_split_rows_colmax", "ozaki_colmax" and
+   "ozaki_split_cols"), "ozaki_gemm", "ozaki_crt", "ozaki_fix").
+   ds_profile_read waits for the recorded events and returns the summed
+   milliseconds and the launch count.  ds_profile_select limits the
+   recording to the families named in a comma-separated list (NULL or ""
+   records all), so that a timed loop pays for the brackets of one kernel
+   only. */
 /* Plan of the tensor-core dot_general for contraction length K: the number
    of int8 GEMMs (moduli) it runs and the bits each operand keeps relative to
    its row (column) maximum. */
@@ -434,6 +438,7 @@ DS_API int ds_dot_tensor_plan(int64_t K, int32_t* moduli, int32_t* bits);
 DS_API int ds_dot_tensor_kernel_info(int32_t* cta_pairs, int32_t* query_error);
 
 DS_API void ds_profile_enable(int on);
+DS_API void ds_profile_select(const char* names);
 DS_API void ds_profile_reset(void);
 DS_API int ds_profile_read(const char* name, double* total_ms, int64_t* launches);
 
