@@ -53,3 +53,29 @@ def test_handlers_call_declared_entry_points():
     called = set(re.findall(r"\b(ds_[a-z0-9_]+)\(", FFI)) - {"ds_last_error"}
     declared = set(re.findall(r"DS_API\s+[\w\s\*]+?\b(ds_[a-z0-9_]+)\(", HEADER))
     assert called and called <= declared, called - declared
+
+
+PROXY = open(os.path.join(ADAPTERS, "ds_pjrt_proxy_b200.cc")).read()
+
+
+def test_pjrt_proxy_runs_the_retargeted_pass():
+    """The proxy's default pipeline names the pass DsTransformPassB200.cpp
+    registers, and the opt driver it spawns registers that pass."""
+    name = re.search(r'getArgument\(\) const final \{ return "([\w-]+)"; \}', PASS).group(1)
+    assert f"func.func({name})" in PROXY
+    assert "mlir-ds-b200-opt" in PROXY
+    driver = open(os.path.join(ADAPTERS, "mlir-ds-b200-opt.cpp")).read()
+    assert "registerDsTransformB200Pass();" in driver
+
+
+def test_pjrt_proxy_has_no_fixed_paths_or_leaked_buffers():
+    """The reference's defects are gone: every temporary file comes from
+    mkstemp, no pinned host buffer is allocated, and the plugin and tool
+    paths are read from the environment; its flags keep their names."""
+    assert not re.search(r'"/tmp/[\w.]+"', PROXY)
+    assert "mkstemp" in PROXY and "cudaMallocHost" not in PROXY
+    for var in ("DS_REAL_PLUGIN", "DS_OPT_BINARY", "DS_PASS_PIPELINE", "DS_BYPASS",
+                "DS_TEST_PASSTHROUGH"):
+        assert f'"{var}"' in PROXY, var
+    # the rewritten program is released with its executable
+    assert "PJRT_LoadedExecutable_Destroy = destroy_wrapper" in PROXY
