@@ -16,6 +16,11 @@
 //       -> @ds_dot_general_f64 {lhs/rhs_batching_dimensions,
 //          lhs/rhs_contracting_dimensions, algorithm}.
 //
+// Operations nested in while / if / case regions are rewritten in place
+// (the reference's pass leaves nested regions for later); a tree never
+// absorbs a producer of another block, so nothing moves into a loop body.
+// The scalar bodies of reduce-like operations are left alone.
+//
 // Values between rewritten operations stay f64 (8 bytes, like the
 // reference's hi/lo pair, and 53 bits instead of 48): an f32 operand is
 // widened where it enters and a result narrowed back where an operation
@@ -119,8 +124,18 @@ std::optional<int32_t> reduceBody(stablehlo::ReduceOp r) {
   return std::nullopt;
 }
 
+// Operations in the function body, or nested only in control flow (while,
+// if, case: the reference's "nested regions" next step) are rewritten.  The
+// scalar computations of reduce-like operations (reduce, reduce_window,
+// scatter, sort, ...) are not: only a reduce itself is.
+bool inRewritableRegion(Operation* op) {
+  for (Operation* p = op->getParentOp(); p && !isa<func::FuncOp>(p); p = p->getParentOp())
+    if (!isa<stablehlo::WhileOp, stablehlo::IfOp, stablehlo::CaseOp>(p)) return false;
+  return true;
+}
+
 bool isCandidate(Operation* op) {
-  if (!op) return false;
+  if (!op || !inRewritableRegion(op)) return false;
   if (isElementwise(op)) return true;
   if (auto d = dyn_cast<stablehlo::DotGeneralOp>(op))
     return isFloatTensor(d.getLhs().getType()) && isFloatTensor(d.getRhs().getType()) &&
@@ -182,11 +197,14 @@ struct Program {
 
 class ProgramBuilder {
  public:
-  ProgramBuilder(OpBuilder& b, Location loc, const llvm::DenseSet<Operation*>& done)
-      : b_(b), loc_(loc), done_(done) {}
+  ProgramBuilder(OpBuilder& b, Location loc, Block* block,
+                 const llvm::DenseSet<Operation*>& done)
+      : b_(b), loc_(loc), block_(block), done_(done) {}
 
   // Index of the operation producing v, absorbing single-use elementwise
-  // producers when `absorb`; -1 when the program would exceed its limits.
+  // producers of the root's own block when `absorb` (a producer outside a
+  // loop body stays outside it); -1 when the program would exceed its
+  // limits.
   int32_t build(Program& p, Value v, bool absorb) {
     if (auto it = p.opOf.find(v); it != p.opOf.end()) return it->second;
     if (static_cast<int>(p.codes.size()) + 1 > kMaxOps) return -1;
@@ -194,7 +212,8 @@ class ProgramBuilder {
     int32_t id;
     if (auto c = splatValue(def)) {
       id = p.push(kConst, 0, 0, *c);
-    } else if (absorb && def && isElementwise(def) && v.hasOneUse() && !done_.contains(def)) {
+    } else if (absorb && def && def->getBlock() == block_ && isCandidate(def) && v.hasOneUse() &&
+               !done_.contains(def) && isElementwise(def)) {
       const int32_t x = build(p, def->getOperand(0), absorb);
       if (x < 0) return -1;
       int32_t y = 0;
@@ -225,6 +244,7 @@ class ProgramBuilder {
  private:
   OpBuilder& b_;
   Location loc_;
+  Block* block_;
   const llvm::DenseSet<Operation*>& done_;
 };
 
@@ -298,7 +318,7 @@ struct DsTransformB200Pass
                          : isa<stablehlo::SubtractOp>(root) ? kSub
                          : isa<stablehlo::MulOp>(root)      ? kMul
                                                             : kNeg;
-    ProgramBuilder pb(b, loc, done);
+    ProgramBuilder pb(b, loc, root->getBlock(), done);
     // The root's operands, absorbing the single-use trees below them; if
     // that exceeds ds_fused's limits, the root alone (its producers then
     // become programs of their own).  Converts made for a failed attempt are
@@ -334,8 +354,8 @@ struct DsTransformB200Pass
     }
   }
 
-  // widen(narrow(x)) between two rewritten operations is x itself; then the
-  // marked converts nothing reads any more are dropped.
+  // widen(narrow(x)) between two rewritten operations of one region is x
+  // itself; then the marked converts nothing reads any more are dropped.
   void foldWidenedNarrowing(func::FuncOp func) {
     SmallVector<stablehlo::ConvertOp> widened;
     func.walk([&](stablehlo::ConvertOp c) {
@@ -343,7 +363,8 @@ struct DsTransformB200Pass
     });
     for (stablehlo::ConvertOp w : widened) {
       auto n = w.getOperand().getDefiningOp<stablehlo::ConvertOp>();
-      if (n && n->hasAttr(kNarrow)) w.getResult().replaceAllUsesWith(n.getOperand());
+      if (n && n->hasAttr(kNarrow) && n->getParentRegion() == w->getParentRegion())
+        w.getResult().replaceAllUsesWith(n.getOperand());
     }
     SmallVector<stablehlo::ConvertOp> marked;
     func.walk([&](stablehlo::ConvertOp c) {

@@ -79,3 +79,13 @@ def test_pjrt_proxy_has_no_fixed_paths_or_leaked_buffers():
         assert f'"{var}"' in PROXY, var
     # the rewritten program is released with its executable
     assert "PJRT_LoadedExecutable_Destroy = destroy_wrapper" in PROXY
+
+
+def test_pass_guards_nested_regions():
+    """Rewrites reach into control flow only: the region check admits while,
+    if and case parents, every candidate goes through it, and a tree absorbs
+    producers of its own block only."""
+    guard = re.search(r"bool inRewritableRegion\(Operation\* op\) \{(.*?)\n\}", PASS, re.S).group(1)
+    assert "stablehlo::WhileOp, stablehlo::IfOp, stablehlo::CaseOp" in guard
+    assert "if (!op || !inRewritableRegion(op)) return false;" in PASS
+    assert "def->getBlock() == block_" in PASS
