@@ -749,6 +749,31 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                "r"(valid ? 16 : 0)
                : "memory");
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel on the stream finishes;
+// it waits here, before reading anything that kernel wrote.  Without such a
+// launch this returns at once.
+__device__ __forceinline__ void wait_previous_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch with programmatic stream serialization (see wait_previous_grid).
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -762,6 +787,7 @@ split_mn_async_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, i
                       int64_t batch, int P, const int* __restrict__ codes,
                       uint8_t* __restrict__ planes, int* __restrict__ shifts) {
   __shared__ __align__(16) double stage[kMnStages][256][kMnCols];
+  wait_previous_grid();  // the column maxima
   const int64_t b = blockIdx.z;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kMnRows + threadIdx.x * kMnCols;
   if (r0 >= rows_pad) return;  // rows_pad is a multiple of kMnCols
@@ -1592,6 +1618,7 @@ __device__ __forceinline__ void crt_load(uint32_t (&w)[kL], const uint8_t* src, 
 __global__ void __launch_bounds__(kCrtThreads, 8)
 crt_kernel(CrtParams p) {
   constexpr int kCols = kCrtCols;
+  wait_previous_grid();  // the GEMM's residues
   const size_t plane = static_cast<size_t>(p.batch) * p.Mp * p.Np;
   const bool failed = *p.err != 0;
   const int64_t j0 = (static_cast<int64_t>(blockIdx.x) * kCrtThreads + threadIdx.x) * kCols;
@@ -1859,6 +1886,7 @@ __device__ void dot2_tile(const FixParams& p, int64_t b, int64_t tm, int64_t tn)
 // the result is deterministic.  Nothing to do costs one read.
 __global__ void __launch_bounds__(kFixThreads, 2)
 fix_kernel(FixParams p) {
+  wait_previous_grid();  // the CRT's list
   const int count = p.err[1];
   if (count == 0 || p.err[0] != 0) return;
   if (count <= p.cap) {
@@ -2004,9 +2032,9 @@ bool split_by_rows(const DotOperand& o, int64_t rows) { return o.s_k == 1 || row
 
 // Pass 2 of a column split: K-major planes (split_cols_kernel), or with mn
 // row-contiguous ones (split_mn_kernel).
-void launch_split_cols(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad,
-                       int64_t K, int64_t Kp, int P, const int* codes, uint8_t* planes,
-                       int* shifts, bool mn, cudaStream_t s) {
+cudaError_t launch_split_cols(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad,
+                              int64_t K, int64_t Kp, int P, const int* codes, uint8_t* planes,
+                              int* shifts, bool mn, cudaStream_t s) {
   ProfileScope prof("ozaki_split_cols", s);
   if (mn && o.f64) {
     // two blocks per SM in one wave, each over many k of one chunk
@@ -2016,8 +2044,8 @@ void launch_split_cols(const DotOperand& o, int64_t batch, int64_t rows, int64_t
     if (ky > 65535) ky = 65535;
     dim3 g(static_cast<unsigned>(chunks), static_cast<unsigned>(ky < 1 ? 1 : ky),
            static_cast<unsigned>(batch));
-    split_mn_async_kernel<<<g, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes,
-                                            shifts);
+    return launch_dependent(split_mn_async_kernel, g, dim3(256), s, o, rows, K, rows_pad, Kp,
+                            batch, P, codes, planes, shifts);
   } else if (mn) {
     dim3 g(static_cast<unsigned>((rows_pad + kMnRows - 1) / kMnRows),
            static_cast<unsigned>((Kp + kMnSlab - 1) / kMnSlab), static_cast<unsigned>(batch));
@@ -2027,6 +2055,7 @@ void launch_split_cols(const DotOperand& o, int64_t batch, int64_t rows, int64_t
            static_cast<unsigned>(batch));
     split_cols_kernel<<<g, 256, 0, s>>>(o, rows, K, rows_pad, Kp, batch, P, codes, planes, shifts);
   }
+  return cudaGetLastError();
 }
 
 int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_pad, int64_t K,
@@ -2047,7 +2076,7 @@ int launch_split(const DotOperand& o, int64_t batch, int64_t rows, int64_t rows_
       ProfileScope prof("ozaki_colmax", s);
       colmax_kernel<<<g1, 256, 0, s>>>(o, rows, K, rows_pad, codes);
     }
-    launch_split_cols(o, batch, rows, rows_pad, K, Kp, P, codes, planes, shifts, mn, s);
+    DSB_CUDA_TRY(launch_split_cols(o, batch, rows, rows_pad, K, Kp, P, codes, planes, shifts, mn, s));
   }
   return launch_status();
 }
@@ -2257,7 +2286,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
     if (gy > n) gy = n;
     if (gy > 65535) gy = 65535;
     dim3 cg(static_cast<unsigned>(gx), static_cast<unsigned>(gy < 1 ? 1 : gy));
-    crt_kernel<<<cg, kCrtThreads, 0, st>>>(q);
+    DSB_CUDA_TRY(launch_dependent(crt_kernel, cg, dim3(kCrtThreads), st, q));
     return launch_status();
   };
 
@@ -2285,7 +2314,7 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
           p.a, p.M, g.Mp, p.b, p.N, g.Np, p.K, g.Kp, P, planes_a, sa, cb, nc, cgx, cgy);
       if (int st = launch_status()) return st;
     }
-    launch_split_cols(p.b, 1, p.N, g.Np, p.K, g.Kp, P, cb, planes_b, sb, b_mn, s);
+    DSB_CUDA_TRY(launch_split_cols(p.b, 1, p.N, g.Np, p.K, g.Kp, P, cb, planes_b, sb, b_mn, s));
     if (int st = launch_status()) return st;
   } else {
     DSB_CUDA_TRY(cudaMemsetAsync(err, 0, clear_end - reinterpret_cast<uint8_t*>(err), s));
@@ -2314,7 +2343,8 @@ int dot_ozaki_one(const DotProblem& p, void* workspace, size_t workspace_bytes, 
   fp.list = cp.fix_list;
   fp.cap = g.fix_cap;
   ProfileScope prof("ozaki_fix", s);
-  fix_kernel<<<static_cast<unsigned>(2 * sm_count()), kFixThreads, 0, s>>>(fp);
+  DSB_CUDA_TRY(launch_dependent(fix_kernel, dim3(static_cast<unsigned>(2 * sm_count())),
+                                dim3(kFixThreads), s, fp));
   return launch_status();
 }
 
