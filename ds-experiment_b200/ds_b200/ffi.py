@@ -9,7 +9,9 @@ platform="CUDA")`` binds a target name to a libds_b200 entry point, and
 ``ffi_call`` allocates the results, passes torch's current CUDA stream and
 raises on a non-OK status.  Every reference target name is registered at
 import.  Scratch for ds_reduce / ds_dot_general comes from torch's caching
-allocator (the role XLA's scratch allocator plays for an FFI handler).
+allocator (the role XLA's scratch allocator plays for an FFI handler); small
+scratch is kept per stream and reused, and a reduce's scratch size is asked
+once per shape.
 """
 from __future__ import annotations
 
@@ -147,8 +149,42 @@ def _buf(t):
     return _lib.make_buffer(t.data_ptr(), t.shape)
 
 
-def _workspace(nbytes: int, device) -> torch.Tensor:
-    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+# Small workspaces (reduce partials) are kept per (device, stream) and reused:
+# calls on one stream run in order, so one buffer serves them all, and a
+# call skips an allocation.  Large ones (the dot_general's residue planes)
+# come from torch's allocator each time, so that they are not held.  None is
+# kept while a CUDA graph is being captured (its replay may overlap eager
+# calls).
+_SMALL_WORKSPACE = 1 << 20
+_workspaces: Dict[tuple, torch.Tensor] = {}
+
+
+def _workspace(nbytes: int, device, stream: int = 0) -> torch.Tensor:
+    nbytes = max(int(nbytes), 1)
+    if nbytes > _SMALL_WORKSPACE or torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        if len(_workspaces) > 64:
+            _workspaces.clear()
+        ws = _workspaces[key] = torch.empty(_SMALL_WORKSPACE, dtype=torch.uint8, device=device)
+    return ws
+
+
+# ds_reduce_workspace_size by (device, shape, dimensions): a pure function
+# of them, asked on every reduce call otherwise.
+_reduce_ws: Dict[tuple, int] = {}
+_dims_arrays: Dict[tuple, object] = {}
+
+
+def _dims_array(dims: tuple):
+    arr = _dims_arrays.get(dims)
+    if arr is None:
+        if len(_dims_arrays) > 256:
+            _dims_arrays.clear()
+        arr = _dims_arrays[dims] = (ctypes.c_int64 * max(len(dims), 1))(*dims)
+    return arr
 
 
 # (target, result specs) -> the callable ffi_call built for them
@@ -227,7 +263,8 @@ def _make_call(target_name: str, result_shape_dtypes):
             keep.append(d)
             bufs.append(b)
         refs = [ctypes.byref(b) for b in bufs]
-        stream = _stream_handle(device)
+        stream_ptr = _lib.current_stream_ptr(device)
+        stream = ctypes.c_void_p(stream_ptr)
         if conv.kind == "plain":
             call_args = refs[:len(args)]
             for name in conv.attrs:
@@ -239,14 +276,22 @@ def _make_call(target_name: str, result_shape_dtypes):
         elif conv.kind in ("reduce", "reduce_f64", "reduce_from_f64", "reduce_packed"):
             dims = tuple(int(d) for d in attrs.get("dimensions", ()))
             body = int(attrs.get("body", _lib.DS_BODY_ADD))
-            cdims = (ctypes.c_int64 * max(len(dims), 1))(*dims)
-            if conv.kind == "reduce_packed":  # sized on the logical shape [..., 2] -> [...]
-                lb, ld = _lib.make_buffer(args[0].data_ptr(), tuple(args[0].shape[:-1]))
-                keep.append(ld)
-                ws_bytes = _lib.lib().ds_reduce_workspace_size(ctypes.byref(lb), cdims, len(dims))
-            else:
-                ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
-            ws = _workspace(ws_bytes, device)
+            cdims = _dims_array(dims)
+            shape = tuple(args[0].shape[:-1]) if conv.kind == "reduce_packed" else tuple(args[0].shape)
+            wkey = (device.index, shape, dims)
+            ws_bytes = _reduce_ws.get(wkey)
+            if ws_bytes is None:
+                if conv.kind == "reduce_packed":  # sized on the logical shape [..., 2] -> [...]
+                    lb, ld = _lib.make_buffer(args[0].data_ptr(), shape)
+                    keep.append(ld)
+                    ws_bytes = _lib.lib().ds_reduce_workspace_size(ctypes.byref(lb), cdims,
+                                                                   len(dims))
+                else:
+                    ws_bytes = _lib.lib().ds_reduce_workspace_size(refs[0], cdims, len(dims))
+                if len(_reduce_ws) > 1024:
+                    _reduce_ws.clear()
+                _reduce_ws[wkey] = ws_bytes
+            ws = _workspace(ws_bytes, device, stream_ptr)
             wsp = ctypes.c_void_p(ws.data_ptr())
             if conv.kind == "reduce":
                 status = fn(refs[0], refs[1], refs[2], refs[3], cdims, len(dims), body,
@@ -266,7 +311,7 @@ def _make_call(target_name: str, result_shape_dtypes):
             rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
             ws_bytes = _lib.lib().ds_dot_general_workspace_size(
                 refs[0], rhs_ref, ctypes.byref(dd), algorithm)
-            ws = _workspace(ws_bytes, device)
+            ws = _workspace(ws_bytes, device, stream_ptr)
             wsp = ctypes.c_void_p(ws.data_ptr())
             if conv.kind == "dot":
                 status = fn(refs[0], refs[1], refs[2], refs[3], ctypes.byref(dd), algorithm,
