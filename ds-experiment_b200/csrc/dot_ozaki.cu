@@ -803,7 +803,9 @@ split_mn_async_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, i
   }
   const bool vec = r0 + kMnCols <= rows && (o.s_k & 1) == 0 && (o.s_b & 1) == 0 &&
                    (reinterpret_cast<uintptr_t>(o.f64) & 15) == 0;
-  const double* base = o.f64 + b * o.s_b + r0;
+  // addresses of copies that read nothing (zero fill) still point inside
+  // the operand
+  const double* base = o.f64 + b * o.s_b + (r0 < rows ? r0 : 0);
   const size_t plane_stride = static_cast<size_t>(batch) * Kp * rows_pad;
   const int64_t kstep = gridDim.y;
   auto issue = [&](int64_t k, int slot) {
@@ -815,7 +817,10 @@ split_mn_async_kernel(DotOperand o, int64_t rows, int64_t K, int64_t rows_pad, i
       cp_async16(dst + 2, src + 2, in);
     } else {
 #pragma unroll
-      for (int j = 0; j < kMnCols; ++j) cp_async8(dst + j, src + j, in && r0 + j < rows);
+      for (int j = 0; j < kMnCols; ++j) {
+        const bool valid = in && r0 + j < rows;
+        cp_async8(dst + j, valid ? src + j : base, valid);
+      }
     }
   };
   // prologue: the first kMnStages - 1 k of this block (empty groups past Kp)
