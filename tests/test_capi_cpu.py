@@ -277,3 +277,18 @@ def test_dot_general_workspace_counts_the_gather_copy(L):
     # mismatched sizes get no workspace (the call itself reports why)
     bad = L.make_dot_dims(lhs_contracting=(1, 2), rhs_contracting=(1, 0))
     assert L.lib().ds_dot_general_workspace_size(r(M3), r(N3), r(bad), 0) == 0
+
+
+def test_profile_select_and_read_without_a_gpu(L):
+    """The diagnostics bookkeeping needs no device: selecting families,
+    enabling, resetting and reading a family that recorded nothing work on
+    the host alone."""
+    from ds_b200 import _lib
+    _lib.profile_select(["ozaki_gemm", "reduce"])
+    _lib.profile_enable(True)
+    _lib.profile_enable(False)
+    _lib.profile_select(None)
+    _lib.profile_reset()
+    assert _lib.profile_read("ozaki_gemm") == (0.0, 0)
+    L.lib().ds_profile_select(b",,reduce,")  # empty names are skipped
+    L.lib().ds_profile_select(None)
