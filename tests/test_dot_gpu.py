@@ -48,7 +48,10 @@ def check_gemm(got, A, B, samples=512, tol_bits=42, ref=None):
 
 @pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("M,N,K", [(1, 7, 5), (5, 1, 9), (33, 17, 65), (128, 256, 128),
-                                   (200, 300, 500), (256, 512, 1024)])
+                                   (200, 300, 500), (256, 512, 1024),
+                                   # rows longer than 4096: A split alone (512 threads a
+                                   # row), B's column maxima and split separately
+                                   (64, 96, 5000)])
 def test_gemm_shapes(ops, algo, M, N, K):
     rng = np.random.default_rng(M * 7 + N * 3 + K)
     A = rng.uniform(-1, 1, (M, K))
