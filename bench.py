@@ -393,6 +393,36 @@ def run_ours(args):
            "pipeline": "copy-in, compute and copy-out streams, two buffer sets",
            "result_matches_device_run": e2e_ok}
 
+    # The same steps' copies alone (A and B in, C out, on the copy streams,
+    # no product): when the e2e step takes about as long, the host copies
+    # bound it, not the GPU.
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    c0, c1 = _events()
+    c0.record(stream)
+    s_in.wait_stream(stream)
+    s_out.wait_stream(stream)
+    for k in range(args.steps):
+        j = k % 2
+        with torch.cuda.stream(s_in):
+            dA2[j].copy_(hA, non_blocking=True)
+            dB2[j].copy_(hB, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            hC[j].copy_(dC2[j], non_blocking=True)
+    stream.wait_stream(s_in)
+    stream.wait_stream(s_out)
+    c1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    copy_ms = max_over_ranks(c0.elapsed_time(c1) / args.steps)
+    e2e["copies_alone_ms_per_step"] = round(copy_ms, 4)
+    e2e["host_copy_GB/s_whole_job"] = round(
+        world * (A.nbytes + B.nbytes + A.nbytes) / (copy_ms * 1e-3) / 1e9, 1)
+    e2e["limiter"] = ("host copies: the step takes no longer than its copies alone"
+                      if e_ms <= 1.1 * copy_ms else
+                      "the product: the step outlasts its copies alone")
+
     if rank == 0:
         err_max, err_med, rows, cols, truth = gemm_error(C_host, A, B)
         ref_err = reference_gemm_error(A, B, rows, cols, truth)
@@ -501,6 +531,35 @@ def _time_calls(fn, steps, warmup=3, families=()):
     return ms, fam, out
 
 
+def _graph_replay_us(fn, calls, want):
+    """Device time per call (us) of `calls` calls of fn captured in one CUDA
+    graph and replayed, and whether the last captured result has the bits
+    of `want` (an eager result of the same call)."""
+    import torch
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()  # warm-up on the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            outs = [fn() for _ in range(calls)]
+    torch.cuda.current_stream().wait_stream(stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    e0, e1 = _events()
+    e0.record(cur)
+    g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / calls * 1e3
+    ok = bool(torch.equal(outs[-1].view(torch.int64), want.view(torch.int64)))
+    del g
+    return us, ok
+
+
 def _hbm_roofline(bytes_per_call, kernel_ms, family, peaks, peak_src, workload):
     ach = bytes_per_call / (kernel_ms * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": family, "achieved": round(ach, 1),
@@ -602,12 +661,17 @@ def config2_lines(dev, peaks, peak_src):
             host_us = (time.perf_counter() - t) / steps * 1e6
             torch.cuda.synchronize()
             kus = fam["reduce"] * 1e3
+            graph_us, graph_ok = _graph_replay_us(fn, steps, r)
             line.update({"us_per_call": round(ms * 1e3, 2), "kernel_us": round(kus, 2),
                          "host_us_per_call": round(host_us, 2),
+                         "graph_us_per_call": round(graph_us, 2),
+                         "graph_result_bits_equal": graph_ok,
                          "bound": "launch: the two kernels (block partials, their fold) run "
                                   f"{kus:.1f} us; back-to-back calls cost "
                                   f"{ms * 1e3:.1f} us each on the device and {host_us:.1f} us "
-                                  "of host time (Python op, argument checks, launches)"})
+                                  "of host time (Python op, argument checks, launches); "
+                                  f"{steps} calls captured in one CUDA graph replay at "
+                                  f"{graph_us:.1f} us per call, the host's share gone"})
         else:
             line["roofline"] = _hbm_roofline(8.0 * n, fam["reduce"], "reduce", peaks, peak_src,
                                              f"reduce{n}")
