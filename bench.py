@@ -604,6 +604,24 @@ def config1_lines(dev, peaks, peak_src):
                                                            want.view(np.uint64))),
                 "bit_exact_checked": m,
                 "max_abs_err_vs_numpy_f64": float(np.max(np.abs(got - (a + b) * c)))}
+        if lg == 20:
+            # Back-to-back calls from Python leave the GPU idle between
+            # launches at this size, and that idle time falls inside the
+            # kernel's events.  The same calls captured in one CUDA graph
+            # run with no host gaps: the device time per call, the
+            # roofline's time here.
+            calls = 50
+            gus, gok = _graph_replay_us(fn, calls, y)
+            line["graph"] = {"us_per_call": round(gus, 2),
+                             "GB/s": round(32.0 * n / (gus * 1e-6) / 1e9, 1),
+                             "result_bits_equal": gok,
+                             "what": f"{calls} calls captured in one CUDA graph and replayed"}
+            line["roofline"] = _hbm_roofline(32.0 * n, gus * 1e-3, "elementwise", peaks,
+                                             peak_src, f"fused_add_mul{n}")
+            line["roofline"]["kernel_ms_source"] = (
+                "graph replay, device time per call (the launch gaps between the graph's "
+                "kernels included); the kernel's own events, with host gaps, read "
+                f"{fam['elementwise']:.4f} ms")
         # e2e through the public op: pinned inputs copied in, the result out
         ha, hb, hc = (torch.from_numpy(v).pin_memory() for v in (a, b, c))
         hy = torch.empty(n, dtype=torch.float64).pin_memory()

@@ -1,5 +1,5 @@
-// Shared host-side plumbing of libds_b200: status codes, the per-thread error
-// message, CUDA error checks and device properties.
+// Shared plumbing of libds_b200: status codes, the per-thread error message,
+// CUDA error checks, device properties and programmatic dependent launches.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -46,5 +46,32 @@ inline unsigned grid_for(int64_t work, int threads, int per_sm) {
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
+
+#ifdef __CUDACC__
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel on the stream finishes;
+// it waits here, before reading anything that kernel wrote.  Without such a
+// launch this returns at once.
+__device__ __forceinline__ void wait_previous_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch with programmatic stream serialization (see wait_previous_grid).
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+#endif
 
 }  // namespace dsb

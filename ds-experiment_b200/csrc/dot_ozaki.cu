@@ -749,31 +749,6 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                "r"(valid ? 16 : 0)
                : "memory");
 }
-// Programmatic dependent launch: a kernel launched with programmatic stream
-// serialization may start while the previous kernel on the stream finishes;
-// it waits here, before reading anything that kernel wrote.  Without such a
-// launch this returns at once.
-__device__ __forceinline__ void wait_previous_grid() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// Launch with programmatic stream serialization (see wait_previous_grid).
-template <typename... Params, typename... Args>
-cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s,
-                             Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
-}
-
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }

@@ -302,10 +302,12 @@ reduce_bulk_kernel(const double* __restrict__ x, int64_t n, ds2* __restrict__ pa
   }
 }
 
-// Full reduction, stage 2: one block folds the G partials.
+// Full reduction, stage 2: one block folds the G partials.  Launched as a
+// programmatic dependent of stage 1, so its launch overlaps stage 1's tail.
 __global__ void __launch_bounds__(kThreads)
 reduce_partials_kernel(const ds2* __restrict__ partials, int g, int body, Dst dst,
                        const double* init_f64, const float* init_hi, const float* init_lo) {
+  wait_previous_grid();  // stage 1's partials
   const bool is_mul = body == 2;
   ds2 acc = identity(is_mul);
   for (int i = threadIdx.x; i < g; i += blockDim.x) acc = combine(is_mul, acc, partials[i]);
@@ -390,6 +392,7 @@ reduce_cols_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body,
 __global__ void __launch_bounds__(kThreads)
 reduce_cols_tile_kernel(Src src, int64_t outer, int64_t red, int64_t inner, int body, Dst dst,
                         const double* init_f64, const float* init_hi, const float* init_lo) {
+  wait_previous_grid();  // as the sliced path's second pass: the slices' partials
   __shared__ ds2 part[kThreads / 32][32];
   const bool is_mul = body == 2;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -545,8 +548,9 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
                                  a.init_lo, false, s);
     if (used < 0) return DS_INTERNAL;
     if (used > 1) {
-      reduce_partials_kernel<<<1, kThreads, 0, s>>>(partials, used, a.body, dst, a.init_f64,
-                                                    a.init_hi, a.init_lo);
+      DSB_CUDA_TRY(launch_dependent(reduce_partials_kernel, dim3(1), dim3(kThreads), s,
+                                    static_cast<const ds2*>(partials), used, a.body, dst,
+                                    a.init_f64, a.init_hi, a.init_lo));
     }
     return launch_status();
   }
@@ -580,8 +584,10 @@ int reduce_launch(const ReduceArgs& a, cudaStream_t s) {
                                                    partials);
       if (int st = launch_status()) return st;
       Src ps{nullptr, reinterpret_cast<const float*>(partials), nullptr, false, true};
-      reduce_cols_tile_kernel<<<static_cast<unsigned>(tiles), kThreads, 0, s>>>(
-          ps, 1, sl, outer * inner, a.body, dst, a.init_f64, a.init_hi, a.init_lo);
+      DSB_CUDA_TRY(launch_dependent(reduce_cols_tile_kernel,
+                                    dim3(static_cast<unsigned>(tiles)), dim3(kThreads), s, ps,
+                                    int64_t{1}, sl, outer * inner, a.body, dst, a.init_f64,
+                                    a.init_hi, a.init_lo));
       return launch_status();
     }
     reduce_cols_tile_kernel<<<static_cast<unsigned>(tiles), kThreads, 0, s>>>(
