@@ -182,6 +182,7 @@ dot_vec_kernel(DotProblem p, Acc* partials) {
 
 __global__ void __launch_bounds__(kThreads)
 dot_vec_finish_kernel(DotProblem p, const Acc* __restrict__ partials, int splits) {
+  wait_previous_grid();  // the partials (a programmatic dependent launch)
   const int64_t b = blockIdx.x;
   Acc acc{0.0f, 0.0f};
   for (int i = threadIdx.x; i < splits; i += blockDim.x) acc = acc_merge(acc, partials[b * splits + i]);
@@ -228,7 +229,10 @@ int dot_batched_vec(const DotProblem& p, void* workspace, size_t workspace_bytes
   Acc* partials = static_cast<Acc*>(workspace);
   ProfileScope prof("dot_vec", s);
   dot_vec_kernel<<<dim3(g, static_cast<unsigned>(p.batch)), kThreads, 0, s>>>(p, partials);
-  if (g > 1) dot_vec_finish_kernel<<<static_cast<unsigned>(p.batch), kThreads, 0, s>>>(p, partials, g);
+  if (int st = launch_status()) return st;
+  if (g > 1)
+    DSB_CUDA_TRY(launch_dependent(dot_vec_finish_kernel, dim3(static_cast<unsigned>(p.batch)),
+                                  dim3(kThreads), s, p, static_cast<const Acc*>(partials), g));
   return launch_status();
 }
 

@@ -138,6 +138,7 @@ __global__ void __launch_bounds__(kThreads)
 ew_pair_kernel(const TIn* __restrict__ a, const TIn* __restrict__ b,
                const TIn* __restrict__ c, TOut* __restrict__ out, int64_t n,
                Op op) {
+  wait_previous_grid();  // launched as a programmatic dependent: the producer's writes
   const int64_t npairs = n >> 1;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kThreads)
 ew_scalar_kernel(const TIn* __restrict__ a, const TIn* __restrict__ b,
                  const TIn* __restrict__ c, TOut* __restrict__ out, int64_t n,
                  Op op) {
+  wait_previous_grid();  // launched as a programmatic dependent: the producer's writes
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < n; i += stride) {
@@ -195,14 +197,19 @@ int launch_ew(const void* a, const void* b, const void* c, void* out, int64_t n,
   bool vec = aligned(a, PairIO<TIn>::kAlign) && aligned(out, PairIO<TOut>::kAlign);
   if (NIN > 1) vec = vec && aligned(b, PairIO<TIn>::kAlign);
   if (NIN > 2) vec = vec && aligned(c, PairIO<TIn>::kAlign);
+  // Programmatic dependent launches: a chain of calls on one stream overlaps
+  // each launch with the previous kernel's tail (each kernel waits for its
+  // predecessor before touching memory).
   ProfileScope prof("elementwise", s);
   if (vec) {
     const int64_t steps = ((n >> 1) + kUnroll - 1) / kUnroll;
-    ew_pair_kernel<NIN, TIn, TOut, Op>
-        <<<grid_for(steps, kThreads, 8), kThreads, 0, s>>>(ap, bp, cp, op_, n, op);
+    DSB_CUDA_TRY(launch_dependent(ew_pair_kernel<NIN, TIn, TOut, Op>,
+                                  dim3(grid_for(steps, kThreads, 8)), dim3(kThreads), s, ap, bp,
+                                  cp, op_, n, op));
   } else {
-    ew_scalar_kernel<NIN, TIn, TOut, Op>
-        <<<grid_for(n, kThreads, 8), kThreads, 0, s>>>(ap, bp, cp, op_, n, op);
+    DSB_CUDA_TRY(launch_dependent(ew_scalar_kernel<NIN, TIn, TOut, Op>,
+                                  dim3(grid_for(n, kThreads, 8)), dim3(kThreads), s, ap, bp, cp,
+                                  op_, n, op));
   }
   return launch_status();
 }

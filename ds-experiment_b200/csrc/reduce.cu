@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kThreads)
 reduce_full_kernel(Src src, int64_t n, int body, ds2* partials, Dst dst,
                    const double* init_f64, const float* init_hi, const float* init_lo,
                    bool always_partials = false) {
+  wait_previous_grid();  // launched as a programmatic dependent: the producer's writes
   const bool is_mul = body == 2;
   ds2 acc = identity(is_mul);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -519,8 +520,10 @@ int full_stage1(const Src& src, int64_t n, int body, ds2* partials, Dst dst,
     return launch_status() == DS_OK ? g : -1;
   }
   const int g = n == 0 ? 1 : reduce_full_blocks(n);
-  reduce_full_kernel<<<g, kThreads, 0, s>>>(src, n, body, partials, dst, init_f64, init_hi,
-                                            init_lo, always_partials);
+  if (cuda_status(launch_dependent(reduce_full_kernel, dim3(g), dim3(kThreads), s, src, n, body,
+                                   partials, dst, init_f64, init_hi, init_lo,
+                                   always_partials)) != DS_OK)
+    return -1;
   return launch_status() == DS_OK ? g : -1;
 }
 
