@@ -90,8 +90,7 @@ const Nvrtc& nvrtc() {
 struct Driver {
   CUresult (*load)(CUmodule*, const void*) = nullptr;
   CUresult (*get)(CUfunction*, CUmodule, const char*) = nullptr;
-  CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
-                     unsigned, CUstream, void**, void**) = nullptr;
+  CUresult (*launch_ex)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
   bool ok = false;
 };
 
@@ -109,10 +108,32 @@ const Driver& driver() {
     };
     d.load = reinterpret_cast<decltype(d.load)>(get("cuModuleLoadData"));
     d.get = reinterpret_cast<decltype(d.get)>(get("cuModuleGetFunction"));
-    d.launch = reinterpret_cast<decltype(d.launch)>(get("cuLaunchKernel"));
-    d.ok = d.load && d.get && d.launch;
+    d.launch_ex = reinterpret_cast<decltype(d.launch_ex)>(get("cuLaunchKernelEx"));
+    d.ok = d.load && d.get && d.launch_ex;
   });
   return d;
+}
+
+// Launches a generated kernel as a programmatic dependent of the previous
+// kernel on the stream: every generated kernel waits on griddepcontrol
+// before its first memory access, so its launch overlaps that kernel's tail.
+CUresult launch_generated(CUfunction fn, unsigned grid, unsigned threads, void* stream,
+                          void** args) {
+  CUlaunchAttribute attr[1] = {};
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg = {};
+  cfg.gridDimX = grid;
+  cfg.gridDimY = 1;
+  cfg.gridDimZ = 1;
+  cfg.blockDimX = threads;
+  cfg.blockDimY = 1;
+  cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = 0;
+  cfg.hStream = static_cast<CUstream>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return driver().launch_ex(&cfg, fn, args, nullptr);
 }
 
 // ---- program description and code generation -------------------------------
@@ -241,6 +262,7 @@ std::string generate(const Desc& d) {
     s += std::string("const ") + ctype(d.in[k].type) + "* __restrict__ in" + std::to_string(k) +
          ", ";
   s += std::string(reduce ? "float2" : ctype(d.out_type)) + "* __restrict__ out, long long n) {\n";
+  s += "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
   s += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
   s += "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
   if (reduce) s += "  ds2 acc = " + ident + ";\n";
@@ -353,6 +375,7 @@ std::string generate_rows(const Desc& d) {
          ", ";
   s += "float* __restrict__ out_hi, float* __restrict__ out_lo, const float* __restrict__ init_hi, "
        "const float* __restrict__ init_lo, long long rows, long long R) {\n";
+  s += "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
   s += "  const ds2 init = ds2{*init_hi, *init_lo};\n";
   s += "  __shared__ float2 part[8];\n";
   s += "  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {\n";
@@ -405,6 +428,7 @@ std::string generate_rows_groups(const Desc& d, int L) {
          ", ";
   s += "float* __restrict__ out_hi, float* __restrict__ out_lo, const float* __restrict__ init_hi, "
        "const float* __restrict__ init_lo, long long rows, long long R) {\n";
+  s += "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
   s += "  const ds2 init = ds2{*init_hi, *init_lo};\n";
   s += "  const int lane = threadIdx.x & 31, sub = lane % " + Ls + ";\n";
   s += "  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;\n";
@@ -688,9 +712,8 @@ int ds_fused_run(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_typ
   args[n_inputs + 1] = &n;
   const unsigned grid = grid_for(d.pairs ? (d.n + 1) / 2 : d.n, 256, 8);
   ProfileScope prof("fused", static_cast<cudaStream_t>(stream));
-  if (driver().launch(fn, grid, 1, 1, 256, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
-                      nullptr) != CUDA_SUCCESS)
-    return set_error(DS_INTERNAL, "ds_fused: cuLaunchKernel failed");
+  if (launch_generated(fn, grid, 256, stream, args.data()) != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused: cuLaunchKernelEx failed");
   return ok();
 }
 
@@ -753,9 +776,8 @@ int ds_fused_reduce(const ds_fused_op* ops, int32_t n_ops, const int32_t* input_
     args[n_inputs + 1] = &n;
     grid = grid_for(d.pairs ? (d.n + 1) / 2 : d.n, 256, 8);
     ProfileScope prof("fused_reduce", static_cast<cudaStream_t>(stream));
-    if (driver().launch(fn, grid, 1, 1, 256, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
-                        nullptr) != CUDA_SUCCESS)
-      return set_error(DS_INTERNAL, "ds_fused_reduce: cuLaunchKernel failed");
+    if (launch_generated(fn, grid, 256, stream, args.data()) != CUDA_SUCCESS)
+      return set_error(DS_INTERNAL, "ds_fused_reduce: cuLaunchKernelEx failed");
   }
   const int64_t pdims[2] = {static_cast<int64_t>(grid), 2};
   const ds_buffer pbuf{partials, pdims, 2};
@@ -838,9 +860,8 @@ int ds_fused_reduce_rows(const ds_fused_op* ops, int32_t n_ops, const int32_t* i
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
   ProfileScope prof("fused_reduce", static_cast<cudaStream_t>(stream));
-  if (driver().launch(fn, grid, 1, 1, threads, 1, 1, 0, static_cast<CUstream>(stream), args.data(),
-                      nullptr) != CUDA_SUCCESS)
-    return set_error(DS_INTERNAL, "ds_fused_reduce_rows: cuLaunchKernel failed");
+  if (launch_generated(fn, grid, threads, stream, args.data()) != CUDA_SUCCESS)
+    return set_error(DS_INTERNAL, "ds_fused_reduce_rows: cuLaunchKernelEx failed");
   return ok();
 }
 
