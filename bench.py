@@ -921,6 +921,46 @@ def int8_library_line(dev, ours_kernel_ms):
     return out
 
 
+def published_sizes_line(dev):
+    """The sizes the reference publishes for this path (one H100 PCIe; its
+    handoff.md:386-389), timed its way: wall clock around the call and a
+    device synchronize, median of 50 repetitions after 5 warm-up calls, so
+    Python dispatch and the synchronize are included.  Inputs are f64
+    U[-1,1] (seed 7); the programs are the reference benchmark's."""
+    import torch
+    from ds_b200 import fuse, ops
+    rng = np.random.default_rng(7)
+
+    def median_ms(fn, reps=50):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            t = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t)
+        return round(statistics.median(ts) * 1e3, 4)
+
+    n = 1 << 20
+    A, B = (torch.from_numpy(rng.uniform(-1, 1, n)).to(dev) for _ in range(2))
+    aab = fuse.jit(lambda a, b: a * a + b)
+    out = {"method": "wall clock around the call and torch.cuda.synchronize(), median of 50",
+           "elementwise_A*A+B_1M": {"ms": median_ms(lambda: aab(A, B)),
+                                   "reference_h100_pcie_ms": 0.058,
+                                   "program": "one fused DS program, f64 in and out"},
+           "sum_1M": {"ms": median_ms(lambda: ops.ds_sum_f64(A)),
+                      "reference_h100_pcie_ms": 0.043}}
+    for m, ref in ((256, 0.06), (2048, 0.32)):
+        X, Y = (torch.from_numpy(rng.uniform(-1, 1, (m, m))).to(dev) for _ in range(2))
+        out[f"matmul_{m}^2"] = {"ms": median_ms(lambda: ops.ds_matmul_f64(X, Y)),
+                                "reference_h100_pcie_ms": ref}
+    out["matmul_2048^2"]["reference_note"] = (
+        "the reference's four sub-GEMMs ran at default precision (TF32)")
+    return out
+
+
 def every_config(dev, clk, ours_kernel_ms):
     """The other configurations, each with its roofline, CPU baseline and
     exactness flag (rank 0, N = 1)."""
@@ -931,7 +971,8 @@ def every_config(dev, clk, ours_kernel_ms):
                      ("config2_ds_sum", lambda: config2_lines(dev, peaks, peak_src)),
                      ("config4_recurrence", lambda: config4_lines(dev, peaks, mhz)),
                      ("config5", lambda: config5_lines(dev, peaks, peak_src)),
-                     ("int8_library_gemm", lambda: int8_library_line(dev, ours_kernel_ms))):
+                     ("int8_library_gemm", lambda: int8_library_line(dev, ours_kernel_ms)),
+                     ("reference_published_sizes", lambda: published_sizes_line(dev))):
         t = time.perf_counter()
         out[name] = fn()
         out[name]["host_seconds"] = round(time.perf_counter() - t, 1)

@@ -231,15 +231,22 @@ def check(status: int, what: str = "") -> None:
 
 
 _DIMS_TYPES = [ctypes.c_int64 * max(n, 1) for n in range(17)]
+# dims arrays by shape: read-only once built, so buffers of one shape share one
+_shape_dims: dict = {}
 
 
 def make_buffer(ptr: int, shape) -> tuple:
     """A DsBuffer for `shape` at device address `ptr`; returns (buffer, dims)
     (keep `dims` alive while the buffer is used)."""
     shape = tuple(shape)
-    n = len(shape)
-    dims = (_DIMS_TYPES[n] if n < 17 else ctypes.c_int64 * n)(*shape)
-    return DsBuffer(ptr, dims, n), dims
+    dims = _shape_dims.get(shape)
+    if dims is None:
+        n = len(shape)
+        dims = (_DIMS_TYPES[n] if n < 17 else ctypes.c_int64 * n)(*shape)
+        if len(_shape_dims) > 1024:
+            _shape_dims.clear()
+        _shape_dims[shape] = dims
+    return DsBuffer(ptr, dims, len(shape)), dims
 
 
 def make_dot_dims(n_batch=0, lhs_contracting=1, rhs_contracting=0, lhs_batch=None,

@@ -149,32 +149,40 @@ def _buf(t):
     return _lib.make_buffer(t.data_ptr(), t.shape)
 
 
-# Small workspaces (reduce partials) are kept per (device, stream) and reused:
-# calls on one stream run in order, so one buffer serves them all, and a
-# call skips an allocation.  Large ones (the dot_general's residue planes)
-# come from torch's allocator each time, so that they are not held.  None is
-# kept while a CUDA graph is being captured (its replay may overlap eager
-# calls).
+# Workspaces up to _CACHED_WORKSPACE_MAX (reduce partials, the residue
+# planes of products up to about 1100 x 1100) are kept per (device, stream)
+# and reused: calls on one stream run in order, so one buffer serves them
+# all, and a call skips an allocation.  The buffer starts at 1 MiB and grows
+# to the next power of two a request needs; the one it replaces was
+# allocated on the same stream, so torch's allocator hands its memory out
+# again only to work ordered after the calls that used it.  Larger ones come
+# from torch's allocator each time, so that they are not held.  None is kept
+# while a CUDA graph is being captured (its replay may overlap eager calls).
 _SMALL_WORKSPACE = 1 << 20
+_CACHED_WORKSPACE_MAX = 64 << 20
 _workspaces: Dict[tuple, torch.Tensor] = {}
 
 
 def _workspace(nbytes: int, device, stream: int = 0) -> torch.Tensor:
     nbytes = max(int(nbytes), 1)
-    if nbytes > _SMALL_WORKSPACE or torch.cuda.is_current_stream_capturing():
+    if nbytes > _CACHED_WORKSPACE_MAX or torch.cuda.is_current_stream_capturing():
         return torch.empty(nbytes, dtype=torch.uint8, device=device)
     key = (device.index, stream)
     ws = _workspaces.get(key)
-    if ws is None:
-        if len(_workspaces) > 64:
+    if ws is None or ws.numel() < nbytes:
+        if ws is None and len(_workspaces) > 64:
             _workspaces.clear()
-        ws = _workspaces[key] = torch.empty(_SMALL_WORKSPACE, dtype=torch.uint8, device=device)
+        size = max(_SMALL_WORKSPACE, 1 << (nbytes - 1).bit_length())
+        ws = _workspaces[key] = torch.empty(size, dtype=torch.uint8, device=device)
     return ws
 
 
 # ds_reduce_workspace_size by (device, shape, dimensions): a pure function
-# of them, asked on every reduce call otherwise.
+# of them, asked on every reduce call otherwise.  Likewise the dot_general's
+# dimension-number struct and ds_dot_general_workspace_size, by (target,
+# device, shapes, algorithm, dimension numbers).
 _reduce_ws: Dict[tuple, int] = {}
+_dot_setup: Dict[tuple, tuple] = {}
 _dims_arrays: Dict[tuple, object] = {}
 
 
@@ -306,11 +314,25 @@ def _make_call(target_name: str, result_shape_dtypes):
                 status = fn(refs[0], refs[1], cdims, len(dims), body, refs[2], refs[3],
                             wsp, ws_bytes, stream)
         else:
-            dd = _dot_dims(attrs, args[0].dim())
             algorithm = int(attrs.get("algorithm", _lib.DS_DOT_TENSOR_INT8))
-            rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
-            ws_bytes = _lib.lib().ds_dot_general_workspace_size(
-                refs[0], rhs_ref, ctypes.byref(dd), algorithm)
+            rhs = args[2] if conv.kind == "dot" else args[1]
+            dkey = (conv.kind, device.index, tuple(args[0].shape), tuple(rhs.shape), algorithm,
+                    tuple(attrs.get("lhs_batching_dimensions", ())),
+                    tuple(attrs.get("rhs_batching_dimensions", ())),
+                    tuple(attrs.get("lhs_contracting_dimensions", ())),
+                    tuple(attrs.get("rhs_contracting_dimensions", ())))
+            cached = _dot_setup.get(dkey)
+            if cached is None:
+                dd = _dot_dims(attrs, args[0].dim())
+                rhs_ref = refs[2] if conv.kind == "dot" else refs[1]
+                ws_bytes = _lib.lib().ds_dot_general_workspace_size(
+                    refs[0], rhs_ref, ctypes.byref(dd), algorithm)
+                if ws_bytes:  # 0: invalid; the call below reports why
+                    if len(_dot_setup) > 1024:
+                        _dot_setup.clear()
+                    _dot_setup[dkey] = (dd, ws_bytes)
+            else:
+                dd, ws_bytes = cached
             ws = _workspace(ws_bytes, device, stream_ptr)
             wsp = ctypes.c_void_p(ws.data_ptr())
             if conv.kind == "dot":
